@@ -1,0 +1,390 @@
+#!/usr/bin/env python
+"""Benchmark of the TP Mamba forward on B200 (one process per GPU).
+
+Workload: mamba-1.4b-shaped model, seeded
+random-init bf16 weights, tensor parallel over all GPUs of the run (TP = N),
+mixed precision map (out_proj of layer 0 and of the last 4 layers in fp16,
+every other site int8-per-token).
+
+  value   prefill tokens/s of a batch 32 x 1024 of uniform random token ids,
+          inputs resident in HBM, whole job (TP shares the tokens across ranks)
+  e2e     the same through the public API with the ids in pinned host memory:
+          host->device copy of the ids, prefill, greedy next token read back
+  decode  CUDA-graph decode ms/token (256 replayed steps) at batch 1 and 32
+          after a 64-token prompt
+
+    python bench.py [--gpus N --steps K --warmup W]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+    python bench.py --impl reference      (the reference algorithm on the host cores)
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "prefill tok/s & graphed decode ms/token, mamba-1.4b shape, TP=1/2/4/8"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+CLOCK_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+
+def mixed_spec(n_layer: int):
+    over = {f"{i}:out_proj": "fp16" for i in (0, n_layer - 4, n_layer - 3, n_layer - 2, n_layer - 1)}
+    return {"default": "int8", "overrides": over}
+
+
+def load_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+def read_traffic(name: str):
+    """DRAM bytes per launch of a kernel from the committed ncu summary
+    (a line ``dram_bytes_per_launch[<name>]: <int>``), else None."""
+    p = os.path.join(REPO, "profiles", "traffic.txt")
+    if not os.path.exists(p):
+        return None
+    key = f"dram_bytes_per_launch[{name}]:"
+    with open(p) as f:
+        for line in f:
+            if line.startswith(key):
+                return float(line.split(":", 1)[1].strip())
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi samples every 200 ms while running (started before the timed
+    region, stopped after)."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.out = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={CLOCK_FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.index)], stdout=self.out,
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.out.close()
+
+    def summary(self):
+        if self.proc is None or not self.path:
+            return None
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+                except ValueError:
+                    continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3]) if v.lower().startswith("active")})
+        loaded = [r[0] for r in rows if r[2] > 300] or [r[0] for r in rows]
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ------------------------------------------------------------------ CPU arm (oracle port)
+def cpu_sample(shape: str, tokens: int, layers: int, seed: int = 0):
+    """Times the numpy restatement of the reference forward (oracle/) on a
+    bounded sample: ``layers`` mixer layers of the shape plus the lm_head, for
+    one sequence of ``tokens`` positions, and scales to tokens/s of the full
+    n_layer model.  Returns (tok_s, seconds, description, threads)."""
+    import numpy as np
+
+    from mamba_tp_lite_b200.config import shape_config
+    from oracle import mamba_oracle as O
+
+    cfg = shape_config(shape)
+    rng = np.random.default_rng(seed)
+    e, d, n, r = cfg.d_inner, cfg.d_model, cfg.d_state, cfg.dt_rank
+    f32 = np.float32
+
+    def nrm(*s):
+        return (rng.standard_normal(s, dtype=f32) * f32(0.02))
+
+    layers_p = []
+    for _ in range(layers):
+        dt = np.exp(rng.uniform(math.log(1e-3), math.log(1e-1), e)).astype(f32)
+        layers_p.append({
+            "in_proj.weight": nrm(2 * e, d), "conv1d.weight": rng.uniform(-0.5, 0.5, (e, 4)).astype(f32),
+            "conv1d.bias": rng.uniform(-0.5, 0.5, e).astype(f32), "x_proj.weight": nrm(r + 2 * n, e),
+            "dt_proj.weight": nrm(e, r), "dt_proj.bias": (dt + np.log(-np.expm1(-dt))).astype(f32),
+            "A_log": np.log(np.tile(np.arange(1, n + 1, dtype=f32), (e, 1))), "D": np.ones(e, f32),
+            "out_proj.weight": nrm(d, e)})
+    emb = nrm(cfg.vocab_size, d)
+    ids = rng.integers(0, cfg.vocab_size, (1, tokens))
+    x = emb[ids]
+    t0 = time.perf_counter()
+    for p in layers_p:
+        y, _ = O.mixer_prefill([p], O.rmsnorm(x, np.ones(d, f32), 1e-5))
+        x = (x + y).astype(f32)
+    t1 = time.perf_counter()
+    O._linear(O.rmsnorm(x, np.ones(d, f32), 1e-5), emb)
+    t2 = time.perf_counter()
+    per_seq = (t1 - t0) * cfg.n_layer / layers + (t2 - t1)
+    try:
+        from threadpoolctl import threadpool_info
+
+        threads = max([i.get("num_threads", 1) for i in threadpool_info()] + [1])
+    except Exception:
+        threads = os.cpu_count() or 1
+    desc = (f"numpy oracle port, fp32: prefill of 1 x {tokens} tokens through {layers} of {cfg.n_layer} "
+            f"{shape}-shaped layers + lm_head, scaled to {cfg.n_layer} layers")
+    return tokens / per_seq, t2 - t0, desc, threads
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    tokens, layers = a.ref_tokens, a.ref_layers
+    for _ in range(a.warmup):
+        cpu_sample(a.shape, tokens, layers)
+    vals, secs = [], []
+    for _ in range(a.steps):
+        v, s, desc, threads = cpu_sample(a.shape, tokens, layers)
+        vals.append(v)
+        secs.append(s)
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": a.gpus,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1000 * statistics.median(secs),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded random weights, uniform random token ids)",
+        "config": {"workload": f"mamba-{a.shape}-shaped prefill, reference algorithm on the host cores",
+                   "shape": a.shape, "sample_tokens": tokens, "sample_layers": layers},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ GPU arm
+def run_ours(a):
+    import torch
+    import torch.distributed as dist
+
+    from mamba_tp_lite_b200 import _lib as L
+    from mamba_tp_lite_b200 import _mixer
+    from mamba_tp_lite_b200.checkpoint import random_init_state_dict
+    from mamba_tp_lite_b200.config import shape_config
+    from mamba_tp_lite_b200.cuda_graph import GraphedStepper
+    from mamba_tp_lite_b200.tp_model import TPMambaLM
+    from mamba_tp_lite_b200.tp_utils import build_spec, destroy_comms
+
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if ws > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    L.load()
+
+    def barrier():
+        if ws > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if ws == 1:
+            return v
+        t = torch.tensor([v], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    cfg = shape_config(a.shape)
+    spec = build_spec(mixed_spec(cfg.n_layer), cfg.n_layer) if a.spec == "mixed" else a.spec
+    sd = random_init_state_dict(cfg, seed=0, dtype=torch.bfloat16, device="cuda")
+    model = TPMambaLM.from_state_dict_shard(cfg, sd, rank, ws, dtype=torch.bfloat16, allreduce_dtype=spec,
+                                            device="cuda")
+    del sd
+    torch.cuda.empty_cache()
+    B, S = a.batch, a.seqlen
+    g = torch.Generator(device="cuda").manual_seed(0)
+    ids = torch.randint(0, cfg.vocab_size, (B, S), device="cuda", generator=g)
+
+    # warm-up (also creates the comm context and sizes library scratch)
+    for _ in range(a.warmup):
+        model.prefill(ids)
+    torch.cuda.synchronize()
+    barrier()
+
+    # ------------------------------------------------ timed prefill (device-resident inputs)
+    _mixer.PROFILE = {}
+    launches0 = L.launch_count()
+    with ClockSampler(local) as clocks:
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.steps):
+            model.prefill(ids)
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+    launches = L.launch_count() - launches0
+    prof, _mixer.PROFILE = _mixer.PROFILE, None
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    value = B * S * a.steps / (ms / 1000.0)
+
+    kern = {}
+    for name, recs in prof.items():
+        durs = [s.elapsed_time(e) for s, e, _ in recs]
+        work = recs[0][2]
+        kern[name] = {"launches": len(recs), "avg_ms": sum(durs) / len(durs), "total_ms": sum(durs), "work": work}
+    peaks, peak_src = load_peaks()
+    gemms = {k: v for k, v in kern.items() if k != "scan"}
+    top = max(gemms, key=lambda k: gemms[k]["total_ms"])
+    k = gemms[top]
+    ach = k["work"] / (k["avg_ms"] / 1000.0) / 1e12
+    pk = peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
+    traffic = read_traffic(top)
+    roofline = {"kernel": f"gemm_tc ({top})", "bound": "tensor", "achieved": ach, "peak": pk, "unit": "TFLOP/s",
+                "frac": ach / pk, "traffic": traffic, "peak_source": f"{peak_src} sustained bf16",
+                "launches": k["launches"], "avg_launch_ms": k["avg_ms"]}
+    per_kernel = {}
+    for name, v in kern.items():
+        if name == "scan":
+            gbs = v["work"] / (v["avg_ms"] / 1000.0) / 1e9
+            per_kernel[name] = {"bound": "hbm", "achieved_GBps": gbs, "frac_of_hbm": gbs / peaks["hbm_gbs"],
+                                "avg_ms": v["avg_ms"], "share_of_step": v["total_ms"] / ms}
+        else:
+            tf = v["work"] / (v["avg_ms"] / 1000.0) / 1e12
+            per_kernel[name] = {"bound": "tensor", "achieved_TFLOPs": tf, "frac": tf / pk, "avg_ms": v["avg_ms"],
+                                "share_of_step": v["total_ms"] / ms}
+
+    # ------------------------------------------------ end to end through the API, host ids
+    host_ids = ids.cpu().pin_memory()
+    nxt_host = torch.empty(B, 1, dtype=torch.int64).pin_memory()
+    barrier()
+    torch.cuda.synchronize()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record()
+    for _ in range(a.steps):
+        dev_ids = host_ids.to("cuda", non_blocking=True)
+        logits, _ = model.prefill(dev_ids)
+        nxt_host.copy_(model.greedy_next(logits), non_blocking=True)
+    e3.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms_e2e = max_over_ranks(e2.elapsed_time(e3))
+    e2e = {"value": B * S * a.steps / (ms_e2e / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": B * S * 8,
+           "d2h_bytes_per_step": B * 8}
+    del logits
+
+    # ------------------------------------------------ graphed decode
+    decode = {}
+    if not a.no_decode:
+        for db in a.decode_batches:
+            prompt = ids[:db, :64].contiguous()
+            _, cache = model.prefill(prompt)
+            st = GraphedStepper(model, cache, db, "cuda")
+            st.capture()
+            nid = torch.zeros(db, 1, dtype=torch.long, device="cuda")
+            for _ in range(5):
+                st.replay(nid)
+            torch.cuda.synchronize()
+            barrier()
+            d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            d0.record()
+            for _ in range(a.decode_steps):
+                st.replay(nid)
+            d1.record()
+            torch.cuda.synchronize()
+            barrier()
+            dms = max_over_ranks(d0.elapsed_time(d1)) / a.decode_steps
+            decode[f"b{db}_ms_per_token"] = dms
+            st.release()
+            del cache
+        decode["steps"] = a.decode_steps
+        decode["prompt"] = 64
+
+    cpu = None
+    if rank == 0 and ws == 1 and not a.no_cpu_baseline:
+        v, _, desc, threads = cpu_sample(a.shape, a.ref_tokens, a.ref_layers)
+        cpu = {"value": v, "unit": "tok/s", "cores": threads, "kind": "port", "sample": desc}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": ms / a.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded random-init weights, uniform random token ids)",
+        "config": {"workload": f"mamba-{a.shape}-shaped TP prefill {B}x{S} + graphed decode", "shape": a.shape,
+                   "global_batch": B, "seq_len": S, "tp": ws, "parallelism": f"tp{ws}",
+                   "precision_map": a.spec if a.spec != "mixed" else
+                   "int8-per-token, out_proj of layers 0 and last 4 in fp16",
+                   "l2": "inputs larger than L2 (2.8 GB of weights, >126 MB of activations per layer)"},
+        "decode": decode, "roofline": roofline, "kernels": per_kernel, "cpu_baseline": cpu, "e2e": e2e,
+        "clocks": clocks.summary(), "gpu_launches": launches,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    destroy_comms()
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--shape", default="1.4b")
+    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--seqlen", type=int, default=1024)
+    ap.add_argument("--spec", default="mixed", help="'mixed' (configuration 4 map) or one reduction name")
+    ap.add_argument("--decode-steps", type=int, default=256)
+    ap.add_argument("--decode-batches", type=int, nargs="*", default=[1, 32])
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-tokens", type=int, default=1024)
+    ap.add_argument("--ref-layers", type=int, default=4)
+    a = ap.parse_args()
+    if a.warmup < 3 and a.impl == "ours":
+        print("note: fewer than 3 warm-up steps", file=sys.stderr)
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,175 @@
+/*
+ * mtp.h -- C ABI of libmtp.so, the B200 (sm_100a) kernels behind the
+ * channel-sharded tensor-parallel Mamba-1 forward pass.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * (passed as void*), returns an int status (0 = ok, see MTP_ERR_*), allocates
+ * no device memory (the comm context allocates once, in mtp_comm_create), and
+ * launches only on the given stream, so all of them can be recorded in a CUDA
+ * graph.  No torch types appear here; the Python package binds this header
+ * with ctypes.
+ *
+ * Layout conventions: matrices are row-major; a "token row" is one position
+ * of one sequence, tokens ordered (batch, position).  Element type codes are
+ * MTP_F32 / MTP_BF16 / MTP_F16.
+ *
+ * Each function names the reference (Mamba-TP Lite, pure PyTorch) code it
+ * replaces, as path:line within that project.
+ */
+#ifndef MTP_H_
+#define MTP_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  MTP_OK = 0,
+  MTP_ERR_ARG = 1,         /* bad size, pointer, stride or alignment */
+  MTP_ERR_CUDA = 2,        /* a CUDA runtime call or launch failed */
+  MTP_ERR_TIMEOUT = 3,     /* a bounded device wait expired (peer never arrived) */
+  MTP_ERR_UNSUPPORTED = 4  /* combination not built (dtype, size class) */
+};
+
+enum { MTP_F32 = 0, MTP_BF16 = 1, MTP_F16 = 2 };
+
+/* Reduction (collective) wire modes: the reference's ALLREDUCE_FNS names
+ * "fp32", "fp16" and "int8" (== "int8_gather_tok"), mamba_lite/tp_utils.py:152-160. */
+enum { MTP_RED_FP32 = 0, MTP_RED_FP16 = 1, MTP_RED_INT8TOK = 2 };
+
+/* GEMM epilogues. */
+enum {
+  MTP_EPI_STORE = 0,         /* C = acc                                   */
+  MTP_EPI_BIAS_SOFTPLUS = 1, /* C = softplus(acc + bias[n]) (torch threshold 20) */
+  MTP_EPI_BIAS = 2           /* C = acc + bias[n]                          */
+};
+
+/* GEMM algorithm selector (mtp_gemm_ex).  AUTO picks TCGEN05 for bf16 with
+ * M >= 128 and TMA-compatible strides, GEMV for M <= 64, SIMT otherwise. */
+enum { MTP_GEMM_AUTO = 0, MTP_GEMM_TCGEN05 = 1, MTP_GEMM_SIMT = 2, MTP_GEMM_GEMV = 3 };
+
+const char *mtp_version(void);
+/* Text of the last host-side error of the calling thread ("" if none). */
+const char *mtp_last_error(void);
+/* Number of kernel launches issued by this library since load (all threads). */
+uint64_t mtp_launch_count(void);
+
+/* ------------------------------------------------------------------ GEMM
+ * C[M,N] = A[M,K] . B[N,K]^T, fp32 accumulation, optional epilogue.
+ * A: activations (a_dtype), B: weights (same dtype as A), C: c_dtype.
+ * Replaces nn.Linear / F.linear on the hot path:
+ *   in_proj  mamba_lite/tp_model.py:91, :142   (model.py:197, :261)
+ *   x_proj   tp_model.py:106, :159             (model.py:214, :279)
+ *   dt_proj  tp_model.py:110-111, :162-163 with MTP_EPI_BIAS_SOFTPLUS
+ *   out_proj tp_model.py:131, :175             (model.py:239, :293)
+ *   lm_head  tp_model.py:302-303               (model.py:325-326)
+ */
+int mtp_gemm(const void *A, const void *B, void *C, int M, int N, int K, int lda, int ldb, int ldc,
+             int ab_dtype, int c_dtype, int epilogue, const void *bias, int bias_dtype, void *stream);
+int mtp_gemm_ex(const void *A, const void *B, void *C, int M, int N, int K, int lda, int ldb, int ldc,
+                int ab_dtype, int c_dtype, int epilogue, const void *bias, int bias_dtype, int algo,
+                void *stream);
+
+/* ------------------------------------------------------------------ SSM
+ * Causal depthwise conv1d + SiLU over the x half of in_proj's output.
+ * xz: [B*L, ld_xz] (x in columns [0,Es)); conv_w [Es,K]; conv_b [Es] or NULL;
+ * hist: [B,Es,K-1] prior conv history or NULL (zeros); xc: [B*L, ld_xc].
+ * Pure (writes only xc); the fused scan / step kernels own the cache update.
+ * Replaces tp_model.py:93-100 (model.py:199-209) and the conv part of
+ * tp_model.py:145-157.  dtype: activation / parameter type (F32 or BF16). */
+int mtp_conv1d_silu(const void *xz, int ld_xz, const void *conv_w, const void *conv_b,
+                    const void *hist, void *xc, int ld_xc, int B, int L, int Es, int K, int dtype,
+                    void *stream);
+
+/* Fused prefill: causal conv1d + SiLU + selective scan + D skip + SiLU(z) gate.
+ * xz: [B*L, ld_xz] (x | z); dt: [B*L, ld_dt] fp32, softplus already applied;
+ * bc: [B*L, ld_bc] fp32 with B in columns [0,N) and C in [N,2N);
+ * A_log [Es,N], D [Es], conv_w [Es,K], conv_b [Es] in dtype;
+ * conv_init [B,Es,K-1] (dtype) / ssm_init [B,Es,N] (fp32) or NULL for zeros;
+ * y: [B*L, ld_y] (dtype); conv_final [B,Es,K-1] (dtype), ssm_final [B,Es,N] (fp32).
+ * conv_final may alias conv_init and ssm_final may alias ssm_init (in-place
+ * chunked prefill).  Replaces tp_model.py:93-103 and :113-129
+ * (model.py:199-241), the Python loop over t at tp_model.py:124-126. */
+int mtp_scan_prefill(const void *xz, int ld_xz, const float *dt, int ld_dt, const float *bc, int ld_bc,
+                     const void *A_log, const void *Dp, const void *conv_w, const void *conv_b,
+                     const void *conv_init, const float *ssm_init, void *y, int ld_y, void *conv_final,
+                     float *ssm_final, int B, int L, int Es, int N, int K, int dtype, void *stream);
+
+/* Single-token recurrent step, in place: conv history shift, SiLU, dt_proj
+ * (dt_low . W_dt^T + b) and softplus, state update, y = C.h + D.x, SiLU(z) gate.
+ * xz [B, ld_xz]; dt_low [B, ld_dl] (R values, dtype) ; W_dt [Es,R], b_dt [Es];
+ * bc [B, ld_bc] fp32 (B | C); conv_state [B,Es,K-1] (dtype) and ssm_state
+ * [B,Es,N] (fp32) are read and overwritten; y [B, ld_y].
+ * Replaces tp_model.py:145-173 (model.py:264-292); in-place copy_ at
+ * tp_model.py:154 and :170. */
+int mtp_step(const void *xz, int ld_xz, const void *dt_low, int ld_dl, const void *W_dt, const void *b_dt,
+             const float *bc, int ld_bc, const void *A_log, const void *Dp, const void *conv_w,
+             const void *conv_b, void *conv_state, float *ssm_state, void *y, int ld_y, int B, int Es,
+             int N, int R, int K, int dtype, void *stream);
+
+/* ------------------------------------------------------------------ misc
+ * Embedding gather (tp_model.py:308, :318): out[t,:] = table[ids[t],:] (fp32 out).
+ * ids are int64. */
+int mtp_embedding(const int64_t *ids, int T, const void *table, int D, int dtype, float *out, void *stream);
+/* RMSNorm (model.py:130-135): out = w * (x * rsqrt(mean(x^2) + eps)), x fp32
+ * [T, D], out in out_dtype. */
+int mtp_rmsnorm(const float *x, int T, int D, const void *w, int w_dtype, float eps, void *out,
+                int out_dtype, void *stream);
+/* Row-wise argmax of logits [T, V] (dtype) -> int64 (greedy decode, model.py:359/:363). */
+int mtp_argmax_rows(const void *logits, int T, int V, int ld, int dtype, int64_t *out, void *stream);
+
+/* ------------------------------------------------------------------ quantiser
+ * Per-row int8 quantiser of the "int8" collective (tp_utils.py:108-113):
+ * scale = max(amax|row|, 1e-8) / 127 (IEEE fp32 divide), q = clamp(rint(x / scale), +-127).
+ * Same device function as the one inside mtp_reduce_*; exported so tests can
+ * compare payload bytes with the reference bit for bit. */
+int mtp_quantize_rows_int8(const float *in, int rows, int cols, int ld, float *scales, int8_t *q,
+                           void *stream);
+/* Rank-ordered dequant-sum of packed payloads [ws][rows*4 scale bytes | rows*cols q]
+ * (tp_utils.py:127-130), product rounded before the add. */
+int mtp_dequant_sum(const uint8_t *payloads, int ws, int rows, int cols, float *out, void *stream);
+
+/* ------------------------------------------------------------------ collectives
+ * A comm context owns, per reduction site kind (0 = x_proj, 1 = out_proj),
+ * receive slots for every rank, a gather buffer, flag words and epoch
+ * counters in one device allocation that peers map through CUDA IPC.
+ * Bootstrap: mtp_comm_create on every rank, exchange the 64-byte handles
+ * (mtp_comm_ipc_handle) out of band, mtp_comm_open_peers, then a host
+ * barrier before the first reduction.  world_size 1 needs no context (pass
+ * NULL to the reduce calls).  Replaces the NCCL/gloo calls of
+ * tp_utils.py:27, :41, :120/:124. */
+typedef struct mtp_comm mtp_comm;
+int mtp_comm_create(int rank, int world_size, int max_rows, int cols_x, int cols_out, double timeout_s,
+                    mtp_comm **out);
+int mtp_comm_ipc_handle(mtp_comm *c, void *handle64);
+int mtp_comm_open_peers(mtp_comm *c, const void *handles /* world_size x 64 bytes */);
+int mtp_comm_destroy(mtp_comm *c);
+/* Device status word of the context: 0 ok, else MTP_ERR_TIMEOUT (host reads it
+ * after a synchronize; a timed-out reduction leaves its outputs undefined). */
+int mtp_comm_status(mtp_comm *c, int *status);
+int mtp_comm_reset_status(mtp_comm *c);
+
+/* AllReduce #1 epilogue (tp_model.py:106-108, :159-161): sum the fp32
+ * partial [rows, R+2N] over ranks in `mode`, then split it: dt_low [rows, R]
+ * (dt_dtype, input of dt_proj) and bc [rows, 2N] fp32 (scan input). */
+int mtp_reduce_xproj(mtp_comm *c, int mode, const float *partial, int rows, int R, int N2,
+                     void *dt_low, int dt_dtype, float *bc, void *stream);
+/* AllReduce #2 epilogue (tp_model.py:131-134 then the block residual
+ * tp_model.py:254-257 and the next RMSNorm): out = sum over ranks of the fp32
+ * partial [rows, D] (+ bias), resid += out (fp32, in place), and
+ * normed = RMSNorm(resid) * norm_w in out_dtype (skipped when normed is NULL). */
+int mtp_reduce_outproj(mtp_comm *c, int mode, const float *partial, int rows, int D, const void *bias,
+                       float *resid, const void *norm_w, float eps, void *normed, int out_dtype,
+                       void *stream);
+/* Plain reduction (the isolated site of the collective microbenchmark):
+ * out[rows, cols] (fp32) = reduce(in) over ranks; site selects the buffers. */
+int mtp_allreduce(mtp_comm *c, int site, int mode, const float *in, float *out, int rows, int cols,
+                  void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MTP_H_ */

@@ -1,0 +1,609 @@
+// Row-parallel reductions over NVLink peer memory, with the reference's wire formats.
+//
+// Modes (mamba_lite/tp_utils.py):
+//   fp32     all_reduce_sum            :23-28   ranks' fp32 partials summed in rank order
+//   fp16     all_reduce_sum_fp16       :31-42   fp16 on the wire, fp32 rank-ordered sum, one fp16 rounding
+//   int8tok  all_reduce_sum_int8_gather_tok :103-131, :145-149
+//            per row: scale = max(amax, 1e-8)/127, q = clamp(rint(x/scale), +-127);
+//            slot payload [rows*4 scale bytes | rows*cols int8] exactly as tp_utils.py:113;
+//            result = sum_r float(q_r) * s_r from zeros, in rank order (product rounded, then add).
+//
+// Transport: every rank's comm allocation is mapped by its peers through CUDA IPC.  A reduction
+// kernel of G CTAs runs on every rank; CTA j owns the same rows on every rank.
+//   one-shot (small):  push wire rows to every rank's slot[my_rank] -> flag -> wait for all ranks'
+//                      CTA j -> every rank reduces all its rows itself (identical order => identical bits)
+//   two-shot (large):  push each wire row only to the row's owner rank (rows split in ws chunks) ->
+//                      flag -> owner reduces its rows and pushes the fp32 result row to every rank's
+//                      gather buffer -> flag -> every rank runs the epilogue on the gathered rows.
+// Flag values come from a per-site epoch counter in device memory: every CTA of a call reads it at
+// start and the last CTA to finish advances it, so a captured CUDA graph replays correctly and all
+// ranks agree on it.  Receive slots are double-buffered by epoch parity: a rank can run at most one
+// call ahead of a peer, so consecutive calls on one site never write a slot a peer still reads.  Each wait is bounded (globaltimer); on expiry
+// the kernel stores MTP_ERR_TIMEOUT in the context's status word and returns.
+#include <cstring>
+#include <vector>
+#include "common.cuh"
+
+namespace mtp {
+
+constexpr int MAX_WS = 8;
+constexpr int G_MAX = 256;
+constexpr int WPB = 8;  // warps (rows in flight) per CTA
+
+struct CommDev {
+  char *peer[MAX_WS];  // base of each rank's allocation (peer[rank] = own)
+  size_t off_flags, off_epoch, off_done, off_status, off_recv[2], off_gath[2], slot_bytes[2];
+  int rank, ws;
+  unsigned long long timeout_ns;
+};
+
+}  // namespace mtp
+
+struct mtp_comm {
+  mtp::CommDev d;
+  char *base = nullptr;
+  size_t total = 0;
+  int max_rows = 0, cols[2] = {0, 0};
+  bool opened = false;
+  cudaIpcMemHandle_t handle;
+};
+
+namespace mtp {
+
+// ----------------------------------------------------------------- device helpers
+__device__ __forceinline__ float warp_max(float v) {
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Per-row int8 quantisation (tp_utils.py:111-112), IEEE divide and round-half-even.
+__device__ __forceinline__ float row_scale(float amax) { return __fdiv_rn(fmaxf(amax, 1e-8f), 127.0f); }
+__device__ __forceinline__ int quant1(float x, float scale) {
+  float r = rintf(__fdiv_rn(x, scale));
+  r = fminf(fmaxf(r, -127.0f), 127.0f);
+  return (int)r;
+}
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+  return (uint32_t)(a & 0xff) | ((uint32_t)(b & 0xff) << 8) | ((uint32_t)(c & 0xff) << 16) | ((uint32_t)(d & 0xff) << 24);
+}
+__device__ __forceinline__ float unpack_i8(uint32_t w, int i) { return (float)(int8_t)((w >> (8 * i)) & 0xffu); }
+
+// Row amax of a fp32 row (warp).
+__device__ __forceinline__ float row_amax(const float *row, int cols, int lane) {
+  float m = 0.f;
+  for (int c = lane; c < cols; c += 32) m = fmaxf(m, fabsf(row[c]));
+  return warp_max(m);
+}
+
+// Write one row's wire representation to slot `dst` (a rank's receive slot base for this call).
+template <int MODE>
+__device__ __forceinline__ void write_wire_row(char *dst, const float *row, int r, int rows, int cols, int lane,
+                                               float scale) {
+  if (MODE == MTP_RED_FP32) {
+    float *o = reinterpret_cast<float *>(dst) + (size_t)r * cols;
+    if ((cols & 3) == 0) {
+      for (int c = lane * 4; c < cols; c += 128) *reinterpret_cast<float4 *>(o + c) = *reinterpret_cast<const float4 *>(row + c);
+    } else {
+      for (int c = lane; c < cols; c += 32) o[c] = row[c];
+    }
+  } else if (MODE == MTP_RED_FP16) {
+    __half *o = reinterpret_cast<__half *>(dst) + (size_t)r * cols;
+    if ((cols & 3) == 0) {
+      for (int c = lane * 4; c < cols; c += 128) {
+        const float4 v = *reinterpret_cast<const float4 *>(row + c);
+        __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t *>(&a);
+        u.y = *reinterpret_cast<uint32_t *>(&b);
+        *reinterpret_cast<uint2 *>(o + c) = u;
+      }
+    } else {
+      for (int c = lane; c < cols; c += 32) o[c] = __float2half_rn(row[c]);
+    }
+  } else {
+    float *sc = reinterpret_cast<float *>(dst);
+    int8_t *q = reinterpret_cast<int8_t *>(dst + (size_t)4 * rows) + (size_t)r * cols;
+    if (lane == 0) sc[r] = scale;
+    if ((cols & 3) == 0) {
+      for (int c = lane * 4; c < cols; c += 128) {
+        const float4 v = *reinterpret_cast<const float4 *>(row + c);
+        *reinterpret_cast<uint32_t *>(q + c) = pack4(quant1(v.x, scale), quant1(v.y, scale), quant1(v.z, scale), quant1(v.w, scale));
+      }
+    } else {
+      for (int c = lane; c < cols; c += 32) q[c] = (int8_t)quant1(row[c], scale);
+    }
+  }
+}
+
+// Rank-ordered reduction of row r over `nsrc` wire slots; writes the fp32 result row to `out`.
+template <int MODE>
+__device__ __forceinline__ void reduce_row(char *const *slots, int nsrc, int r, int rows, int cols, int lane, float *out) {
+  if (MODE == MTP_RED_INT8TOK) {
+    float s[MAX_WS];
+    for (int k = 0; k < nsrc; ++k) s[k] = __ldcg(reinterpret_cast<const float *>(slots[k]) + r);
+    if ((cols & 3) == 0) {
+      for (int c = lane * 4; c < cols; c += 128) {
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        for (int k = 0; k < nsrc; ++k) {
+          const uint32_t w = __ldcg(reinterpret_cast<const unsigned int *>(slots[k] + (size_t)4 * rows + (size_t)r * cols + c));
+          a0 = __fadd_rn(a0, __fmul_rn(unpack_i8(w, 0), s[k]));
+          a1 = __fadd_rn(a1, __fmul_rn(unpack_i8(w, 1), s[k]));
+          a2 = __fadd_rn(a2, __fmul_rn(unpack_i8(w, 2), s[k]));
+          a3 = __fadd_rn(a3, __fmul_rn(unpack_i8(w, 3), s[k]));
+        }
+        *reinterpret_cast<float4 *>(out + c) = make_float4(a0, a1, a2, a3);
+      }
+    } else {
+      for (int c = lane; c < cols; c += 32) {
+        float a = 0.f;
+        for (int k = 0; k < nsrc; ++k) {
+          const int8_t q = *(const volatile int8_t *)(slots[k] + (size_t)4 * rows + (size_t)r * cols + c);
+          a = __fadd_rn(a, __fmul_rn((float)q, s[k]));
+        }
+        out[c] = a;
+      }
+    }
+  } else if (MODE == MTP_RED_FP16) {
+    for (int c = lane; c < cols; c += 32) {
+      float a = 0.f;
+      for (int k = 0; k < nsrc; ++k) {
+        const unsigned short u = __ldcg(reinterpret_cast<const unsigned short *>(slots[k]) + (size_t)r * cols + c);
+        a = __fadd_rn(a, __half2float(__ushort_as_half(u)));
+      }
+      out[c] = __half2float(__float2half_rn(a));
+    }
+  } else {
+    if ((cols & 3) == 0) {
+      for (int c = lane * 4; c < cols; c += 128) {
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k = 0; k < nsrc; ++k) {
+          const float4 v = __ldcg(reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(slots[k]) + (size_t)r * cols + c));
+          a.x = __fadd_rn(a.x, v.x); a.y = __fadd_rn(a.y, v.y); a.z = __fadd_rn(a.z, v.z); a.w = __fadd_rn(a.w, v.w);
+        }
+        *reinterpret_cast<float4 *>(out + c) = a;
+      }
+    } else {
+      for (int c = lane; c < cols; c += 32) {
+        float a = 0.f;
+        for (int k = 0; k < nsrc; ++k) a = __fadd_rn(a, __ldcg(reinterpret_cast<const float *>(slots[k]) + (size_t)r * cols + c));
+        out[c] = a;
+      }
+    }
+  }
+}
+
+// ----------------------------------------------------------------- epilogues
+enum { EPI_PLAIN = 0, EPI_XPROJ = 1, EPI_OUTPROJ = 2 };
+
+struct EpiOut {
+  float *out;           // PLAIN: [rows, cols]
+  void *dt_low;         // XPROJ: [rows, R] in dt_dtype
+  float *bc;            // XPROJ: [rows, 2N]
+  int R, dt_dtype;
+  const void *bias;     // OUTPROJ (model dtype) or NULL
+  float *resid;         // OUTPROJ [rows, D] in/out
+  const void *norm_w;   // OUTPROJ
+  void *normed;         // OUTPROJ [rows, D] or NULL
+  float eps;
+  int out_dtype;        // OUTPROJ: dtype of bias / norm_w / normed
+};
+
+__device__ __forceinline__ float ld_any(const void *p, int dtype, size_t i) {
+  return dtype == MTP_F32 ? ((const float *)p)[i] : __bfloat162float(((const __nv_bfloat16 *)p)[i]);
+}
+__device__ __forceinline__ void st_any(void *p, int dtype, size_t i, float v) {
+  if (dtype == MTP_F32) ((float *)p)[i] = v;
+  else ((__nv_bfloat16 *)p)[i] = __float2bfloat16_rn(v);
+}
+
+// `val` is the reduced row (fp32, in global scratch or the gather buffer); read with __ldcg.
+template <int EPI>
+__device__ __forceinline__ void epilogue_row(const EpiOut &e, const float *val, int r, int cols, int lane) {
+  if (EPI == EPI_PLAIN) {
+    for (int c = lane; c < cols; c += 32) e.out[(size_t)r * cols + c] = __ldcg(val + c);
+  } else if (EPI == EPI_XPROJ) {
+    for (int c = lane; c < cols; c += 32) {
+      const float v = __ldcg(val + c);
+      if (c < e.R) st_any(e.dt_low, e.dt_dtype, (size_t)r * e.R + c, v);
+      else e.bc[(size_t)r * (cols - e.R) + (c - e.R)] = v;
+    }
+  } else {
+    float ss = 0.f;
+    float *res = e.resid + (size_t)r * cols;
+    for (int c = lane; c < cols; c += 32) {
+      float v = __ldcg(val + c);
+      if (e.bias) v = v + ld_any(e.bias, e.out_dtype, c);
+      const float h = res[c] + v;
+      res[c] = h;
+      ss += h * h;
+    }
+    if (e.normed) {
+      ss = warp_sum(ss);
+      const float rs = rsqrtf(ss / (float)cols + e.eps);
+      for (int c = lane; c < cols; c += 32)
+        st_any(e.normed, e.out_dtype, (size_t)r * cols + c, ld_any(e.norm_w, e.out_dtype, c) * (res[c] * rs));
+    }
+  }
+}
+
+// ----------------------------------------------------------------- flags
+__device__ __forceinline__ uint32_t *flag_ptr(char *base, const CommDev &d, int site, int phase, int src, int j) {
+  return reinterpret_cast<uint32_t *>(base + d.off_flags) + (((size_t)(site * 2 + phase) * MAX_WS + src) * G_MAX + j);
+}
+
+// Signal phase `phase` of CTA j to `targets` (bitmask of ranks), after all threads' stores.
+__device__ __forceinline__ void signal(const CommDev &d, int site, int phase, uint32_t epoch, uint32_t targets) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < (unsigned)d.ws && (targets >> threadIdx.x) & 1u)
+    st_release_sys(flag_ptr(d.peer[threadIdx.x], d, site, phase, d.rank, blockIdx.x), epoch);
+}
+
+// Wait until every rank in `sources` signalled phase `phase` of CTA j.  Returns false on timeout.
+__device__ __forceinline__ bool wait_all(const CommDev &d, int site, int phase, uint32_t epoch, uint32_t sources,
+                                         int *abort_sm) {
+  if (threadIdx.x < (unsigned)d.ws && (sources >> threadIdx.x) & 1u) {
+    const uint32_t *f = flag_ptr(d.peer[d.rank], d, site, phase, threadIdx.x, blockIdx.x);
+    const unsigned long long t0 = globaltimer_ns();
+    uint32_t it = 0;
+    while ((int)(ld_acquire_sys(f) - epoch) < 0) {
+      if ((++it & 63u) == 0 && globaltimer_ns() - t0 > d.timeout_ns) {
+        atomicExch(reinterpret_cast<int *>(d.peer[d.rank] + d.off_status), MTP_ERR_TIMEOUT);
+        *abort_sm = 1;
+        break;
+      }
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  return *abort_sm == 0;
+}
+
+// ----------------------------------------------------------------- the reduction kernel
+// partial: [rows, cols] fp32 local.  scratch: [G*WPB, cols] fp32 per-warp row scratch (world size 1 and one-shot).
+template <int MODE, int EPI>
+__global__ void __launch_bounds__(WPB * 32) reduce_kernel(CommDev d, bool has_comm, int site, const float *__restrict__ partial,
+                                                          int rows, int cols, bool two_shot, float *scratch, EpiOut e) {
+  __shared__ int abort_sm;
+  __shared__ uint32_t epoch_sm;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int j = blockIdx.x, G = gridDim.x;
+  float *wrow = scratch + (size_t)(j * WPB + warp) * cols;
+  if (!has_comm) {
+    // world size 1: the wire round trip alone (fp16 cast / int8 quantise-dequantise)
+    for (int r = j * WPB + warp; r < rows; r += G * WPB) {
+      const float *row = partial + (size_t)r * cols;
+      if (MODE == MTP_RED_FP32) {
+        epilogue_row<EPI>(e, row, r, cols, lane);
+        continue;
+      }
+      if (MODE == MTP_RED_FP16) {
+        for (int c = lane; c < cols; c += 32) wrow[c] = __half2float(__float2half_rn(row[c]));
+      } else {
+        const float sc = row_scale(row_amax(row, cols, lane));
+        for (int c = lane; c < cols; c += 32) wrow[c] = __fadd_rn(0.f, __fmul_rn((float)quant1(row[c], sc), sc));
+      }
+      __syncwarp();
+      epilogue_row<EPI>(e, wrow, r, cols, lane);
+      __syncwarp();
+    }
+    return;
+  }
+  uint32_t *ep = reinterpret_cast<uint32_t *>(d.peer[d.rank] + d.off_epoch) + site;
+  if (threadIdx.x == 0) {
+    abort_sm = 0;
+    epoch_sm = *reinterpret_cast<volatile uint32_t *>(ep) + 1u;
+  }
+  __syncthreads();
+  const uint32_t epoch = epoch_sm;
+  // the last CTA to leave publishes the epoch for the next call
+  auto finish = [&]() {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      unsigned int *done = reinterpret_cast<unsigned int *>(d.peer[d.rank] + d.off_done) + site;
+      if (atomicAdd(done, 1u) == (unsigned)G - 1u) {
+        *done = 0u;
+        *reinterpret_cast<volatile uint32_t *>(ep) = epoch;
+        __threadfence();
+      }
+    }
+  };
+  const size_t half = (size_t)(epoch & 1u) * d.ws * d.slot_bytes[site];
+  const uint32_t all = (1u << d.ws) - 1u;
+  const int chunk = (rows + d.ws - 1) / d.ws;  // two-shot ownership: rows [k*chunk, (k+1)*chunk) -> rank k
+  // phase 0: push wire rows
+  for (int r = j * WPB + warp; r < rows; r += G * WPB) {
+    const float *row = partial + (size_t)r * cols;
+    const float sc = MODE == MTP_RED_INT8TOK ? row_scale(row_amax(row, cols, lane)) : 0.f;
+    if (two_shot) {
+      const int owner = r / chunk;
+      write_wire_row<MODE>(d.peer[owner] + d.off_recv[site] + half + (size_t)d.rank * d.slot_bytes[site], row, r, rows, cols, lane, sc);
+    } else {
+      for (int k = 0; k < d.ws; ++k) {
+        const int dst = (d.rank + k) % d.ws;  // stagger destinations across ranks
+        write_wire_row<MODE>(d.peer[dst] + d.off_recv[site] + half + (size_t)d.rank * d.slot_bytes[site], row, r, rows, cols, lane, sc);
+      }
+    }
+  }
+  signal(d, site, 0, epoch, all);
+  if (!wait_all(d, site, 0, epoch, all, &abort_sm)) { finish(); return; }
+  char *slots[MAX_WS];
+  for (int k = 0; k < d.ws; ++k) slots[k] = d.peer[d.rank] + d.off_recv[site] + half + (size_t)k * d.slot_bytes[site];
+  if (!two_shot) {
+    for (int r = j * WPB + warp; r < rows; r += G * WPB) {
+      reduce_row<MODE>(slots, d.ws, r, rows, cols, lane, wrow);
+      __syncwarp();
+      epilogue_row<EPI>(e, wrow, r, cols, lane);
+      __syncwarp();
+    }
+    finish();
+    return;
+  }
+  // phase 1 (owner): reduce owned rows, push fp32 result rows to every rank's gather buffer
+  float *gath_local = reinterpret_cast<float *>(d.peer[d.rank] + d.off_gath[site]);
+  for (int r = j * WPB + warp; r < rows; r += G * WPB) {
+    if (r / chunk != d.rank) continue;
+    float *mine = gath_local + (size_t)r * cols;
+    reduce_row<MODE>(slots, d.ws, r, rows, cols, lane, mine);
+    __syncwarp();
+    for (int k = 1; k < d.ws; ++k) {
+      const int dst = (d.rank + k) % d.ws;
+      float *o = reinterpret_cast<float *>(d.peer[dst] + d.off_gath[site]) + (size_t)r * cols;
+      if ((cols & 3) == 0) {
+        for (int c = lane * 4; c < cols; c += 128) *reinterpret_cast<float4 *>(o + c) = *reinterpret_cast<const float4 *>(mine + c);
+      } else {
+        for (int c = lane; c < cols; c += 32) o[c] = mine[c];
+      }
+    }
+  }
+  signal(d, site, 1, epoch, all);
+  if (!wait_all(d, site, 1, epoch, all, &abort_sm)) { finish(); return; }
+  for (int r = j * WPB + warp; r < rows; r += G * WPB) epilogue_row<EPI>(e, gath_local + (size_t)r * cols, r, cols, lane);
+  finish();
+}
+
+// ----------------------------------------------------------------- standalone quantiser / dequant
+__global__ void quantize_rows_kernel(const float *__restrict__ in, int rows, int cols, int ld, float *scales, int8_t *q) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const float *row = in + (size_t)warp * ld;
+  const float sc = row_scale(row_amax(row, cols, lane));
+  if (lane == 0) scales[warp] = sc;
+  for (int c = lane; c < cols; c += 32) q[(size_t)warp * cols + c] = (int8_t)quant1(row[c], sc);
+}
+
+__global__ void dequant_sum_kernel(const uint8_t *__restrict__ pl, int ws, int rows, int cols, float *out) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (size_t)rows * cols) return;
+  const int r = (int)(i / cols);
+  const size_t bytes = (size_t)rows * (4 + cols);
+  float a = 0.f;
+  for (int k = 0; k < ws; ++k) {
+    const uint8_t *p = pl + (size_t)k * bytes;
+    float s;
+    memcpy(&s, p + 4 * (size_t)r, 4);
+    a = __fadd_rn(a, __fmul_rn((float)(int8_t)p[4 * (size_t)rows + i], s));
+  }
+  out[i] = a;
+}
+
+// ----------------------------------------------------------------- host
+static float *g_scratch = nullptr;
+static size_t g_scratch_bytes = 0;
+
+// Per-warp row scratch of the reduction kernels.  Grown, never freed: a captured CUDA graph
+// may still hold an older pointer.  The first call (eager, before any capture) sizes it.
+static float *row_scratch(size_t bytes) {
+  if (bytes > g_scratch_bytes) {
+    float *p = nullptr;
+    if (bytes < ((size_t)32 << 20)) bytes = (size_t)32 << 20;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
+    g_scratch = p;
+    g_scratch_bytes = bytes;
+  }
+  return g_scratch;
+}
+
+template <int EPI>
+static int run_reduce(mtp_comm *c, int site, int mode, const float *partial, int rows, int cols, EpiOut e,
+                      cudaStream_t s) {
+  MTP_REQUIRE(partial && rows >= 0 && cols > 0, "bad arguments");
+  MTP_REQUIRE(mode == MTP_RED_FP32 || mode == MTP_RED_FP16 || mode == MTP_RED_INT8TOK, "unknown reduction mode");
+  MTP_REQUIRE(aligned16(partial), "partial must be 16-byte aligned");
+  if (rows == 0) return MTP_OK;
+  const bool has_comm = c && c->d.ws > 1;
+  if (has_comm) {
+    MTP_REQUIRE(c->opened, "comm context peers not opened");
+    MTP_REQUIRE(cols <= c->cols[site], "row width exceeds the context's site width");
+  }
+  const int sms = num_sms();
+  // rows per launch: bounded by the context's slots; each launch is a complete reduction
+  const int step = has_comm ? c->max_rows : rows;
+  for (int r0 = 0; r0 < rows; r0 += step) {
+    const int nr = rows - r0 < step ? rows - r0 : step;
+    int G = ceil_div(nr, WPB);
+    if (G > sms) G = sms;
+    if (G > G_MAX) G = G_MAX;
+    float *scr = row_scratch((size_t)G * WPB * cols * sizeof(float));
+    if (!scr) return fail(MTP_ERR_CUDA, "could not allocate reduction scratch");
+    EpiOut ee = e;
+    // advance outputs by r0 rows
+    if (EPI == EPI_PLAIN) ee.out = e.out + (size_t)r0 * cols;
+    if (EPI == EPI_XPROJ) {
+      ee.dt_low = (char *)e.dt_low + (size_t)r0 * e.R * (e.dt_dtype == MTP_F32 ? 4 : 2);
+      ee.bc = e.bc + (size_t)r0 * (cols - e.R);
+    }
+    if (EPI == EPI_OUTPROJ) {
+      ee.resid = e.resid + (size_t)r0 * cols;
+      if (e.normed) ee.normed = (char *)e.normed + (size_t)r0 * cols * (e.out_dtype == MTP_F32 ? 4 : 2);
+    }
+    CommDev d{};
+    if (has_comm) d = c->d;
+    const size_t wire_bytes = (size_t)nr * cols * 4;
+    const bool two_shot = has_comm && c->d.ws > 2 && wire_bytes >= ((size_t)1 << 20);
+    const float *pp = partial + (size_t)r0 * cols;
+#define MTP_RED_LAUNCH(M) \
+  reduce_kernel<M, EPI><<<G, WPB * 32, 0, s>>>(d, has_comm, site, pp, nr, cols, two_shot, scr, ee)
+    if (mode == MTP_RED_FP32) MTP_RED_LAUNCH(MTP_RED_FP32);
+    else if (mode == MTP_RED_FP16) MTP_RED_LAUNCH(MTP_RED_FP16);
+    else MTP_RED_LAUNCH(MTP_RED_INT8TOK);
+#undef MTP_RED_LAUNCH
+    int rc = check_launch("reduce");
+    if (rc) return rc;
+  }
+  return MTP_OK;
+}
+
+}  // namespace mtp
+
+using namespace mtp;
+
+extern "C" {
+
+int mtp_comm_create(int rank, int world_size, int max_rows, int cols_x, int cols_out, double timeout_s, mtp_comm **out) {
+  MTP_REQUIRE(out, "null out");
+  MTP_REQUIRE(world_size >= 1 && world_size <= MAX_WS && rank >= 0 && rank < world_size, "bad rank / world size");
+  MTP_REQUIRE(max_rows > 0 && cols_x > 0 && cols_out > 0, "bad sizes");
+  mtp_comm *c = new mtp_comm();
+  c->max_rows = max_rows;
+  c->cols[0] = cols_x;
+  c->cols[1] = cols_out;
+  auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
+  size_t off = 0;
+  c->d.off_flags = off;
+  off = al(off + sizeof(uint32_t) * 2 * 2 * MAX_WS * G_MAX);
+  c->d.off_epoch = off;
+  off = al(off + sizeof(uint32_t) * 2);
+  c->d.off_done = off;
+  off = al(off + sizeof(uint32_t) * 2);
+  c->d.off_status = off;
+  off = al(off + 256);
+  for (int s = 0; s < 2; ++s) {
+    c->d.slot_bytes[s] = al((size_t)max_rows * (4 * (size_t)c->cols[s] + 16));
+    c->d.off_recv[s] = off;
+    off = al(off + c->d.slot_bytes[s] * world_size * 2);  // two halves, by epoch parity
+    c->d.off_gath[s] = off;
+    off = al(off + (size_t)max_rows * c->cols[s] * 4);
+  }
+  c->total = off;
+  if (cudaMalloc(&c->base, c->total) != cudaSuccess) {
+    delete c;
+    return fail(MTP_ERR_CUDA, "cudaMalloc of the comm buffers failed");
+  }
+  cudaMemset(c->base, 0, c->d.off_recv[0]);
+  c->d.rank = rank;
+  c->d.ws = world_size;
+  c->d.timeout_ns = (unsigned long long)(timeout_s * 1e9);
+  for (int k = 0; k < MAX_WS; ++k) c->d.peer[k] = nullptr;
+  c->d.peer[rank] = c->base;
+  if (world_size > 1 && cudaIpcGetMemHandle(&c->handle, c->base) != cudaSuccess) {
+    cudaFree(c->base);
+    delete c;
+    return fail(MTP_ERR_CUDA, "cudaIpcGetMemHandle failed");
+  }
+  c->opened = world_size == 1;
+  if (cudaDeviceSynchronize() != cudaSuccess) return fail(MTP_ERR_CUDA, "comm init sync failed");
+  *out = c;
+  return MTP_OK;
+}
+
+int mtp_comm_ipc_handle(mtp_comm *c, void *handle64) {
+  MTP_REQUIRE(c && handle64, "null argument");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  memcpy(handle64, &c->handle, 64);
+  return MTP_OK;
+}
+
+int mtp_comm_open_peers(mtp_comm *c, const void *handles) {
+  MTP_REQUIRE(c && handles, "null argument");
+  for (int k = 0; k < c->d.ws; ++k) {
+    if (k == c->d.rank) continue;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, (const char *)handles + 64 * k, 64);
+    void *p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return fail(MTP_ERR_CUDA, std::string("cudaIpcOpenMemHandle: ") + cudaGetErrorString(e));
+    c->d.peer[k] = (char *)p;
+  }
+  c->opened = true;
+  return MTP_OK;
+}
+
+int mtp_comm_destroy(mtp_comm *c) {
+  if (!c) return MTP_OK;
+  cudaDeviceSynchronize();
+  for (int k = 0; k < c->d.ws; ++k)
+    if (k != c->d.rank && c->d.peer[k]) cudaIpcCloseMemHandle(c->d.peer[k]);
+  if (c->base) cudaFree(c->base);
+  delete c;
+  return MTP_OK;
+}
+
+int mtp_comm_status(mtp_comm *c, int *status) {
+  MTP_REQUIRE(c && status, "null argument");
+  if (cudaMemcpy(status, c->base + c->d.off_status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return fail(MTP_ERR_CUDA, "reading the comm status failed");
+  return MTP_OK;
+}
+
+int mtp_comm_reset_status(mtp_comm *c) {
+  MTP_REQUIRE(c, "null argument");
+  if (cudaMemset(c->base + c->d.off_status, 0, sizeof(int)) != cudaSuccess) return fail(MTP_ERR_CUDA, "reset status");
+  return MTP_OK;
+}
+
+int mtp_reduce_xproj(mtp_comm *c, int mode, const float *partial, int rows, int R, int N2, void *dt_low, int dt_dtype,
+                     float *bc, void *stream) {
+  MTP_REQUIRE(dt_low && bc && R > 0 && N2 > 0, "bad arguments");
+  MTP_REQUIRE(dt_dtype == MTP_F32 || dt_dtype == MTP_BF16, "dt_low must be F32 or BF16");
+  EpiOut e{};
+  e.dt_low = dt_low;
+  e.bc = bc;
+  e.R = R;
+  e.dt_dtype = dt_dtype;
+  return run_reduce<EPI_XPROJ>(c, 0, mode, partial, rows, R + N2, e, (cudaStream_t)stream);
+}
+
+int mtp_reduce_outproj(mtp_comm *c, int mode, const float *partial, int rows, int D, const void *bias, float *resid,
+                       const void *norm_w, float eps, void *normed, int out_dtype, void *stream) {
+  MTP_REQUIRE(resid && D > 0, "bad arguments");
+  MTP_REQUIRE(!normed || norm_w, "normed output needs norm weights");
+  MTP_REQUIRE(out_dtype == MTP_F32 || out_dtype == MTP_BF16, "out dtype must be F32 or BF16");
+  EpiOut e{};
+  e.bias = bias;
+  e.resid = resid;
+  e.norm_w = norm_w;
+  e.normed = normed;
+  e.eps = eps;
+  e.out_dtype = out_dtype;
+  return run_reduce<EPI_OUTPROJ>(c, 1, mode, partial, rows, D, e, (cudaStream_t)stream);
+}
+
+int mtp_allreduce(mtp_comm *c, int site, int mode, const float *in, float *out, int rows, int cols, void *stream) {
+  MTP_REQUIRE(out && (site == 0 || site == 1), "bad arguments");
+  EpiOut e{};
+  e.out = out;
+  return run_reduce<EPI_PLAIN>(c, site, mode, in, rows, cols, e, (cudaStream_t)stream);
+}
+
+int mtp_quantize_rows_int8(const float *in, int rows, int cols, int ld, float *scales, int8_t *q, void *stream) {
+  MTP_REQUIRE(in && scales && q && rows >= 0 && cols > 0 && ld >= cols, "bad arguments");
+  if (rows == 0) return MTP_OK;
+  quantize_rows_kernel<<<ceil_div(rows, 8), 256, 0, (cudaStream_t)stream>>>(in, rows, cols, ld, scales, q);
+  return check_launch("quantize_rows_int8");
+}
+
+int mtp_dequant_sum(const uint8_t *payloads, int ws, int rows, int cols, float *out, void *stream) {
+  MTP_REQUIRE(payloads && out && ws >= 1 && rows >= 0 && cols > 0, "bad arguments");
+  if (rows == 0) return MTP_OK;
+  const size_t n = (size_t)rows * cols;
+  dequant_sum_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(payloads, ws, rows, cols, out);
+  return check_launch("dequant_sum");
+}
+
+}  // extern "C"

@@ -1,0 +1,77 @@
+// Shared helpers for libmtp.so (sm_100a only).
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <atomic>
+#include <string>
+
+#include "../../include/mtp.h"
+
+namespace mtp {
+
+// ----------------------------------------------------------------- host errors
+void set_error(const std::string &msg);
+int fail(int code, const std::string &msg);
+int check_launch(const char *what);
+extern std::atomic<uint64_t> g_launches;
+inline void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+int num_sms();
+
+#define MTP_REQUIRE(cond, msg)                                   \
+  do {                                                           \
+    if (!(cond)) return ::mtp::fail(MTP_ERR_ARG, std::string(__func__) + ": " + (msg)); \
+  } while (0)
+
+inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+inline int ceil_div(long a, long b) { return (int)((a + b - 1) / b); }
+
+// ----------------------------------------------------------------- element access
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+  static __device__ __forceinline__ float ld(const float *p) { return *p; }
+  static __device__ __forceinline__ void st(float *p, float v) { *p = v; }
+};
+template <> struct Elem<__nv_bfloat16> {
+  static __device__ __forceinline__ float ld(const __nv_bfloat16 *p) { return __bfloat162float(*p); }
+  static __device__ __forceinline__ void st(__nv_bfloat16 *p, float v) { *p = __float2bfloat16_rn(v); }
+};
+template <> struct Elem<__half> {
+  static __device__ __forceinline__ float ld(const __half *p) { return __half2float(*p); }
+  static __device__ __forceinline__ void st(__half *p, float v) { *p = __float2half_rn(v); }
+};
+
+template <typename T> __device__ __forceinline__ float ldf(const T *p) { return Elem<T>::ld(p); }
+template <typename T> __device__ __forceinline__ void stf(T *p, float v) { Elem<T>::st(p, v); }
+
+// torch semantics, fp32.  Library expf / log1pf are called (not reimplemented).
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+__device__ __forceinline__ float softplus_f(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+
+// ----------------------------------------------------------------- timing / waits
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// dispatch on a runtime dtype code
+#define MTP_DISPATCH_FB(code, T, ...)                                       \
+  do {                                                                      \
+    if ((code) == MTP_F32) { using T = float; __VA_ARGS__; }                \
+    else if ((code) == MTP_BF16) { using T = __nv_bfloat16; __VA_ARGS__; } \
+    else return ::mtp::fail(MTP_ERR_UNSUPPORTED, "dtype must be F32 or BF16"); \
+  } while (0)
+
+}  // namespace mtp

@@ -1,0 +1,414 @@
+// tcgen05 / TMEM tensor-core GEMM for sm_100a:  C[M,N] = A[M,K] . B[N,K]^T  (bf16 in, fp32 accumulate).
+//
+// Persistent, warp-specialised CTA of 6 warps (one CTA per SM):
+//   warp 0      one lane issues TMA tile loads (A 128x64, B bn x64, 128-byte swizzle) into a
+//               4-stage shared-memory ring, completion tracked by mbarrier transaction counts;
+//   warp 1      allocates 512 TMEM columns (two 128 x bn fp32 accumulators) and one lane issues
+//               tcgen05.mma (kind::f16, M=128, N=bn, K=16 per instruction), releasing ring slots
+//               and signalling finished accumulators with tcgen05.commit;
+//   warps 2-5   epilogue: tcgen05.ld 32 lanes x 16 columns at a time, fused epilogue op, stores;
+//               overlaps the next tile's MMAs thanks to the second accumulator.
+// Every mbarrier wait is bounded (globaltimer); on expiry the CTA records MTP_ERR_TIMEOUT in a
+// device word, drains its in-flight copies and MMAs with bounded waits, frees TMEM and returns.
+#include <cuda.h>
+#include "common.cuh"
+
+namespace mtp {
+namespace tc {
+
+constexpr int BM = 128, BK = 64, BN_MAX = 256, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_BYTES = BN_MAX * BK * 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int NUM_THREADS = 192;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+
+struct Params {
+  void *C;
+  const void *bias;
+  int *err;
+  unsigned long long timeout_ns;
+  int M, N, K, ldc;
+  int c_dtype, epi, bias_dtype;
+  int bn, tiles_m, tiles_n, num_tiles, group_m;
+  uint32_t idesc;
+  int vec_ok;  // 16-byte vector stores allowed
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n.reg .pred p;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait.  Returns false (and raises the CTA abort flag) on timeout, or
+// false immediately once another role has aborted.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort,
+                                          unsigned long long timeout_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  uint32_t it = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if ((++it & 255u) == 0) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > timeout_ns) {
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *tm, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(tm), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major tile, 128-byte swizzle, rows of 64 bf16,
+// 8-row core groups 1024 bytes apart (SBO), descriptor version 1 (sm_100).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+  return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tile_coords(const Params &p, int t, int &mt, int &nt) {
+  const int gsize = p.group_m * p.tiles_n;
+  const int g = t / gsize;
+  const int first_m = g * p.group_m;
+  const int gm = min(p.tiles_m - first_m, p.group_m);
+  const int r = t - g * gsize;
+  mt = first_m + r % gm;
+  nt = r / gm;
+}
+
+__device__ __forceinline__ float load_bias(const Params &p, int n) {
+  return p.bias_dtype == MTP_F32 ? ((const float *)p.bias)[n] : __bfloat162float(((const __nv_bfloat16 *)p.bias)[n]);
+}
+
+// Apply the epilogue to 16 accumulator columns [n0, n0+16) of row `row` and store.
+__device__ __forceinline__ void epilogue_store(const Params &p, int row, int n0, float (&v)[16]) {
+  if (p.epi != MTP_EPI_STORE) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int n = n0 + i;
+      const float t = v[i] + (n < p.N ? load_bias(p, n) : 0.f);
+      v[i] = p.epi == MTP_EPI_BIAS_SOFTPLUS ? softplus_f(t) : t;
+    }
+  }
+  if (row >= p.M) return;
+  const bool full = p.vec_ok && (n0 + 16 <= p.N);
+  if (p.c_dtype == MTP_F32) {
+    float *c = (float *)p.C + (size_t)row * p.ldc + n0;
+    if (full) {
+#pragma unroll
+      for (int i = 0; i < 16; i += 4) *(float4 *)(c + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+    } else {
+      for (int i = 0; i < 16 && n0 + i < p.N; ++i) c[i] = v[i];
+    }
+  } else {
+    __nv_bfloat16 *c = (__nv_bfloat16 *)p.C + (size_t)row * p.ldc + n0;
+    if (full) {
+      uint32_t w[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+        w[i] = *reinterpret_cast<uint32_t *>(&h2);
+      }
+      *(uint4 *)c = make_uint4(w[0], w[1], w[2], w[3]);
+      *(uint4 *)(c + 8) = make_uint4(w[4], w[5], w[6], w[7]);
+    } else {
+      for (int i = 0; i < 16 && n0 + i < p.N; ++i) c[i] = __float2bfloat16_rn(v[i]);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+  extern __shared__ __align__(1024) unsigned char smem_dyn[];
+  const uint32_t raw = smem_u32(smem_dyn);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  unsigned char *gbase = smem_dyn + (base - raw);
+  // barrier block after the stage ring
+  const uint32_t bar0 = base + STAGES * STAGE_BYTES;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
+  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 4);
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(gbase + STAGES * STAGE_BYTES + 8 * (2 * STAGES + 5));
+  volatile int *abort = reinterpret_cast<volatile int *>(gbase + STAGES * STAGE_BYTES + 8 * (2 * STAGES + 5) + 8);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const int num_kb = (p.K + BK - 1) / BK;
+  const uint32_t tx_bytes = (uint32_t)(A_BYTES + p.bn * BK * 2);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      int issued = 0;
+      for (int t = blockIdx.x; t < p.num_tiles && !*abort; t += gridDim.x) {
+        int mt, nt;
+        tile_coords(p, t, mt, nt);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(empty_bar(s), ph ^ 1u, abort, p.timeout_ns)) break;
+          mbar_expect_tx(full_bar(s), tx_bytes);
+          const uint32_t sa = base + s * STAGE_BYTES;
+          tma_load_2d(sa, &tmA, full_bar(s), kb * BK, mt * BM);
+          tma_load_2d(sa + A_BYTES, &tmB, full_bar(s), kb * BK, nt * p.bn);
+          ++issued;
+          if (++s == STAGES) { s = 0; ph ^= 1u; }
+        }
+      }
+      if (*abort) {
+        // drain: wait (bounded) until the most recent fills have landed
+        int back = issued < STAGES ? issued : STAGES;
+        int ss = s;
+        uint32_t pp = ph;
+        for (int i = 0; i < back; ++i) {
+          if (--ss < 0) { ss = STAGES - 1; pp ^= 1u; }
+          const unsigned long long t0 = globaltimer_ns();
+          while (!mbar_try_wait(full_bar(ss), pp) && globaltimer_ns() - t0 < 100000000ull) {}
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      int local = 0;
+      bool any = false;
+      for (int t = blockIdx.x; t < p.num_tiles && !*abort; t += gridDim.x, ++local) {
+        const int a = local & 1;
+        const uint32_t use = (uint32_t)(local >> 1);
+        if (!mbar_wait(tempty_bar(a), (use & 1u) ^ 1u, abort, p.timeout_ns)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(a * BN_MAX);
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(full_bar(s), ph, abort, p.timeout_ns)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = base + s * STAGE_BYTES;
+          const uint64_t ad = sw128_desc(sa), bd = sw128_desc(sa + A_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)  // +32 bytes along K per instruction
+            umma_bf16(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), p.idesc, (kb | k) != 0);
+          any = true;
+          umma_commit(empty_bar(s));
+          if (++s == STAGES) { s = 0; ph ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit(tfull_bar(a));
+      }
+      if (*abort && any) {
+        umma_commit(drain_bar);
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(drain_bar, 0) && globaltimer_ns() - t0 < 100000000ull) {}
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5)
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int local = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
+      const int a = local & 1;
+      const uint32_t use = (uint32_t)(local >> 1);
+      if (!mbar_wait(tfull_bar(a), use & 1u, abort, p.timeout_ns)) break;
+      tc_fence_after();
+      int mt, nt;
+      tile_coords(p, t, mt, nt);
+      const int row = mt * BM + q * 32 + lane;
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN_MAX);
+      for (int j = 0; j < p.bn; j += 16) {
+        float v[16];
+        tmem_ld16(tbase + (uint32_t)j, v);
+        const int n0 = nt * p.bn + j;
+        if (n0 < p.N) epilogue_store(p, row, n0, v);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar(a));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x == 0 && *abort) atomicExch(p.err, MTP_ERR_TIMEOUT);
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
+}
+
+// ------------------------------------------------------------------ host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)ptr;
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix with leading dimension ld
+// (elements); box = box_rows x 64 columns, 128-byte swizzle, zero fill out of bounds.
+static int make_tmap(CUtensorMap *tm, const void *ptr, int rows, int cols, int ld, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(MTP_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MTP_ERR_ARG, "cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
+  return MTP_OK;
+}
+
+static int *device_err_word() {
+  static int *w = nullptr;  // one word per process (single device per process)
+  if (!w) {
+    if (cudaMalloc(&w, sizeof(int)) != cudaSuccess) return nullptr;
+    cudaMemset(w, 0, sizeof(int));
+  }
+  return w;
+}
+
+}  // namespace tc
+
+// True when the operands satisfy the TMA rules of this kernel.
+bool gemm_tc_eligible(const void *A, const void *B, int M, int N, int K, int lda, int ldb) {
+  return M > 0 && N > 0 && K >= 8 && aligned16(A) && aligned16(B) && lda % 8 == 0 && ldb % 8 == 0 && lda >= K &&
+         ldb >= K;
+}
+
+int gemm_tc(const void *A, const void *B, void *C, int M, int N, int K, int lda, int ldb, int ldc, int c_dtype,
+            int epi, const void *bias, int bias_dtype, cudaStream_t stream) {
+  using namespace tc;
+  MTP_REQUIRE(gemm_tc_eligible(A, B, M, N, K, lda, ldb),
+              "tcgen05 GEMM needs 16-byte aligned A/B, K >= 8 and lda, ldb multiples of 8");
+  MTP_REQUIRE(c_dtype == MTP_F32 || c_dtype == MTP_BF16, "C must be F32 or BF16");
+  MTP_REQUIRE(epi == MTP_EPI_STORE || ((epi == MTP_EPI_BIAS_SOFTPLUS || epi == MTP_EPI_BIAS) && bias), "bad epilogue");
+  Params p{};
+  p.C = C;
+  p.bias = bias;
+  p.bias_dtype = bias_dtype;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ldc = ldc;
+  p.c_dtype = c_dtype;
+  p.epi = epi;
+  p.bn = N <= BN_MAX ? ((N + 15) / 16) * 16 : BN_MAX;
+  p.tiles_m = ceil_div(M, BM);
+  p.tiles_n = ceil_div(N, p.bn);
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  p.group_m = 16;
+  p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+  const size_t cb = c_dtype == MTP_F32 ? 4 : 2;
+  p.vec_ok = aligned16(C) && ((size_t)ldc * cb) % 16 == 0;
+  p.timeout_ns = 2000000000ull;
+  p.err = device_err_word();
+  if (!p.err) return fail(MTP_ERR_CUDA, "could not allocate the GEMM status word");
+  CUtensorMap ta, tb;
+  int rc = make_tmap(&ta, A, M, K, lda, BM);
+  if (rc) return rc;
+  rc = make_tmap(&tb, B, N, K, ldb, p.bn);
+  if (rc) return rc;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    attr = true;
+  }
+  const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
+  gemm_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, p);
+  return check_launch("gemm_tc");
+}
+
+int gemm_tc_status(int *status) {
+  int *w = tc::device_err_word();
+  if (!w) return fail(MTP_ERR_CUDA, "no status word");
+  if (cudaMemcpy(status, w, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return fail(MTP_ERR_CUDA, "read status");
+  return MTP_OK;
+}
+
+}  // namespace mtp

@@ -1,0 +1,270 @@
+"""Dense Mamba-1 model with the reference's API (``mamba_lite/model.py``):
+``MambaConfig``, ``load_hf_state_dict``, ``LayerCache``, ``MambaCache``,
+``RMSNorm``, ``MambaMixer``, ``MambaBlock``, ``MambaLM``.
+
+Parameter names and shapes are the reference's, so ``state_dict()`` and
+``load_state_dict`` interchange with it.  Every forward runs in libmtp's CUDA
+kernels (see ``_mixer.py``); tensors must live on a CUDA device.
+
+Deliberate difference: the SSM state in a cache is float32 whatever the model
+dtype (the reference keeps it in the model dtype, model.py:115-117, which in
+bf16 rounds the recurrent state every step).  The conv history stays in the
+model dtype.
+"""
+from __future__ import annotations
+
+import json
+import os
+from dataclasses import dataclass
+
+import torch
+import torch.nn as nn
+
+from . import _lib as L
+from ._mixer import MixerKernels
+from .config import MambaConfig
+
+__all__ = ["MambaConfig", "load_hf_state_dict", "LayerCache", "MambaCache", "RMSNorm", "MambaMixer", "MambaBlock",
+           "MambaLM"]
+
+
+def load_hf_state_dict(hf_path: str) -> dict[str, torch.Tensor]:
+    """All tensors of a single-file or sharded (``model.safetensors.index.json``)
+    HF checkpoint directory (model.py:28-47)."""
+    from safetensors.torch import load_file
+
+    single = os.path.join(hf_path, "model.safetensors")
+    index = os.path.join(hf_path, "model.safetensors.index.json")
+    if os.path.exists(single):
+        return load_file(single)
+    if os.path.exists(index):
+        with open(index) as f:
+            weight_map = json.load(f)["weight_map"]
+        sd = {}
+        for shard in sorted(set(weight_map.values())):
+            sd.update(load_file(os.path.join(hf_path, shard)))
+        return sd
+    raise FileNotFoundError(f"no model.safetensors or model.safetensors.index.json under {hf_path}")
+
+
+@dataclass
+class LayerCache:
+    conv_state: torch.Tensor  # [batch, d_inner (shard), d_conv - 1], model dtype
+    ssm_state: torch.Tensor   # [batch, d_inner (shard), d_state], float32
+
+
+class MambaCache:
+    def __init__(self, layers: list[LayerCache]):
+        self.layers = layers
+
+    @staticmethod
+    def allocate(config: MambaConfig, batch_size: int, device, dtype, d_inner: int | None = None) -> "MambaCache":
+        """Zero cache (model.py:108-121).  ``d_inner`` defaults to the full
+        width; a TP rank passes its shard width."""
+        e = config.d_inner if d_inner is None else d_inner
+        return MambaCache([
+            LayerCache(
+                conv_state=torch.zeros(batch_size, e, config.d_conv - 1, device=device, dtype=dtype),
+                ssm_state=torch.zeros(batch_size, e, config.d_state, device=device, dtype=torch.float32),
+            )
+            for _ in range(config.n_layer)
+        ])
+
+
+class RMSNorm(nn.Module):
+    """model.py:124-135; forward runs the libmtp RMSNorm kernel."""
+
+    def __init__(self, d_model: int, eps: float = 1e-5):
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(d_model))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        L.require_cuda(x, "RMSNorm")
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).float().contiguous()
+        out = torch.empty(x2.shape, device=x.device, dtype=x.dtype)
+        L.call("mtp_rmsnorm", L.ptr(x2), x2.shape[0], x2.shape[1], L.ptr(self.weight), L.dtype_code(self.weight.dtype),
+               float(self.eps), L.ptr(out), L.dtype_code(out.dtype), L.stream_ptr())
+        return out.view(shape)
+
+
+class MambaMixer(MixerKernels, nn.Module):
+    """Dense mixer (model.py:138-294): no collectives."""
+
+    def __init__(self, cfg: MambaConfig, layer_idx: int):
+        super().__init__()
+        self.cfg = cfg
+        self.layer_idx = layer_idx
+        self.rank, self.world_size, self.group = 0, 1, None
+        self._site_modes = None
+        self.comm = None
+        e, d, n, r, k = cfg.d_inner, cfg.d_model, cfg.d_state, cfg.dt_rank, cfg.d_conv
+        self.es = e
+        self.in_proj = nn.Linear(d, 2 * e, bias=cfg.bias)
+        self.conv1d = nn.Conv1d(e, e, kernel_size=k, groups=e, padding=k - 1, bias=cfg.conv_bias)
+        self.x_proj = nn.Linear(e, r + 2 * n, bias=False)
+        self.dt_proj = nn.Linear(r, e, bias=True)
+        self.A_log = nn.Parameter(torch.empty(e, n))
+        self.D = nn.Parameter(torch.empty(e))
+        self.out_proj = nn.Linear(e, d, bias=cfg.bias)
+        with torch.no_grad():  # S4D-real init, as model.py:172-181
+            a = torch.arange(1, n + 1, dtype=torch.float32)[None, :].expand(e, n)
+            self.A_log.copy_(torch.log(a))
+            self.D.fill_(1.0)
+
+    def _out_bias(self):
+        return self.out_proj.bias
+
+
+class MambaBlock(nn.Module):
+    def __init__(self, cfg: MambaConfig, layer_idx: int):
+        super().__init__()
+        self.norm = RMSNorm(cfg.d_model, eps=cfg.layer_norm_epsilon)
+        self.mixer = MambaMixer(cfg, layer_idx)
+
+    def prefill(self, x, cache: LayerCache | None):
+        y, conv_state, ssm_state = self.mixer.prefill(self.norm(x), cache)
+        return x + y, conv_state, ssm_state
+
+    def step(self, x_t, cache: LayerCache):
+        return x_t + self.mixer.step(self.norm(x_t), cache)
+
+
+class _LMKernels:
+    """Fused LM forward shared by MambaLM and TPMambaLM: embedding gather, one
+    normed activation buffer and an fp32 residual stream that each layer's
+    out_proj reduction updates in place together with the next RMSNorm."""
+
+    def _param_dtype(self):
+        return self.embedding.weight.dtype
+
+    def _embed(self, ids: torch.Tensor) -> torch.Tensor:
+        L.require_cuda(ids, "input_ids")
+        ids = ids.reshape(-1).to(torch.int64).contiguous()
+        d = self.cfg.d_model
+        out = torch.empty(ids.numel(), d, device=ids.device, dtype=torch.float32)
+        L.call("mtp_embedding", L.ptr(ids), ids.numel(), L.ptr(self.embedding.weight), d,
+               L.dtype_code(self.embedding.weight.dtype), L.ptr(out), L.stream_ptr())
+        return out
+
+    def _norm_into(self, resid, w, out):
+        L.call("mtp_rmsnorm", L.ptr(resid), resid.shape[0], resid.shape[1], L.ptr(w), L.dtype_code(w.dtype),
+               float(self.cfg.layer_norm_epsilon), L.ptr(out), L.dtype_code(out.dtype), L.stream_ptr())
+
+    def _next_norm_w(self, i):
+        return self.layers[i + 1].norm.weight if i + 1 < len(self.layers) else self.norm_f.weight
+
+    def _lm_head(self, normed: torch.Tensor) -> torch.Tensor:
+        w = self.embedding.weight
+        logits = torch.empty(normed.shape[0], w.shape[0], device=normed.device, dtype=w.dtype)
+        from . import _mixer
+
+        ev = _mixer._prof_begin() if normed.shape[0] > 64 else None
+        L.call("mtp_gemm", L.ptr(normed), L.ptr(w), L.ptr(logits), normed.shape[0], w.shape[0], w.shape[1],
+               normed.stride(0), w.stride(0), logits.stride(0), L.dtype_code(w.dtype), L.dtype_code(logits.dtype),
+               L.EPI_STORE, None, 0, L.stream_ptr())
+        _mixer._prof_end(ev, "lm_head", 2.0 * normed.shape[0] * w.shape[0] * w.shape[1])
+        return logits
+
+    def _forward_prefill(self, input_ids: torch.Tensor, cache=None):
+        b, l = input_ids.shape
+        resid = self._embed(input_ids)
+        normed = torch.empty(resid.shape, device=resid.device, dtype=self._param_dtype())
+        self._norm_into(resid, self.layers[0].norm.weight, normed)
+        eps = self.cfg.layer_norm_epsilon
+        new_layers = []
+        for i, layer in enumerate(self.layers):
+            lc = cache.layers[i] if cache is not None else None
+            ci = lc.conv_state if lc is not None else None
+            si = lc.ssm_state.float().contiguous() if lc is not None else None
+            cf, sf = layer.mixer._prefill_core(normed, b, l, ci, si, resid, self._next_norm_w(i), eps, normed)
+            new_layers.append(LayerCache(conv_state=cf, ssm_state=sf))
+        logits = self._lm_head(normed)
+        return logits.view(b, l, -1), MambaCache(new_layers)
+
+    def _forward_step(self, input_ids: torch.Tensor, cache):
+        b = input_ids.shape[0]
+        resid = self._embed(input_ids[:, :1])
+        normed = torch.empty(resid.shape, device=resid.device, dtype=self._param_dtype())
+        self._norm_into(resid, self.layers[0].norm.weight, normed)
+        eps = self.cfg.layer_norm_epsilon
+        for i, layer in enumerate(self.layers):
+            lc = cache.layers[i]
+            layer.mixer._step_core(normed, lc.conv_state, lc.ssm_state, resid, self._next_norm_w(i), eps, normed)
+        return self._lm_head(normed).view(b, 1, -1)
+
+    def greedy_next(self, logits: torch.Tensor) -> torch.Tensor:
+        """argmax over the vocabulary of the last position: [b, l, V] -> [b, 1] (libmtp kernel)."""
+        last = logits[:, -1, :].contiguous()
+        out = torch.empty(last.shape[0], 1, device=last.device, dtype=torch.int64)
+        L.call("mtp_argmax_rows", L.ptr(last), last.shape[0], last.shape[1], last.stride(0), L.dtype_code(last.dtype),
+               L.ptr(out), L.stream_ptr())
+        return out
+
+    @torch.no_grad()
+    def generate(self, input_ids: torch.Tensor, max_new_tokens: int, greedy: bool = True):
+        """Prefill, then greedy decode through the cache (model.py:355-365)."""
+        logits, cache = self.prefill(input_ids)
+        next_id = self.greedy_next(logits)
+        tokens = [input_ids, next_id]
+        for _ in range(max_new_tokens - 1):
+            logits = self.step(next_id, cache)
+            next_id = self.greedy_next(logits)
+            tokens.append(next_id)
+        return torch.cat(tokens, dim=1)
+
+
+class MambaLM(_LMKernels, nn.Module):
+    """Embedding -> n_layer blocks -> final norm -> tied lm_head (model.py:314-397)."""
+
+    def __init__(self, cfg: MambaConfig):
+        super().__init__()
+        self.cfg = cfg
+        self.embedding = nn.Embedding(cfg.vocab_size, cfg.d_model)
+        self.layers = nn.ModuleList([MambaBlock(cfg, i) for i in range(cfg.n_layer)])
+        self.norm_f = RMSNorm(cfg.d_model, eps=cfg.layer_norm_epsilon)
+
+    def lm_head(self, x: torch.Tensor) -> torch.Tensor:
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).to(self._param_dtype()).contiguous()
+        return self._lm_head(x2).view(*shape[:-1], -1)
+
+    @torch.no_grad()
+    def prefill(self, input_ids: torch.Tensor, cache: MambaCache | None = None):
+        """input_ids [b, l] -> (logits [b, l, V] in the model dtype, new MambaCache)."""
+        return self._forward_prefill(input_ids, cache)
+
+    @torch.no_grad()
+    def step(self, input_ids: torch.Tensor, cache: MambaCache):
+        """input_ids [b, 1] -> logits [b, 1, V]; mutates the cache in place."""
+        return self._forward_step(input_ids, cache)
+
+    @classmethod
+    def from_pretrained(cls, hf_path: str, dtype=torch.float32, device="cuda") -> "MambaLM":
+        """Loads an HF ``state-spaces/mamba-*-hf`` directory (model.py:367-397)."""
+        cfg = MambaConfig.from_hf_config(os.path.join(hf_path, "config.json"))
+        return cls.from_state_dict(cfg, load_hf_state_dict(hf_path), dtype, device)
+
+    @classmethod
+    def from_state_dict(cls, cfg: MambaConfig, sd: dict, dtype=torch.float32, device="cuda") -> "MambaLM":
+        """Builds the model from an HF-named state dict (``backbone.*`` keys)."""
+        with torch.device("meta"):
+            model = cls(cfg)
+        remapped = {"embedding.weight": sd["backbone.embeddings.weight"],
+                    "norm_f.weight": sd["backbone.norm_f.weight"]}
+        for i in range(cfg.n_layer):
+            p, q = f"backbone.layers.{i}.", f"layers.{i}."
+            remapped[q + "norm.weight"] = sd[p + "norm.weight"]
+            for k in ("in_proj.weight", "conv1d.weight", "x_proj.weight", "dt_proj.weight", "dt_proj.bias", "A_log",
+                      "D", "out_proj.weight"):
+                remapped[q + "mixer." + k] = sd[p + "mixer." + k]
+            if cfg.conv_bias:
+                remapped[q + "mixer.conv1d.bias"] = sd[p + "mixer.conv1d.bias"]
+            if cfg.bias:
+                remapped[q + "mixer.in_proj.bias"] = sd[p + "mixer.in_proj.bias"]
+                remapped[q + "mixer.out_proj.bias"] = sd[p + "mixer.out_proj.bias"]
+        model = model.to_empty(device=device).to(dtype)
+        missing, unexpected = model.load_state_dict({k: v.to(dtype) for k, v in remapped.items()}, strict=True)
+        assert not missing and not unexpected, (missing, unexpected)
+        return model.eval()

@@ -1,0 +1,314 @@
+"""Collectives and sharding helpers with the reference's names
+(``mamba_lite/tp_utils.py``): ``CommCounter``, ``ALLREDUCE_FNS``,
+``channel_slice``, ``SITES``, ``site_dtype``.
+
+The "fp32", "fp16" and "int8" (= "int8_gather_tok") reductions run in
+libmtp's peer-memory kernels over NVLink (one allocation per rank mapped by
+its peers through CUDA IPC; see ``comm_for``).  The remaining variants of the
+reference ("int8_gather" per-tensor, "int8_sum", "int8_legacy") keep the
+reference's torch.distributed algorithm on CUDA tensors.  Nothing here runs on
+the CPU.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import torch
+import torch.distributed as dist
+
+from . import _lib as L
+
+
+class CommCounter:
+    """Counts collectives per mixer (``count``) and their payload bytes
+    (``bytes``) with the reference's accounting (tp_utils.py:11-20)."""
+
+    def __init__(self):
+        self.count = 0
+        self.bytes = 0
+
+    def reset(self):
+        self.count = 0
+        self.bytes = 0
+
+
+# names served by the fused kernels -> libmtp wire mode
+KERNEL_MODES = {"fp32": L.RED_FP32, "fp16": L.RED_FP16, "int8": L.RED_INT8TOK, "int8_gather_tok": L.RED_INT8TOK}
+ALL_NAMES = ("fp32", "fp16", "int8", "int8_legacy", "int8_sum", "int8_gather", "int8_gather_tok")
+SITES = ("x_proj", "out_proj")
+
+
+def channel_slice(rank: int, world_size: int, total: int) -> slice:
+    """Contiguous channel shard of ``total`` for ``rank`` (tp_utils.py:163-166)."""
+    if total % world_size:
+        raise AssertionError(f"{total} not divisible by world_size={world_size}")
+    shard = total // world_size
+    return slice(rank * shard, (rank + 1) * shard)
+
+
+def site_dtype(spec, layer_idx: int, site: str) -> str:
+    """Reduction name for one (layer, site): ``spec`` is a name used everywhere
+    or a ``{(layer_idx, site): name}`` map whose missing keys mean "fp32"
+    (tp_utils.py:172-180)."""
+    if site not in SITES:
+        raise AssertionError(site)
+    name = spec if isinstance(spec, str) else spec.get((layer_idx, site), "fp32")
+    if name not in ALL_NAMES:
+        raise AssertionError(f"unknown allreduce dtype {name!r}")
+    return name
+
+
+def build_spec(cfg_def, n_layer: int):
+    """``{"default": name, "overrides": {"L:site": name}}`` -> per-site map
+    (the precision-map format of scripts/quant_gpu_bench.py:31-39)."""
+    if isinstance(cfg_def, str):
+        return cfg_def
+    spec = {}
+    for layer in range(n_layer):
+        for site in SITES:
+            spec[(layer, site)] = cfg_def["overrides"].get(f"{layer}:{site}", cfg_def["default"])
+    return spec
+
+
+def count_collective(counter: CommCounter | None, name: str, shape, dtype: torch.dtype) -> None:
+    """Collective count and payload bytes of one site call, as the reference
+    accounts them (tp_utils.py:24-26, :38-40, :62-72, :89-98, :114-116)."""
+    if counter is None:
+        return
+    numel = 1
+    for s in shape:
+        numel *= int(s)
+    es = torch.empty((), dtype=dtype).element_size()
+    if name == "fp32":
+        counter.count += 1
+        counter.bytes += numel * es
+    elif name == "fp16":
+        counter.count += 1
+        counter.bytes += numel * 2
+    elif name in ("int8", "int8_gather_tok"):
+        rows = numel // int(shape[-1]) if len(shape) else 1
+        counter.count += 1
+        counter.bytes += 4 * rows + numel
+    elif name == "int8_gather":
+        counter.count += 1
+        counter.bytes += 4 + numel
+    elif name == "int8_sum":
+        counter.count += 2
+        counter.bytes += 4 + numel
+    elif name == "int8_legacy":
+        counter.count += 2
+        counter.bytes += es + 4 * numel
+    else:
+        raise AssertionError(name)
+
+
+# ------------------------------------------------------------------ comm contexts
+_COMMS: dict = {}
+
+
+def _group_key(group):
+    return id(group) if group is not None else None
+
+
+class Comm:
+    """One libmtp comm context: per-site receive slots sized for rows of
+    ``cols_x`` (x_proj site) and ``cols_out`` (out_proj site) values."""
+
+    def __init__(self, group, rank: int, ws: int, cols_x: int, cols_out: int, max_rows: int | None = None,
+                 timeout_s: float | None = None):
+        self.rank, self.ws = rank, ws
+        self.max_rows = max_rows or int(os.environ.get("MTP_COMM_MAX_ROWS", "8192"))
+        timeout_s = timeout_s if timeout_s is not None else float(os.environ.get("MTP_COMM_TIMEOUT_S", "60"))
+        h = C.c_void_p()
+        L.call("mtp_comm_create", rank, ws, self.max_rows, cols_x, cols_out, float(timeout_s), C.byref(h))
+        self.handle = h
+        if ws > 1:
+            mine = (C.c_uint8 * 64)()
+            L.call("mtp_comm_ipc_handle", h, mine)
+            handles = exchange_handles(bytes(mine), group, ws)
+            buf = (C.c_uint8 * (64 * ws)).from_buffer_copy(b"".join(handles))
+            L.call("mtp_comm_open_peers", h, buf)
+            dist.barrier(group=group)
+
+    @property
+    def ptr(self):
+        return self.handle
+
+    def status(self) -> int:
+        s = C.c_int(0)
+        L.call("mtp_comm_status", self.handle, C.byref(s))
+        return s.value
+
+    def reset_status(self) -> None:
+        L.call("mtp_comm_reset_status", self.handle)
+
+    def check(self) -> None:
+        """Raises if a bounded wait of a reduction timed out (after a synchronize)."""
+        torch.cuda.synchronize()
+        st = self.status()
+        if st != L.MTP_OK:
+            raise L.MTPError(st, "a collective timed out waiting for a peer (rank failed or stalled)")
+
+    def destroy(self) -> None:
+        if self.handle:
+            L.call("mtp_comm_destroy", self.handle)
+            self.handle = C.c_void_p()
+
+
+def exchange_handles(mine: bytes, group, ws: int) -> list[bytes]:
+    """All ranks' 64-byte CUDA IPC handles, in rank order, over the process
+    group (any backend).  A rank that never joins ends the call with the
+    group's timeout error on the others."""
+    if len(mine) != 64:
+        raise ValueError("an IPC handle is 64 bytes")
+    gathered = [None] * ws
+    dist.all_gather_object(gathered, mine, group=group)
+    if any(not isinstance(h, bytes) or len(h) != 64 for h in gathered):
+        raise RuntimeError("malformed IPC handle from a peer")
+    return gathered
+
+
+def get_comm(group, rank: int, ws: int, cols_x: int, cols_out: int) -> Comm | None:
+    """Shared context for (group, device, site widths); collective on first use."""
+    if ws == 1:
+        return None
+    key = (_group_key(group), torch.cuda.current_device(), cols_x, cols_out)
+    c = _COMMS.get(key)
+    if c is None:
+        c = Comm(group, rank, ws, cols_x, cols_out)
+        _COMMS[key] = c
+    return c
+
+
+def comm_for(mixer):
+    c = get_comm(mixer.group, mixer.rank, mixer.world_size, mixer.cfg.dt_rank + 2 * mixer.cfg.d_state,
+                 mixer.cfg.d_model)
+    return None if c is None else c.ptr
+
+
+def all_comms() -> list[Comm]:
+    return list(_COMMS.values())
+
+
+def destroy_comms() -> None:
+    for c in _COMMS.values():
+        c.destroy()
+    _COMMS.clear()
+
+
+# ------------------------------------------------------------------ reference-signature functions
+def _world(group) -> tuple[int, int]:
+    if not dist.is_available() or not dist.is_initialized():
+        return 0, 1
+    return dist.get_rank(group), dist.get_world_size(group)
+
+
+def _kernel_allreduce(name: str, tensor: torch.Tensor, group, counter) -> torch.Tensor:
+    L.require_cuda(tensor, f"allreduce {name}")
+    count_collective(counter, name, tensor.shape, tensor.dtype)
+    rank, ws = _world(group)
+    cols = tensor.shape[-1] if tensor.dim() else 1
+    rows = tensor.numel() // cols
+    src = tensor.reshape(rows, cols).float().contiguous()
+    out = src if tensor.dtype == torch.float32 and name == "fp32" else torch.empty_like(src)
+    comm = get_comm(group, rank, ws, cols, cols)
+    L.call("mtp_allreduce", None if comm is None else comm.ptr, 1, KERNEL_MODES[name], L.ptr(src), L.ptr(out), rows,
+           cols, L.stream_ptr())
+    if name == "fp32":
+        # in place, like the reference (tp_utils.py:27-28)
+        if out.data_ptr() != tensor.data_ptr():
+            tensor.copy_(out.view(tensor.shape))
+        return tensor
+    return out.view(tensor.shape).to(tensor.dtype)
+
+
+def all_reduce_sum(tensor, group=None, counter=None):
+    return _kernel_allreduce("fp32", tensor, group, counter)
+
+
+def all_reduce_sum_fp16(tensor, group=None, counter=None):
+    return _kernel_allreduce("fp16", tensor, group, counter)
+
+
+def all_reduce_sum_int8_gather_tok(tensor, group=None, counter=None):
+    return _kernel_allreduce("int8", tensor, group, counter)
+
+
+def _payload_gather_dequant(tensor: torch.Tensor, group, rows: int, cols: int) -> torch.Tensor:
+    """Quantise [rows, cols] with libmtp, all-gather the packed payloads with
+    torch.distributed, dequant-sum in rank order with libmtp."""
+    _, ws = _world(group)
+    t = tensor.reshape(rows, cols).float().contiguous()
+    payload = torch.empty(rows * (4 + cols), dtype=torch.uint8, device=t.device)
+    scales = payload[: 4 * rows].view(torch.float32)
+    q = payload[4 * rows:].view(torch.int8)
+    L.call("mtp_quantize_rows_int8", L.ptr(t), rows, cols, cols, L.ptr(scales), L.ptr(q), L.stream_ptr())
+    gathered = torch.empty(ws * payload.numel(), dtype=torch.uint8, device=t.device)
+    if ws > 1:
+        dist.all_gather_into_tensor(gathered, payload, group=group)
+    else:
+        gathered.copy_(payload)
+    out = torch.empty(rows, cols, dtype=torch.float32, device=t.device)
+    L.call("mtp_dequant_sum", L.ptr(gathered), ws, rows, cols, L.ptr(out), L.stream_ptr())
+    return out
+
+
+def all_reduce_sum_int8_gather(tensor, group=None, counter=None):
+    """One int8 scale for the whole tensor (tp_utils.py:134-142)."""
+    L.require_cuda(tensor, "int8_gather")
+    count_collective(counter, "int8_gather", tensor.shape, tensor.dtype)
+    out = _payload_gather_dequant(tensor, group, 1, tensor.numel())
+    return out.view(tensor.shape).to(tensor.dtype)
+
+
+def all_reduce_sum_int8_sum(tensor, group=None, counter=None):
+    """Shared scale from a MAX reduction, +-(127 // world_size) int8 values
+    summed in int8 (tp_utils.py:78-100)."""
+    L.require_cuda(tensor, "int8_sum")
+    count_collective(counter, "int8_sum", tensor.shape, tensor.dtype)
+    _, ws = _world(group)
+    qmax = 127 // ws
+    t = tensor.contiguous().float()
+    amax = t.abs().max().clamp(min=1e-8).reshape(1)
+    if ws > 1:
+        dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=group)
+    scale = amax / qmax
+    q = torch.clamp(torch.round(t / scale), -qmax, qmax).to(torch.int8)
+    if ws > 1:
+        dist.all_reduce(q, op=dist.ReduceOp.SUM, group=group)
+    return (q.float() * scale).to(tensor.dtype)
+
+
+def all_reduce_sum_int8_legacy(tensor, group=None, counter=None):
+    """Per-tensor scale agreed through a MAX reduction read back to the host,
+    then an int32 SUM (tp_utils.py:45-75); not graph-capturable."""
+    L.require_cuda(tensor, "int8_legacy")
+    count_collective(counter, "int8_legacy", tensor.shape, tensor.dtype)
+    _, ws = _world(group)
+    t = tensor.contiguous()
+    m = t.abs().max().clamp(min=1e-8).reshape(1)
+    if ws > 1:
+        dist.all_reduce(m, op=dist.ReduceOp.MAX, group=group)
+    scale = m.item() / 127.0
+    q32 = torch.clamp(torch.round(t / scale), -127, 127).to(torch.int8).to(torch.int32)
+    if ws > 1:
+        dist.all_reduce(q32, op=dist.ReduceOp.SUM, group=group)
+    return (q32.float() * scale).to(tensor.dtype)
+
+
+ALLREDUCE_FNS = {
+    "fp32": all_reduce_sum,
+    "fp16": all_reduce_sum_fp16,
+    "int8": all_reduce_sum_int8_gather_tok,
+    "int8_legacy": all_reduce_sum_int8_legacy,
+    "int8_sum": all_reduce_sum_int8_sum,
+    "int8_gather": all_reduce_sum_int8_gather,
+    "int8_gather_tok": all_reduce_sum_int8_gather_tok,
+}
+
+
+def torch_allreduce(name: str, tensor: torch.Tensor, group) -> torch.Tensor:
+    """The reference algorithm of an out-of-kernel variant, without counting
+    (the mixer counts)."""
+    return ALLREDUCE_FNS[name](tensor, group, None)

@@ -543,3 +543,64 @@ def state_dict_numpy(sd) -> dict:
 
 def inv_softplus(x):
     return x + math.log(-math.expm1(-x))
+
+
+# --------------------------------------------------------------------------
+# kernel-level restatements (pieces of tp_model.py:93-129 / :145-173) used to
+# check single kernels; the inputs are the tensors the kernels receive.
+# --------------------------------------------------------------------------
+def conv_silu_ref(x, conv_w, conv_b, hist):
+    """x [B, L, Es] raw in_proj x half; hist [B, Es, K-1] or None.
+    Returns (silu(conv) [B, L, Es], final history [B, Es, K-1]) (tp_model.py:93-103)."""
+    b, l, es = x.shape
+    k = conv_w.shape[1]
+    xs = np.transpose(x.astype(F32), (0, 2, 1))
+    h = np.zeros((b, es, k - 1), F32) if hist is None else hist.astype(F32)
+    xp = np.concatenate([h, xs], axis=-1)
+    conv = np.zeros((b, es, l), F32)
+    for j in range(k):
+        conv = (conv + conv_w[None, :, j, None] * xp[..., j:j + l]).astype(F32)
+    if conv_b is not None:
+        conv = (conv + conv_b[None, :, None]).astype(F32)
+    return np.transpose(silu(conv), (0, 2, 1)), xp[..., l:].copy()
+
+
+def scan_ref(x, z, dt, B, C, A_log, Dp, conv_w, conv_b, conv_init, ssm_init):
+    """Fused prefill kernel contract: x, z [B, L, Es] (raw), dt [B, L, Es] after
+    softplus, B, C [B, L, N].  Returns (y [B,L,Es], conv_final, ssm_final)
+    (tp_model.py:93-103, :113-129)."""
+    xc, cf = conv_silu_ref(x, conv_w, conv_b, conv_init)
+    b, l, es = x.shape
+    n = A_log.shape[1]
+    A = (-np.exp(A_log.astype(F32))).astype(F32)
+    h = np.zeros((b, es, n), F32) if ssm_init is None else ssm_init.astype(F32).copy()
+    ys = np.zeros((b, l, es), F32)
+    for t in range(l):
+        dtt = dt[:, t, :, None]
+        dA = np.exp((dtt * A[None]).astype(F32)).astype(F32)
+        dBx = ((dtt * B[:, t, None, :]).astype(F32) * xc[:, t, :, None]).astype(F32)
+        h = (dA * h + dBx).astype(F32)
+        ys[:, t] = np.einsum("bdn,bn->bd", h, C[:, t]).astype(F32)
+    y = ((ys + xc * Dp[None, None]) * silu(z)).astype(F32)
+    return y, cf, h
+
+
+def step_ref(x, z, dt_low, W_dt, b_dt, B, C, A_log, Dp, conv_w, conv_b, conv_state, ssm_state):
+    """Single-token step kernel contract (tp_model.py:145-173).  x, z [B, Es];
+    dt_low [B, R]; B, C [B, N].  Returns (y, new conv_state, new ssm_state)."""
+    k = conv_w.shape[1]
+    cin = np.concatenate([conv_state.astype(F32), x.astype(F32)[:, :, None]], axis=-1)
+    conv = np.zeros(x.shape, F32)
+    for j in range(k):
+        conv = (conv + cin[:, :, j] * conv_w[None, :, j]).astype(F32)
+    if conv_b is not None:
+        conv = (conv + conv_b[None]).astype(F32)
+    xc = silu(conv)
+    dt = softplus(_linear(dt_low, W_dt, b_dt))
+    A = (-np.exp(A_log.astype(F32))).astype(F32)
+    dA = np.exp((dt[..., None] * A[None]).astype(F32)).astype(F32)
+    dBx = ((dt[..., None] * B[:, None, :]).astype(F32) * xc[..., None]).astype(F32)
+    h = (ssm_state.astype(F32) * dA + dBx).astype(F32)
+    y = np.einsum("bdn,bn->bd", h, C).astype(F32)
+    y = ((y + xc * Dp) * silu(z)).astype(F32)
+    return y, cin[:, :, 1:].copy(), h

@@ -1,0 +1,244 @@
+"""Kernel-level parity on the GPU, through the C ABI: each libmtp kernel against
+the numpy oracle, a torch fp32 reference (GEMMs) or the reference-recorded
+golden fixtures (quantiser)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from mamba_tp_lite_b200 import _lib as L
+from oracle import mamba_oracle as O
+from tests.gpu_util import dev, gemm, n, t
+
+pytestmark = pytest.mark.gpu
+
+BF = torch.bfloat16
+
+
+def _rand(shape, seed, scale=1.0):
+    return np.random.default_rng(seed).standard_normal(shape).astype(np.float32) * scale
+
+
+# ------------------------------------------------------------------ GEMMs
+TC_SHAPES = [  # (M, N, K): tile edges, partial tiles, x_proj-like skinny N, lm_head-like ragged N, tiny K
+    (128, 256, 64), (256, 512, 128), (300, 200, 72), (1000, 160, 512), (513, 2000, 96), (2048, 1024, 2048),
+    (777, 80, 1536), (384, 50280 // 40, 256), (130, 4096, 128), (64 * 3 + 5, 96, 256)]
+
+
+@pytest.mark.parametrize("M,N,K", TC_SHAPES)
+@pytest.mark.parametrize("out_dtype", [torch.float32, BF])
+def test_tcgen05_gemm_matches_fp32_torch(M, N, K, out_dtype):
+    a = torch.randn(M, K, device=dev(), dtype=BF)
+    w = torch.randn(N, K, device=dev(), dtype=BF) * 0.05
+    c = gemm(a, w, out_dtype, algo=L.GEMM_TCGEN05)
+    ref = a.float() @ w.float().T
+    torch.cuda.synchronize()
+    tol = 2e-3 if out_dtype == torch.float32 else 1e-2
+    torch.testing.assert_close(c.float(), ref, atol=tol * ref.abs().max().item(), rtol=tol)
+
+
+def test_tcgen05_gemm_softplus_bias_epilogue_and_strides():
+    M, N, K = 640, 384, 160
+    base = torch.randn(M, K + 32, device=dev(), dtype=BF)  # lda = K + 32 (still a multiple of 8)
+    a = base[:, :K]
+    w = torch.randn(N, K, device=dev(), dtype=BF) * 0.05
+    bias = torch.randn(N, device=dev(), dtype=torch.float32) - 3
+    c = gemm(a, w, torch.float32, L.EPI_BIAS_SOFTPLUS, bias, L.GEMM_TCGEN05)
+    ref = torch.nn.functional.softplus(a.float() @ w.float().T + bias)
+    torch.testing.assert_close(c, ref, atol=2e-3, rtol=2e-3)
+    c2 = gemm(a, w, BF, L.EPI_BIAS, bias.to(BF), L.GEMM_TCGEN05)
+    torch.testing.assert_close(c2.float(), a.float() @ w.float().T + bias.to(BF).float(), atol=3e-2, rtol=1e-2)
+
+
+def test_tcgen05_gemm_is_deterministic():
+    a = torch.randn(1024, 2048, device=dev(), dtype=BF)
+    w = torch.randn(1536, 2048, device=dev(), dtype=BF)
+    c1 = gemm(a, w, torch.float32, algo=L.GEMM_TCGEN05)
+    c2 = gemm(a, w, torch.float32, algo=L.GEMM_TCGEN05)
+    assert torch.equal(c1, c2)
+
+
+@pytest.mark.parametrize("algo", [L.GEMM_SIMT, L.GEMM_GEMV])
+@pytest.mark.parametrize("dtype", [torch.float32, BF])
+@pytest.mark.parametrize("M,N,K", [(1, 300, 200), (3, 1024, 2048), (8, 160, 96), (32, 517, 333), (70, 64, 16)])
+def test_cuda_core_gemms_match_fp32_torch(algo, dtype, M, N, K):
+    a = torch.randn(M, K, device=dev(), dtype=dtype)
+    w = torch.randn(N, K, device=dev(), dtype=dtype) * 0.05
+    bias = torch.randn(N, device=dev(), dtype=torch.float32)
+    c = gemm(a, w, torch.float32, L.EPI_BIAS_SOFTPLUS, bias, algo)
+    ref = torch.nn.functional.softplus(a.float() @ w.float().T + bias)
+    torch.testing.assert_close(c, ref, atol=1e-4, rtol=1e-4)
+
+
+# ------------------------------------------------------------------ conv / scan / step
+def _ssm_inputs(b, l, es, nst, seed, dtype):
+    rng = np.random.default_rng(seed)
+    r = lambda *s: rng.standard_normal(s).astype(np.float32)
+    rnd = O.bf16_round if dtype == BF else (lambda v: v)
+    x = rnd(r(b, l, es))
+    z = rnd(r(b, l, es))
+    dt = O.softplus(r(b, l, es) - 3.0)
+    Bm, Cm = r(b, l, nst), r(b, l, nst)
+    A_log = rnd(np.log(np.tile(np.arange(1, nst + 1, dtype=np.float32), (es, 1))) + 0.1 * r(es, nst))
+    Dp = rnd(1 + 0.1 * r(es))
+    conv_w = rnd(0.5 * r(es, 4))
+    conv_b = rnd(0.5 * r(es))
+    conv_init = rnd(r(b, es, 3))
+    ssm_init = r(b, es, nst)
+    return x, z, dt, Bm, Cm, A_log, Dp, conv_w, conv_b, conv_init, ssm_init
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, BF])
+@pytest.mark.parametrize("b,l,es,nst,init", [(2, 37, 64, 16, True), (1, 70, 200, 16, False), (3, 5, 96, 8, True),
+                                               (4, 129, 1024, 16, True), (2, 2, 32, 16, False)])
+def test_scan_prefill_matches_oracle(dtype, b, l, es, nst, init):
+    x, z, dt, Bm, Cm, A_log, Dp, cw, cb, ci, si = _ssm_inputs(b, l, es, nst, 5, dtype)
+    if not init:
+        ci = si = None
+    y_ref, cf_ref, sf_ref = O.scan_ref(x, z, dt, Bm, Cm, A_log, Dp, cw, cb, ci, si)
+    T = b * l
+    xz = t(np.concatenate([x, z], -1).reshape(T, 2 * es), dtype)
+    dtt = t(dt.reshape(T, es))
+    bc = t(np.concatenate([Bm, Cm], -1).reshape(T, 2 * nst))
+    y = torch.empty(T, es, device=dev(), dtype=dtype)
+    cf = torch.empty(b, es, 3, device=dev(), dtype=dtype)
+    sf = torch.empty(b, es, nst, device=dev(), dtype=torch.float32)
+    g = lambda a: None if a is None else t(a, dtype)
+    L.call("mtp_scan_prefill", L.ptr(xz), 2 * es, L.ptr(dtt), es, L.ptr(bc), 2 * nst, L.ptr(t(A_log, dtype)),
+           L.ptr(t(Dp, dtype)), L.ptr(t(cw, dtype)), L.ptr(t(cb, dtype)), L.ptr(g(ci)),
+           L.ptr(None if si is None else t(si)), L.ptr(y), es, L.ptr(cf), L.ptr(sf), b, l, es, nst, 4,
+           L.dtype_code(dtype), L.stream_ptr())
+    tol = 2e-4 if dtype == torch.float32 else 2e-2
+    np.testing.assert_allclose(n(y).reshape(b, l, es), y_ref, atol=tol, rtol=tol)
+    np.testing.assert_allclose(n(cf), cf_ref, atol=1e-6, rtol=0)
+    np.testing.assert_allclose(n(sf), sf_ref, atol=tol, rtol=tol)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, BF])
+def test_conv1d_silu_matches_oracle(dtype):
+    b, l, es = 3, 19, 130
+    x, z, *_ , cw, cb, ci, _ = _ssm_inputs(b, l, es, 16, 9, dtype)
+    xc_ref, _ = O.conv_silu_ref(x, cw, cb, ci)
+    T = b * l
+    xz = t(np.concatenate([x, z], -1).reshape(T, 2 * es), dtype)
+    xc = torch.empty(T, es, device=dev(), dtype=dtype)
+    L.call("mtp_conv1d_silu", L.ptr(xz), 2 * es, L.ptr(t(cw, dtype)), L.ptr(t(cb, dtype)), L.ptr(t(ci, dtype)),
+           L.ptr(xc), es, b, l, es, 4, L.dtype_code(dtype), L.stream_ptr())
+    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    np.testing.assert_allclose(n(xc).reshape(b, l, es), xc_ref, atol=tol, rtol=tol)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, BF])
+@pytest.mark.parametrize("b,es,nst,R", [(1, 512, 16, 128), (32, 256, 16, 64), (5, 96, 8, 2), (64, 64, 16, 160)])
+def test_step_matches_oracle(dtype, b, es, nst, R):
+    x, z, _, Bm, Cm, A_log, Dp, cw, cb, ci, si = _ssm_inputs(b, 1, es, nst, 13, dtype)
+    x, z, Bm, Cm = x[:, 0], z[:, 0], Bm[:, 0], Cm[:, 0]
+    rnd = O.bf16_round if dtype == BF else (lambda v: v)
+    dl = rnd(_rand((b, R), 3))
+    W = rnd(_rand((es, R), 4, 0.1))
+    bd = rnd(_rand((es,), 6) - 3)
+    y_ref, cs_ref, ss_ref = O.step_ref(x, z, dl, W, bd, Bm, Cm, A_log, Dp, cw, cb, ci, si)
+    xz = t(np.concatenate([x, z], -1), dtype)
+    cs = t(ci, dtype)
+    ss = t(si)
+    y = torch.empty(b, es, device=dev(), dtype=dtype)
+    L.call("mtp_step", L.ptr(xz), 2 * es, L.ptr(t(dl, dtype)), R, L.ptr(t(W, dtype)), L.ptr(t(bd, dtype)),
+           L.ptr(t(np.concatenate([Bm, Cm], -1))), 2 * nst, L.ptr(t(A_log, dtype)), L.ptr(t(Dp, dtype)),
+           L.ptr(t(cw, dtype)), L.ptr(t(cb, dtype)), L.ptr(cs), L.ptr(ss), L.ptr(y), es, b, es, nst, R, 4,
+           L.dtype_code(dtype), L.stream_ptr())
+    tol = 2e-5 if dtype == torch.float32 else 2e-2
+    np.testing.assert_allclose(n(y), y_ref, atol=tol, rtol=tol)
+    np.testing.assert_allclose(n(cs), cs_ref, atol=0, rtol=0)
+    np.testing.assert_allclose(n(ss), ss_ref, atol=tol, rtol=tol)
+
+
+# ------------------------------------------------------------------ quantiser / reductions at world size 1
+def test_quantiser_bit_exact_vs_reference_golden(golden_dir):
+    g = dict(np.load(os.path.join(golden_dir, "quant_rows.npz")))
+    for name in sorted({k.split("/")[0] for k in g}):
+        x = g[f"{name}/input"]
+        rows, cols = x.shape
+        sc = torch.empty(rows, device=dev(), dtype=torch.float32)
+        q = torch.empty(rows, cols, device=dev(), dtype=torch.int8)
+        L.call("mtp_quantize_rows_int8", L.ptr(t(x)), rows, cols, cols, L.ptr(sc), L.ptr(q), L.stream_ptr())
+        assert sc.cpu().numpy().tobytes() == g[f"{name}/scales"].tobytes(), name
+        assert q.cpu().numpy().tobytes() == g[f"{name}/q"].tobytes(), name
+
+
+def test_quantiser_bit_exact_vs_oracle_large():
+    x = _rand((4096, 2048), 21)
+    x[:, ::97] *= 20
+    s_ref, q_ref = O.quantize_rows_int8(x)
+    sc = torch.empty(4096, device=dev(), dtype=torch.float32)
+    q = torch.empty(4096, 2048, device=dev(), dtype=torch.int8)
+    L.call("mtp_quantize_rows_int8", L.ptr(t(x)), 4096, 2048, 2048, L.ptr(sc), L.ptr(q), L.stream_ptr())
+    assert sc.cpu().numpy().tobytes() == s_ref.tobytes()
+    assert q.cpu().numpy().tobytes() == q_ref.tobytes()
+
+
+@pytest.mark.parametrize("ws", [2, 4])
+def test_dequant_sum_bit_exact_on_reference_payloads(golden_dir, ws):
+    g = dict(np.load(os.path.join(golden_dir, "tp_mixer.npz")))
+    pls = np.concatenate([g[f"ws{ws}/r{r}/int8/payload1"] for r in range(ws)])
+    ref = g[f"ws{ws}/r0/int8/out"]
+    rows, cols = ref.shape[0] * ref.shape[1], ref.shape[2]
+    out = torch.empty(rows, cols, device=dev(), dtype=torch.float32)
+    L.call("mtp_dequant_sum", L.ptr(torch.as_tensor(pls).to(dev())), ws, rows, cols, L.ptr(out), L.stream_ptr())
+    assert out.cpu().numpy().tobytes() == ref.reshape(rows, cols).astype(np.float32).tobytes()
+
+
+@pytest.mark.parametrize("mode,name", [(L.RED_FP32, "fp32"), (L.RED_FP16, "fp16"), (L.RED_INT8TOK, "int8")])
+@pytest.mark.parametrize("rows,cols", [(1, 160), (37, 80), (5000, 2048), (9, 18)])
+def test_allreduce_world_size_one_round_trip(mode, name, rows, cols):
+    """At world size 1 the reference still round-trips through the wire format."""
+    x = _rand((rows, cols), 31, 3.0)
+    ref = O.REDUCE_FNS[name]([x])
+    out = torch.empty(rows, cols, device=dev(), dtype=torch.float32)
+    L.call("mtp_allreduce", None, 1, mode, L.ptr(t(x)), L.ptr(out), rows, cols, L.stream_ptr())
+    assert n(out).tobytes() == ref.astype(np.float32).tobytes()
+
+
+def test_reduce_outproj_epilogue_matches_oracle():
+    rows, d = 77, 768
+    part = _rand((rows, d), 41)
+    resid = _rand((rows, d), 42)
+    w = _rand((d,), 43) + 1
+    eps = 1e-5
+    res_ref = (resid + part).astype(np.float32)
+    norm_ref = O.rmsnorm(res_ref, w, eps)
+    r_t = t(resid)
+    normed = torch.empty(rows, d, device=dev(), dtype=torch.float32)
+    L.call("mtp_reduce_outproj", None, L.RED_FP32, L.ptr(t(part)), rows, d, None, L.ptr(r_t), L.ptr(t(w)),
+           float(eps), L.ptr(normed), L.F32, L.stream_ptr())
+    np.testing.assert_allclose(n(r_t), res_ref, atol=0, rtol=0)
+    np.testing.assert_allclose(n(normed), norm_ref, atol=1e-5, rtol=1e-5)
+
+
+def test_reduce_xproj_split():
+    rows, R, N2 = 50, 48, 32
+    part = _rand((rows, R + N2), 51)
+    dl = torch.empty(rows, R, device=dev(), dtype=BF)
+    bc = torch.empty(rows, N2, device=dev(), dtype=torch.float32)
+    L.call("mtp_reduce_xproj", None, L.RED_FP32, L.ptr(t(part)), rows, R, N2, L.ptr(dl), L.BF16, L.ptr(bc),
+           L.stream_ptr())
+    np.testing.assert_array_equal(n(dl), O.bf16_round(part[:, :R]))
+    np.testing.assert_array_equal(n(bc), part[:, R:])
+
+
+def test_embedding_rmsnorm_argmax():
+    V, D = 1000, 256
+    table = torch.randn(V, D, device=dev(), dtype=BF)
+    ids = torch.randint(0, V, (37,), device=dev())
+    out = torch.empty(37, D, device=dev(), dtype=torch.float32)
+    L.call("mtp_embedding", L.ptr(ids), 37, L.ptr(table), D, L.BF16, L.ptr(out), L.stream_ptr())
+    assert torch.equal(out, table[ids].float())
+    w = torch.randn(D, device=dev())
+    nrm = torch.empty(37, D, device=dev(), dtype=torch.float32)
+    L.call("mtp_rmsnorm", L.ptr(out), 37, D, L.ptr(w), L.F32, 1e-5, L.ptr(nrm), L.F32, L.stream_ptr())
+    np.testing.assert_allclose(n(nrm), O.rmsnorm(n(out), n(w), 1e-5), atol=1e-5, rtol=1e-5)
+    logits = torch.randn(5, 50280, device=dev())
+    logits[2, 77] = logits[2, 9000] = 100.0  # tie: first index wins, as torch.argmax
+    am = torch.empty(5, device=dev(), dtype=torch.int64)
+    L.call("mtp_argmax_rows", L.ptr(logits), 5, 50280, 50280, L.F32, L.ptr(am), L.stream_ptr())
+    assert torch.equal(am, logits.argmax(-1))
