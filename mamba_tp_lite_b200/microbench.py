@@ -1,0 +1,212 @@
+"""Single-kernel microbenchmarks (one process per GPU), used for rooflines and
+for ncu captures of one kernel on a bounded case.
+
+    python -m mamba_tp_lite_b200.microbench gemm --m 32768 --n 8192 --k 2048
+    python -m mamba_tp_lite_b200.microbench scan --batch 32 --seqlen 1024 --channels 4096
+    python -m mamba_tp_lite_b200.microbench step --batch 32 --channels 4096 --rank 128
+    torchrun --nproc-per-node N -m mamba_tp_lite_b200.microbench allreduce --rows 32768 --cols 2048 --mode int8
+
+Each prints one JSON line: average kernel time from CUDA events over --iters
+launches after --warmup launches, and the achieved rate against the measured
+peak (TFLOP/s for GEMMs, GB/s for the memory-bound kernels, NVLink GB/s per
+direction for the reductions).
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+
+import torch
+
+from . import _lib as L
+
+_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks():
+    p = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return _PEAKS
+
+
+def _time(fn, warmup, iters):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def bench_gemm(a):
+    M, N, K = a.m, a.n, a.k
+    A = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    W = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    odt = torch.bfloat16 if a.out == "bf16" else torch.float32
+    C = torch.empty(M, N, device="cuda", dtype=odt)
+    algo = {"tc": L.GEMM_TCGEN05, "simt": L.GEMM_SIMT, "gemv": L.GEMM_GEMV, "auto": L.GEMM_AUTO}[a.algo]
+
+    def run():
+        L.call("mtp_gemm_ex", L.ptr(A), L.ptr(W), L.ptr(C), M, N, K, K, K, N, L.BF16, L.dtype_code(odt), L.EPI_STORE,
+               None, 0, algo, L.stream_ptr())
+
+    ms = _time(run, a.warmup, a.iters)
+    tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
+    out = {"kernel": f"gemm_{a.algo}", "M": M, "N": N, "K": K, "avg_ms": ms, "TFLOPs": tf,
+           "frac_of_burst_peak": tf / peaks()["bf16_tflops"]}
+    if a.check:
+        ref = A.float() @ W.float().T
+        out["max_rel_err"] = ((C.float() - ref).abs().max() / ref.abs().max()).item()
+    return out
+
+
+def bench_scan(a):
+    B, Lq, es, n = a.batch, a.seqlen, a.channels, 16
+    T = B * Lq
+    dt_ = torch.bfloat16
+    xz = torch.randn(T, 2 * es, device="cuda", dtype=dt_)
+    dt = torch.rand(T, es, device="cuda") * 0.1
+    bc = torch.randn(T, 2 * n, device="cuda")
+    A_log = torch.log(torch.arange(1, n + 1, device="cuda", dtype=torch.float32)).repeat(es, 1).to(dt_)
+    Dp = torch.ones(es, device="cuda", dtype=dt_)
+    cw = torch.randn(es, 4, device="cuda", dtype=dt_) * 0.5
+    cb = torch.randn(es, device="cuda", dtype=dt_) * 0.5
+    y = torch.empty(T, es, device="cuda", dtype=dt_)
+    cf = torch.empty(B, es, 3, device="cuda", dtype=dt_)
+    sf = torch.empty(B, es, n, device="cuda")
+
+    def run():
+        L.call("mtp_scan_prefill", L.ptr(xz), 2 * es, L.ptr(dt), es, L.ptr(bc), 2 * n, L.ptr(A_log), L.ptr(Dp),
+               L.ptr(cw), L.ptr(cb), None, None, L.ptr(y), es, L.ptr(cf), L.ptr(sf), B, Lq, es, n, 4, L.BF16,
+               L.stream_ptr())
+
+    ms = _time(run, a.warmup, a.iters)
+    nbytes = T * (es * (3 * 2 + 4) + 2 * n * 4) + B * es * (n * 4 + 3 * 2)
+    gbs = nbytes / (ms / 1e3) / 1e9
+    exps = T * es * n
+    return {"kernel": "scan_prefill", "B": B, "L": Lq, "Es": es, "avg_ms": ms, "GBps": gbs,
+            "frac_of_hbm": gbs / peaks()["hbm_gbs"], "algorithmic_bytes": nbytes, "Gexp_per_s": exps / (ms / 1e3) / 1e9}
+
+
+def bench_step(a):
+    B, es, n, R = a.batch, a.channels, 16, a.rank
+    dt_ = torch.bfloat16
+    xz = torch.randn(B, 2 * es, device="cuda", dtype=dt_)
+    dl = torch.randn(B, R, device="cuda", dtype=dt_)
+    W = torch.randn(es, R, device="cuda", dtype=dt_) * 0.05
+    bdt = torch.randn(es, device="cuda", dtype=dt_) - 3
+    bc = torch.randn(B, 2 * n, device="cuda")
+    A_log = torch.log(torch.arange(1, n + 1, device="cuda", dtype=torch.float32)).repeat(es, 1).to(dt_)
+    Dp = torch.ones(es, device="cuda", dtype=dt_)
+    cw = torch.randn(es, 4, device="cuda", dtype=dt_) * 0.5
+    cb = torch.randn(es, device="cuda", dtype=dt_) * 0.5
+    cs = torch.zeros(B, es, 3, device="cuda", dtype=dt_)
+    ss = torch.zeros(B, es, n, device="cuda")
+    y = torch.empty(B, es, device="cuda", dtype=dt_)
+
+    def run():
+        L.call("mtp_step", L.ptr(xz), 2 * es, L.ptr(dl), R, L.ptr(W), L.ptr(bdt), L.ptr(bc), 2 * n, L.ptr(A_log),
+               L.ptr(Dp), L.ptr(cw), L.ptr(cb), L.ptr(cs), L.ptr(ss), L.ptr(y), es, B, es, n, R, 4, L.BF16,
+               L.stream_ptr())
+
+    ms = _time(run, a.warmup, a.iters)
+    nbytes = B * es * (2 * n * 4 + 2 * 3 * 2 + 3 * 2) + es * (R * 2 + n * 2 + 4 * 2 + 3 * 2) + B * (R * 2 + 2 * n * 4)
+    gbs = nbytes / (ms / 1e3) / 1e9
+    return {"kernel": "step", "B": B, "Es": es, "R": R, "avg_ms": ms, "GBps": gbs,
+            "frac_of_hbm": gbs / peaks()["hbm_gbs"], "algorithmic_bytes": nbytes}
+
+
+def bench_allreduce(a):
+    import torch.distributed as dist
+
+    from .tp_utils import Comm
+
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if ws > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    rows, cols = a.rows, a.cols
+    g = torch.Generator(device="cuda").manual_seed(rank * 1000 + rows)
+    x = torch.randn(rows, cols, device="cuda", generator=g)
+    x[:, torch.randperm(cols, device="cuda", generator=g)[: max(1, cols // 100)]] *= 20
+    out = torch.empty_like(x)
+    comm = Comm(None, rank, ws, cols, cols, max_rows=max(rows, 1)) if ws > 1 else None
+    mode = {"fp32": L.RED_FP32, "fp16": L.RED_FP16, "int8": L.RED_INT8TOK}[a.mode]
+
+    def run():
+        L.call("mtp_allreduce", None if comm is None else comm.ptr, 1, mode, L.ptr(x), L.ptr(out), rows, cols,
+               L.stream_ptr())
+
+    if ws > 1:
+        dist.barrier()
+    ms = _time(run, a.warmup, a.iters)
+    if ws > 1:
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    esz = {"fp32": 4, "fp16": 2, "int8": 1}[a.mode]
+    per_row = cols * esz + (4 if a.mode == "int8" else 0)
+    two_shot = ws > 2 and rows * cols * 4 >= (1 << 20)
+    # bytes each rank sends over NVLink per call
+    if ws == 1:
+        sent = 0
+    elif two_shot:
+        sent = rows * per_row * (ws - 1) / ws + rows * cols * 4 * (ws - 1) / ws
+    else:
+        sent = rows * per_row * (ws - 1)
+    res = {"kernel": f"allreduce_{a.mode}", "ws": ws, "rows": rows, "cols": cols, "avg_us": ms * 1e3,
+           "protocol": "two-shot" if two_shot else "one-shot", "nvlink_bytes_sent_per_rank": sent,
+           "nvlink_GBps_per_direction": sent / (ms / 1e3) / 1e9 if sent else 0.0,
+           "frac_of_770": (sent / (ms / 1e3) / 1e9) / 770.0 if sent else 0.0}
+    if comm is not None:
+        comm.check()
+        comm.destroy()
+        dist.barrier()
+        dist.destroy_process_group()
+    return res if rank == 0 else None
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    sub = ap.add_subparsers(dest="what", required=True)
+    g = sub.add_parser("gemm")
+    g.add_argument("--m", type=int, default=32768)
+    g.add_argument("--n", type=int, default=8192)
+    g.add_argument("--k", type=int, default=2048)
+    g.add_argument("--out", choices=["bf16", "f32"], default="bf16")
+    g.add_argument("--algo", choices=["tc", "simt", "gemv", "auto"], default="tc")
+    g.add_argument("--check", action="store_true")
+    s = sub.add_parser("scan")
+    s.add_argument("--batch", type=int, default=32)
+    s.add_argument("--seqlen", type=int, default=1024)
+    s.add_argument("--channels", type=int, default=4096)
+    st = sub.add_parser("step")
+    st.add_argument("--batch", type=int, default=32)
+    st.add_argument("--channels", type=int, default=4096)
+    st.add_argument("--rank", type=int, default=128)
+    r = sub.add_parser("allreduce")
+    r.add_argument("--rows", type=int, default=32768)
+    r.add_argument("--cols", type=int, default=2048)
+    r.add_argument("--mode", choices=["fp32", "fp16", "int8"], default="int8")
+    for p in (g, s, st, r):
+        p.add_argument("--warmup", type=int, default=3)
+        p.add_argument("--iters", type=int, default=10)
+    a = ap.parse_args()
+    L.load()
+    res = {"gemm": bench_gemm, "scan": bench_scan, "step": bench_step, "allreduce": bench_allreduce}[a.what](a)
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -104,11 +104,12 @@ def test_scan_prefill_matches_oracle(dtype, b, l, es, nst, init):
     y = torch.empty(T, es, device=dev(), dtype=dtype)
     cf = torch.empty(b, es, 3, device=dev(), dtype=dtype)
     sf = torch.empty(b, es, nst, device=dev(), dtype=torch.float32)
-    g = lambda a: None if a is None else t(a, dtype)
-    L.call("mtp_scan_prefill", L.ptr(xz), 2 * es, L.ptr(dtt), es, L.ptr(bc), 2 * nst, L.ptr(t(A_log, dtype)),
-           L.ptr(t(Dp, dtype)), L.ptr(t(cw, dtype)), L.ptr(t(cb, dtype)), L.ptr(g(ci)),
-           L.ptr(None if si is None else t(si)), L.ptr(y), es, L.ptr(cf), L.ptr(sf), b, l, es, nst, 4,
-           L.dtype_code(dtype), L.stream_ptr())
+    # keep every argument tensor alive until the kernel has run
+    args = [t(A_log, dtype), t(Dp, dtype), t(cw, dtype), t(cb, dtype), None if ci is None else t(ci, dtype),
+            None if si is None else t(si)]
+    L.call("mtp_scan_prefill", L.ptr(xz), 2 * es, L.ptr(dtt), es, L.ptr(bc), 2 * nst, *[L.ptr(a) for a in args],
+           L.ptr(y), es, L.ptr(cf), L.ptr(sf), b, l, es, nst, 4, L.dtype_code(dtype), L.stream_ptr())
+    torch.cuda.synchronize()
     tol = 2e-4 if dtype == torch.float32 else 2e-2
     np.testing.assert_allclose(n(y).reshape(b, l, es), y_ref, atol=tol, rtol=tol)
     np.testing.assert_allclose(n(cf), cf_ref, atol=1e-6, rtol=0)
@@ -123,8 +124,10 @@ def test_conv1d_silu_matches_oracle(dtype):
     T = b * l
     xz = t(np.concatenate([x, z], -1).reshape(T, 2 * es), dtype)
     xc = torch.empty(T, es, device=dev(), dtype=dtype)
-    L.call("mtp_conv1d_silu", L.ptr(xz), 2 * es, L.ptr(t(cw, dtype)), L.ptr(t(cb, dtype)), L.ptr(t(ci, dtype)),
-           L.ptr(xc), es, b, l, es, 4, L.dtype_code(dtype), L.stream_ptr())
+    args = [t(cw, dtype), t(cb, dtype), t(ci, dtype)]
+    L.call("mtp_conv1d_silu", L.ptr(xz), 2 * es, *[L.ptr(a) for a in args], L.ptr(xc), es, b, l, es, 4,
+           L.dtype_code(dtype), L.stream_ptr())
+    torch.cuda.synchronize()
     tol = 1e-5 if dtype == torch.float32 else 1e-2
     np.testing.assert_allclose(n(xc).reshape(b, l, es), xc_ref, atol=tol, rtol=tol)
 
@@ -143,10 +146,13 @@ def test_step_matches_oracle(dtype, b, es, nst, R):
     cs = t(ci, dtype)
     ss = t(si)
     y = torch.empty(b, es, device=dev(), dtype=dtype)
-    L.call("mtp_step", L.ptr(xz), 2 * es, L.ptr(t(dl, dtype)), R, L.ptr(t(W, dtype)), L.ptr(t(bd, dtype)),
-           L.ptr(t(np.concatenate([Bm, Cm], -1))), 2 * nst, L.ptr(t(A_log, dtype)), L.ptr(t(Dp, dtype)),
-           L.ptr(t(cw, dtype)), L.ptr(t(cb, dtype)), L.ptr(cs), L.ptr(ss), L.ptr(y), es, b, es, nst, R, 4,
-           L.dtype_code(dtype), L.stream_ptr())
+    dl_t, w_t, bd_t = t(dl, dtype), t(W, dtype), t(bd, dtype)
+    bc_t = t(np.concatenate([Bm, Cm], -1))
+    rest = [t(A_log, dtype), t(Dp, dtype), t(cw, dtype), t(cb, dtype)]
+    L.call("mtp_step", L.ptr(xz), 2 * es, L.ptr(dl_t), R, L.ptr(w_t), L.ptr(bd_t), L.ptr(bc_t), 2 * nst,
+           *[L.ptr(a) for a in rest], L.ptr(cs), L.ptr(ss), L.ptr(y), es, b, es, nst, R, 4, L.dtype_code(dtype),
+           L.stream_ptr())
+    torch.cuda.synchronize()
     tol = 2e-5 if dtype == torch.float32 else 2e-2
     np.testing.assert_allclose(n(y), y_ref, atol=tol, rtol=tol)
     np.testing.assert_allclose(n(cs), cs_ref, atol=0, rtol=0)
@@ -161,7 +167,8 @@ def test_quantiser_bit_exact_vs_reference_golden(golden_dir):
         rows, cols = x.shape
         sc = torch.empty(rows, device=dev(), dtype=torch.float32)
         q = torch.empty(rows, cols, device=dev(), dtype=torch.int8)
-        L.call("mtp_quantize_rows_int8", L.ptr(t(x)), rows, cols, cols, L.ptr(sc), L.ptr(q), L.stream_ptr())
+        xt = t(x)
+        L.call("mtp_quantize_rows_int8", L.ptr(xt), rows, cols, cols, L.ptr(sc), L.ptr(q), L.stream_ptr())
         assert sc.cpu().numpy().tobytes() == g[f"{name}/scales"].tobytes(), name
         assert q.cpu().numpy().tobytes() == g[f"{name}/q"].tobytes(), name
 
@@ -172,7 +179,8 @@ def test_quantiser_bit_exact_vs_oracle_large():
     s_ref, q_ref = O.quantize_rows_int8(x)
     sc = torch.empty(4096, device=dev(), dtype=torch.float32)
     q = torch.empty(4096, 2048, device=dev(), dtype=torch.int8)
-    L.call("mtp_quantize_rows_int8", L.ptr(t(x)), 4096, 2048, 2048, L.ptr(sc), L.ptr(q), L.stream_ptr())
+    xt = t(x)
+    L.call("mtp_quantize_rows_int8", L.ptr(xt), 4096, 2048, 2048, L.ptr(sc), L.ptr(q), L.stream_ptr())
     assert sc.cpu().numpy().tobytes() == s_ref.tobytes()
     assert q.cpu().numpy().tobytes() == q_ref.tobytes()
 
@@ -184,7 +192,8 @@ def test_dequant_sum_bit_exact_on_reference_payloads(golden_dir, ws):
     ref = g[f"ws{ws}/r0/int8/out"]
     rows, cols = ref.shape[0] * ref.shape[1], ref.shape[2]
     out = torch.empty(rows, cols, device=dev(), dtype=torch.float32)
-    L.call("mtp_dequant_sum", L.ptr(torch.as_tensor(pls).to(dev())), ws, rows, cols, L.ptr(out), L.stream_ptr())
+    pl_t = torch.as_tensor(pls).to(dev())
+    L.call("mtp_dequant_sum", L.ptr(pl_t), ws, rows, cols, L.ptr(out), L.stream_ptr())
     assert out.cpu().numpy().tobytes() == ref.reshape(rows, cols).astype(np.float32).tobytes()
 
 
@@ -195,7 +204,8 @@ def test_allreduce_world_size_one_round_trip(mode, name, rows, cols):
     x = _rand((rows, cols), 31, 3.0)
     ref = O.REDUCE_FNS[name]([x])
     out = torch.empty(rows, cols, device=dev(), dtype=torch.float32)
-    L.call("mtp_allreduce", None, 1, mode, L.ptr(t(x)), L.ptr(out), rows, cols, L.stream_ptr())
+    xt = t(x)
+    L.call("mtp_allreduce", None, 1, mode, L.ptr(xt), L.ptr(out), rows, cols, L.stream_ptr())
     assert n(out).tobytes() == ref.astype(np.float32).tobytes()
 
 
@@ -209,7 +219,8 @@ def test_reduce_outproj_epilogue_matches_oracle():
     norm_ref = O.rmsnorm(res_ref, w, eps)
     r_t = t(resid)
     normed = torch.empty(rows, d, device=dev(), dtype=torch.float32)
-    L.call("mtp_reduce_outproj", None, L.RED_FP32, L.ptr(t(part)), rows, d, None, L.ptr(r_t), L.ptr(t(w)),
+    p_t, w_t = t(part), t(w)
+    L.call("mtp_reduce_outproj", None, L.RED_FP32, L.ptr(p_t), rows, d, None, L.ptr(r_t), L.ptr(w_t),
            float(eps), L.ptr(normed), L.F32, L.stream_ptr())
     np.testing.assert_allclose(n(r_t), res_ref, atol=0, rtol=0)
     np.testing.assert_allclose(n(normed), norm_ref, atol=1e-5, rtol=1e-5)
@@ -220,7 +231,8 @@ def test_reduce_xproj_split():
     part = _rand((rows, R + N2), 51)
     dl = torch.empty(rows, R, device=dev(), dtype=BF)
     bc = torch.empty(rows, N2, device=dev(), dtype=torch.float32)
-    L.call("mtp_reduce_xproj", None, L.RED_FP32, L.ptr(t(part)), rows, R, N2, L.ptr(dl), L.BF16, L.ptr(bc),
+    p_t = t(part)
+    L.call("mtp_reduce_xproj", None, L.RED_FP32, L.ptr(p_t), rows, R, N2, L.ptr(dl), L.BF16, L.ptr(bc),
            L.stream_ptr())
     np.testing.assert_array_equal(n(dl), O.bf16_round(part[:, :R]))
     np.testing.assert_array_equal(n(bc), part[:, R:])
