@@ -367,6 +367,251 @@ __global__ void __launch_bounds__(WPB * 32) reduce_kernel(CommDev d, bool has_co
   finish();
 }
 
+// ----------------------------------------------------------------- register-row reduction
+// One warp per row; the row lives in registers as VPL float4 chunks per lane
+// (columns 4*(i*32+lane) .. +3 of chunk i), so the quantiser, the wire writes,
+// the rank-ordered reduce and the epilogue each touch memory once, with 16-byte
+// (fp32), 8-byte (fp16) or 4-byte (int8) vector accesses.  Needs cols % 4 == 0
+// and cols <= 128 * VPL.
+template <int VPL> struct RowV { float4 v[VPL]; };
+
+template <bool CG, int VPL>
+__device__ __forceinline__ void load_rowv(const float *row, int cols, int lane, RowV<VPL> &R) {
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = (i * 32 + lane) * 4;
+    if (c < cols) R.v[i] = CG ? __ldcg(reinterpret_cast<const float4 *>(row + c)) : *reinterpret_cast<const float4 *>(row + c);
+    else R.v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+template <int VPL>
+__device__ __forceinline__ float rowv_amax(const RowV<VPL> &R) {
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) m = fmaxf(fmaxf(fmaxf(m, fabsf(R.v[i].x)), fmaxf(fabsf(R.v[i].y), fabsf(R.v[i].z))), fabsf(R.v[i].w));
+  return warp_max(m);
+}
+
+__device__ __forceinline__ float dq1(float x, float s) { return __fadd_rn(0.f, __fmul_rn((float)quant1(x, s), s)); }
+__device__ __forceinline__ float h1(float x) { return __half2float(__float2half_rn(x)); }
+
+// world size 1: the wire format's round trip alone, in registers
+template <int MODE, int VPL>
+__device__ __forceinline__ void roundtrip_v(RowV<VPL> &R) {
+  if (MODE == MTP_RED_FP16) {
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) R.v[i] = make_float4(h1(R.v[i].x), h1(R.v[i].y), h1(R.v[i].z), h1(R.v[i].w));
+  } else if (MODE == MTP_RED_INT8TOK) {
+    const float s = row_scale(rowv_amax(R));
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) R.v[i] = make_float4(dq1(R.v[i].x, s), dq1(R.v[i].y, s), dq1(R.v[i].z, s), dq1(R.v[i].w, s));
+  }
+}
+
+template <int MODE, int VPL>
+__device__ __forceinline__ void write_wire_v(char *dst, const RowV<VPL> &R, int r, int rows, int cols, int lane, float scale) {
+  if (MODE == MTP_RED_INT8TOK && lane == 0) reinterpret_cast<float *>(dst)[r] = scale;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = (i * 32 + lane) * 4;
+    if (c >= cols) break;
+    const float4 v = R.v[i];
+    if (MODE == MTP_RED_FP32) {
+      *reinterpret_cast<float4 *>(reinterpret_cast<float *>(dst) + (size_t)r * cols + c) = v;
+    } else if (MODE == MTP_RED_FP16) {
+      __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+      uint2 u;
+      u.x = *reinterpret_cast<uint32_t *>(&a);
+      u.y = *reinterpret_cast<uint32_t *>(&b);
+      *reinterpret_cast<uint2 *>(reinterpret_cast<__half *>(dst) + (size_t)r * cols + c) = u;
+    } else {
+      *reinterpret_cast<uint32_t *>(dst + (size_t)4 * rows + (size_t)r * cols + c) =
+          pack4(quant1(v.x, scale), quant1(v.y, scale), quant1(v.z, scale), quant1(v.w, scale));
+    }
+  }
+}
+
+// rank-ordered reduction of row r over the slots, into registers
+template <int MODE, int VPL>
+__device__ __forceinline__ void reduce_v(char *const *slots, int nsrc, int r, int rows, int cols, int lane, RowV<VPL> &R) {
+  float s[MAX_WS];
+  if (MODE == MTP_RED_INT8TOK)
+    for (int k = 0; k < nsrc; ++k) s[k] = __ldcg(reinterpret_cast<const float *>(slots[k]) + r);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = (i * 32 + lane) * 4;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (c < cols) {
+      for (int k = 0; k < nsrc; ++k) {
+        float4 v;
+        if (MODE == MTP_RED_FP32) {
+          v = __ldcg(reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(slots[k]) + (size_t)r * cols + c));
+        } else if (MODE == MTP_RED_FP16) {
+          const uint2 u = __ldcg(reinterpret_cast<const uint2 *>(reinterpret_cast<const __half *>(slots[k]) + (size_t)r * cols + c));
+          const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+          const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+          v = make_float4(lo.x, lo.y, hi.x, hi.y);
+        } else {
+          const uint32_t w = __ldcg(reinterpret_cast<const unsigned int *>(slots[k] + (size_t)4 * rows + (size_t)r * cols + c));
+          v = make_float4(__fmul_rn(unpack_i8(w, 0), s[k]), __fmul_rn(unpack_i8(w, 1), s[k]),
+                          __fmul_rn(unpack_i8(w, 2), s[k]), __fmul_rn(unpack_i8(w, 3), s[k]));
+        }
+        a.x = __fadd_rn(a.x, v.x); a.y = __fadd_rn(a.y, v.y); a.z = __fadd_rn(a.z, v.z); a.w = __fadd_rn(a.w, v.w);
+      }
+      if (MODE == MTP_RED_FP16) a = make_float4(h1(a.x), h1(a.y), h1(a.z), h1(a.w));
+    }
+    R.v[i] = a;
+  }
+}
+
+template <int EPI, int VPL>
+__device__ __forceinline__ void epilogue_v(const EpiOut &e, RowV<VPL> &R, int r, int cols, int lane) {
+  if (EPI == EPI_PLAIN) {
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int c = (i * 32 + lane) * 4;
+      if (c < cols) *reinterpret_cast<float4 *>(e.out + (size_t)r * cols + c) = R.v[i];
+    }
+  } else if (EPI == EPI_XPROJ) {
+    const int n2 = cols - e.R;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int c = (i * 32 + lane) * 4;
+      if (c >= cols) break;
+      const float v[4] = {R.v[i].x, R.v[i].y, R.v[i].z, R.v[i].w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int cc = c + q;
+        if (cc < e.R) st_any(e.dt_low, e.dt_dtype, (size_t)r * e.R + cc, v[q]);
+        else e.bc[(size_t)r * n2 + (cc - e.R)] = v[q];
+      }
+    }
+  } else {
+    float ss = 0.f;
+    float *res = e.resid + (size_t)r * cols;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int c = (i * 32 + lane) * 4;
+      if (c >= cols) break;
+      float4 v = R.v[i];
+      if (e.bias) {
+        v.x += ld_any(e.bias, e.out_dtype, c); v.y += ld_any(e.bias, e.out_dtype, c + 1);
+        v.z += ld_any(e.bias, e.out_dtype, c + 2); v.w += ld_any(e.bias, e.out_dtype, c + 3);
+      }
+      const float4 h0 = *reinterpret_cast<const float4 *>(res + c);
+      const float4 h = make_float4(h0.x + v.x, h0.y + v.y, h0.z + v.z, h0.w + v.w);
+      *reinterpret_cast<float4 *>(res + c) = h;
+      ss += h.x * h.x + h.y * h.y + h.z * h.z + h.w * h.w;
+      R.v[i] = h;
+    }
+    if (e.normed) {
+      const float rs = rsqrtf(warp_sum(ss) / (float)cols + e.eps);
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) {
+        const int c = (i * 32 + lane) * 4;
+        if (c >= cols) break;
+        const float4 h = R.v[i];
+        float o[4] = {h.x * rs, h.y * rs, h.z * rs, h.w * rs};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) o[q] = ld_any(e.norm_w, e.out_dtype, c + q) * o[q];
+        if (e.out_dtype == MTP_F32) {
+          *reinterpret_cast<float4 *>(reinterpret_cast<float *>(e.normed) + (size_t)r * cols + c) = make_float4(o[0], o[1], o[2], o[3]);
+        } else {
+          __nv_bfloat162 a = __floats2bfloat162_rn(o[0], o[1]), b = __floats2bfloat162_rn(o[2], o[3]);
+          uint2 u;
+          u.x = *reinterpret_cast<uint32_t *>(&a);
+          u.y = *reinterpret_cast<uint32_t *>(&b);
+          *reinterpret_cast<uint2 *>(reinterpret_cast<__nv_bfloat16 *>(e.normed) + (size_t)r * cols + c) = u;
+        }
+      }
+    }
+  }
+}
+
+template <int MODE, int EPI, int VPL>
+__global__ void __launch_bounds__(WPB * 32) reduce_rows_kernel(CommDev d, bool has_comm, int site,
+                                                               const float *__restrict__ partial, int rows, int cols,
+                                                               bool two_shot, EpiOut e) {
+  __shared__ int abort_sm;
+  __shared__ uint32_t epoch_sm;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int j = blockIdx.x, G = gridDim.x;
+  RowV<VPL> R;
+  if (!has_comm) {
+    for (int r = j * WPB + warp; r < rows; r += G * WPB) {
+      load_rowv<false>(partial + (size_t)r * cols, cols, lane, R);
+      roundtrip_v<MODE>(R);
+      epilogue_v<EPI>(e, R, r, cols, lane);
+    }
+    return;
+  }
+  uint32_t *ep = reinterpret_cast<uint32_t *>(d.peer[d.rank] + d.off_epoch) + site;
+  if (threadIdx.x == 0) {
+    abort_sm = 0;
+    epoch_sm = *reinterpret_cast<volatile uint32_t *>(ep) + 1u;
+  }
+  __syncthreads();
+  const uint32_t epoch = epoch_sm;
+  auto finish = [&]() {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      unsigned int *done = reinterpret_cast<unsigned int *>(d.peer[d.rank] + d.off_done) + site;
+      if (atomicAdd(done, 1u) == (unsigned)G - 1u) {
+        *done = 0u;
+        *reinterpret_cast<volatile uint32_t *>(ep) = epoch;
+        __threadfence();
+      }
+    }
+  };
+  const size_t half = (size_t)(epoch & 1u) * d.ws * d.slot_bytes[site];
+  const uint32_t all = (1u << d.ws) - 1u;
+  const int chunk = (rows + d.ws - 1) / d.ws;
+  for (int r = j * WPB + warp; r < rows; r += G * WPB) {
+    load_rowv<false>(partial + (size_t)r * cols, cols, lane, R);
+    const float sc = MODE == MTP_RED_INT8TOK ? row_scale(rowv_amax(R)) : 0.f;
+    const size_t my_slot = d.off_recv[site] + half + (size_t)d.rank * d.slot_bytes[site];
+    if (two_shot) {
+      write_wire_v<MODE>(d.peer[r / chunk] + my_slot, R, r, rows, cols, lane, sc);
+    } else {
+      for (int k = 0; k < d.ws; ++k) write_wire_v<MODE>(d.peer[(d.rank + k) % d.ws] + my_slot, R, r, rows, cols, lane, sc);
+    }
+  }
+  signal(d, site, 0, epoch, all);
+  if (!wait_all(d, site, 0, epoch, all, &abort_sm)) { finish(); return; }
+  char *slots[MAX_WS];
+  for (int k = 0; k < d.ws; ++k) slots[k] = d.peer[d.rank] + d.off_recv[site] + half + (size_t)k * d.slot_bytes[site];
+  if (!two_shot) {
+    for (int r = j * WPB + warp; r < rows; r += G * WPB) {
+      reduce_v<MODE>(slots, d.ws, r, rows, cols, lane, R);
+      epilogue_v<EPI>(e, R, r, cols, lane);
+    }
+    finish();
+    return;
+  }
+  for (int r = j * WPB + warp; r < rows; r += G * WPB) {
+    if (r / chunk != d.rank) continue;
+    reduce_v<MODE>(slots, d.ws, r, rows, cols, lane, R);
+    for (int k = 0; k < d.ws; ++k) {
+      float *o = reinterpret_cast<float *>(d.peer[(d.rank + k) % d.ws] + d.off_gath[site]) + (size_t)r * cols;
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) {
+        const int c = (i * 32 + lane) * 4;
+        if (c < cols) *reinterpret_cast<float4 *>(o + c) = R.v[i];
+      }
+    }
+  }
+  signal(d, site, 1, epoch, all);
+  if (!wait_all(d, site, 1, epoch, all, &abort_sm)) { finish(); return; }
+  const float *gath_local = reinterpret_cast<const float *>(d.peer[d.rank] + d.off_gath[site]);
+  for (int r = j * WPB + warp; r < rows; r += G * WPB) {
+    load_rowv<true>(gath_local + (size_t)r * cols, cols, lane, R);
+    epilogue_v<EPI>(e, R, r, cols, lane);
+  }
+  finish();
+}
+
 // ----------------------------------------------------------------- standalone quantiser / dequant
 __global__ void quantize_rows_kernel(const float *__restrict__ in, int rows, int cols, int ld, float *scales, int8_t *q) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
@@ -429,8 +674,11 @@ static int run_reduce(mtp_comm *c, int site, int mode, const float *partial, int
     int G = ceil_div(nr, WPB);
     if (G > sms) G = sms;
     if (G > G_MAX) G = G_MAX;
-    float *scr = row_scratch((size_t)G * WPB * cols * sizeof(float));
-    if (!scr) return fail(MTP_ERR_CUDA, "could not allocate reduction scratch");
+    float *scr = nullptr;
+    if (cols % 4 != 0 || cols > 3072) {
+      scr = row_scratch((size_t)G * WPB * cols * sizeof(float));
+      if (!scr) return fail(MTP_ERR_CUDA, "could not allocate reduction scratch");
+    }
     EpiOut ee = e;
     // advance outputs by r0 rows
     if (EPI == EPI_PLAIN) ee.out = e.out + (size_t)r0 * cols;
@@ -447,12 +695,36 @@ static int run_reduce(mtp_comm *c, int site, int mode, const float *partial, int
     const size_t wire_bytes = (size_t)nr * cols * 4;
     const bool two_shot = has_comm && c->d.ws > 2 && wire_bytes >= ((size_t)1 << 20);
     const float *pp = partial + (size_t)r0 * cols;
+    // register-row kernel when the width allows it
+    const int vpl = (cols % 4 != 0) ? 0 : cols <= 256 ? 2 : cols <= 512 ? 4 : cols <= 1024 ? 8 : cols <= 2048 ? 16 : cols <= 3072 ? 24 : 0;
+    if (vpl) {
+      int Gv = ceil_div(nr, WPB);
+      const int cap = has_comm ? (sms < G_MAX ? sms : G_MAX) : sms * 8;
+      if (Gv > cap) Gv = cap;
+#define MTP_RV(M, V) reduce_rows_kernel<M, EPI, V><<<Gv, WPB * 32, 0, s>>>(d, has_comm, site, pp, nr, cols, two_shot, ee)
+#define MTP_RV_MODE(V)                                      \
+  do {                                                      \
+    if (mode == MTP_RED_FP32) MTP_RV(MTP_RED_FP32, V);      \
+    else if (mode == MTP_RED_FP16) MTP_RV(MTP_RED_FP16, V); \
+    else MTP_RV(MTP_RED_INT8TOK, V);                        \
+  } while (0)
+      switch (vpl) {
+        case 2: MTP_RV_MODE(2); break;
+        case 4: MTP_RV_MODE(4); break;
+        case 8: MTP_RV_MODE(8); break;
+        case 16: MTP_RV_MODE(16); break;
+        default: MTP_RV_MODE(24); break;
+      }
+#undef MTP_RV_MODE
+#undef MTP_RV
+    } else {
 #define MTP_RED_LAUNCH(M) \
   reduce_kernel<M, EPI><<<G, WPB * 32, 0, s>>>(d, has_comm, site, pp, nr, cols, two_shot, scr, ee)
-    if (mode == MTP_RED_FP32) MTP_RED_LAUNCH(MTP_RED_FP32);
-    else if (mode == MTP_RED_FP16) MTP_RED_LAUNCH(MTP_RED_FP16);
-    else MTP_RED_LAUNCH(MTP_RED_INT8TOK);
+      if (mode == MTP_RED_FP32) MTP_RED_LAUNCH(MTP_RED_FP32);
+      else if (mode == MTP_RED_FP16) MTP_RED_LAUNCH(MTP_RED_FP16);
+      else MTP_RED_LAUNCH(MTP_RED_INT8TOK);
 #undef MTP_RED_LAUNCH
+    }
     int rc = check_launch("reduce");
     if (rc) return rc;
   }

@@ -6,8 +6,9 @@
 //   warp 1      allocates 512 TMEM columns (two 128 x bn fp32 accumulators) and one lane issues
 //               tcgen05.mma (kind::f16, M=128, N=bn, K=16 per instruction), releasing ring slots
 //               and signalling finished accumulators with tcgen05.commit;
-//   warps 2-5   epilogue: tcgen05.ld 32 lanes x 16 columns at a time, fused epilogue op, stores;
-//               overlaps the next tile's MMAs thanks to the second accumulator.
+//   warps 2-9   epilogue: two warps per TMEM lane quarter, alternating 16-column chunks;
+//               tcgen05.ld 32 lanes x 16 columns, fused epilogue op, stores; overlaps the next
+//               tile's MMAs thanks to the second accumulator.
 // Every mbarrier wait is bounded (globaltimer); on expiry the CTA records MTP_ERR_TIMEOUT in a
 // device word, drains its in-flight copies and MMAs with bounded waits, frees TMEM and returns.
 #include <cuda.h>
@@ -20,7 +21,8 @@ constexpr int BM = 128, BK = 64, BN_MAX = 256, STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;
 constexpr int B_BYTES = BN_MAX * BK * 2;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int NUM_THREADS = 192;
+constexpr int NUM_EPI_WARPS = 8;
+constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
 
@@ -138,7 +140,7 @@ __device__ __forceinline__ void epilogue_store(const Params &p, int row, int n0,
     for (int i = 0; i < 16; ++i) {
       const int n = n0 + i;
       const float t = v[i] + (n < p.N ? load_bias(p, n) : 0.f);
-      v[i] = p.epi == MTP_EPI_BIAS_SOFTPLUS ? softplus_f(t) : t;
+      v[i] = p.epi == MTP_EPI_BIAS_SOFTPLUS ? (t > 20.f ? t : log1pf(__expf(t))) : t;
     }
   }
   if (row >= p.M) return;
@@ -194,7 +196,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), 4);
+      mbar_init(tempty_bar(a), NUM_EPI_WARPS);
     }
     mbar_init(drain_bar, 1);
     *abort = 0;
@@ -281,8 +283,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------------------ epilogue (warps 2..5)
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    // ------------------------------------------------------------ epilogue (warps 2..9)
+    const int q = warp & 3;              // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;    // which alternate 16-column chunks it takes
     int local = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
       const int a = local & 1;
@@ -293,7 +296,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tile_coords(p, t, mt, nt);
       const int row = mt * BM + q * 32 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN_MAX);
-      for (int j = 0; j < p.bn; j += 16) {
+      for (int j = half * 16; j < p.bn; j += 32) {
         float v[16];
         tmem_ld16(tbase + (uint32_t)j, v);
         const int n0 = nt * p.bn + j;
@@ -382,7 +385,7 @@ int gemm_tc(const void *A, const void *B, void *C, int M, int N, int K, int lda,
   p.tiles_m = ceil_div(M, BM);
   p.tiles_n = ceil_div(N, p.bn);
   p.num_tiles = p.tiles_m * p.tiles_n;
-  p.group_m = 16;
+  p.group_m = 32;
   p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
   const size_t cb = c_dtype == MTP_F32 ? 4 : 2;
   p.vec_ok = aligned16(C) && ((size_t)ldc * cb) % 16 == 0;

@@ -5,6 +5,7 @@
 //   h_t   = exp(dt_t * A_n) * h_{t-1} + (dt_t * B_t[n]) * xc_t
 //   y_t   = (sum_n C_t[n] * h_t[n] + D * xc_t) * silu(z_t)
 // restating mamba_lite/tp_model.py:93-129 (prefill) and :145-173 (step).
+#include <cstdlib>
 #include "common.cuh"
 
 namespace mtp {
@@ -67,30 +68,128 @@ __global__ void conv1d_silu_kernel(const T *__restrict__ xz, int ld_xz, const T 
   }
 }
 
+// Vectorised variant: one thread per (16-byte group of VEC channels, run of TT
+// positions); loads and stores are 16 bytes wide.  Needs Es % VEC == 0 and
+// 16-byte aligned rows.
+template <typename T> struct Pack16;
+template <> struct Pack16<__nv_bfloat16> {
+  static constexpr int V = 8;
+  static __device__ __forceinline__ void load(const __nv_bfloat16 *p, float (&v)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4 *>(p);
+    const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h2[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+  static __device__ __forceinline__ void store(__nv_bfloat16 *p, const float (&v)[8]) {
+    uint4 u;
+    __nv_bfloat162 *h2 = reinterpret_cast<__nv_bfloat162 *>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h2[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    *reinterpret_cast<uint4 *>(p) = u;
+  }
+};
+template <> struct Pack16<float> {
+  static constexpr int V = 4;
+  static __device__ __forceinline__ void load(const float *p, float (&v)[4]) {
+    const float4 f = *reinterpret_cast<const float4 *>(p);
+    v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+  }
+  static __device__ __forceinline__ void store(float *p, const float (&v)[4]) {
+    *reinterpret_cast<float4 *>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  }
+};
+
+template <typename T, int K, int TT>
+__global__ void conv1d_silu_vec_kernel(const T *__restrict__ xz, int ld_xz, const T *__restrict__ w,
+                                       const T *__restrict__ bias, const T *__restrict__ hist, T *__restrict__ xc,
+                                       int ld_xc, int L, int Es) {
+  constexpr int V = Pack16<T>::V;
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * V;
+  const int t0 = blockIdx.y * TT;
+  const int b = blockIdx.z;
+  if (c >= Es) return;
+  float wk[V][K], bc[V], win[V][K - 1];
+#pragma unroll
+  for (int u = 0; u < V; ++u) {
+#pragma unroll
+    for (int j = 0; j < K; ++j) wk[u][j] = ldf(w + (size_t)(c + u) * K + j);
+    bc[u] = bias ? ldf(bias + c + u) : 0.f;
+  }
+#pragma unroll
+  for (int j = 0; j < K - 1; ++j) {
+    const int t = t0 - (K - 1) + j;
+    if (t >= 0) {
+      float v[V];
+      Pack16<T>::load(xz + (size_t)(b * (size_t)L + t) * ld_xz + c, v);
+#pragma unroll
+      for (int u = 0; u < V; ++u) win[u][j] = v[u];
+    } else {
+#pragma unroll
+      for (int u = 0; u < V; ++u) win[u][j] = hist ? ldf(hist + ((size_t)b * Es + c + u) * (K - 1) + (K - 1 + t)) : 0.f;
+    }
+  }
+#pragma unroll 4
+  for (int i = 0; i < TT; ++i) {
+    const int t = t0 + i;
+    if (t >= L) break;
+    float xv[V], o[V];
+    Pack16<T>::load(xz + (size_t)(b * (size_t)L + t) * ld_xz + c, xv);
+#pragma unroll
+    for (int u = 0; u < V; ++u) {
+      float acc = bc[u];
+#pragma unroll
+      for (int j = 0; j < K - 1; ++j) acc = fmaf(wk[u][j], win[u][j], acc);
+      acc = fmaf(wk[u][K - 1], xv[u], acc);
+#pragma unroll
+      for (int j = 0; j < K - 2; ++j) win[u][j] = win[u][j + 1];
+      win[u][K - 2] = xv[u];
+      o[u] = silu_f(acc);
+    }
+    Pack16<T>::store(xc + (size_t)(b * (size_t)L + t) * ld_xc + c, o);
+  }
+}
+
 // ----------------------------------------------------------------- fused prefill scan
-// CTA = (channel block of CB channels, one sequence b); TPC threads share one
-// channel, each holding N/TPC states in registers.  The sequence is walked in
-// chunks of TL positions staged in shared memory by cp.async (double buffer):
-// raw x, z, dt for the block's channels and B|C (shared by all channels).
-template <typename T, int N, int TPC, int CB, int TL>
+// CTA = 128 threads = (128 / TPC) channels of one sequence b; TPC threads share
+// a channel, each holding N/TPC states in registers.  The sequence is walked in
+// chunks of TL positions; raw x, dt and B|C of the next chunk are staged in
+// shared memory by cp.async while the current one is processed.  Per chunk:
+//   phase A  conv1d + SiLU of the TL positions (independent of the state: ILP)
+//   phase B  the recurrence over the TL positions
+//   phase C  coalesced store y = (C.h + D.xc) * silu(z), z read straight from global.
+template <typename T, int N, int TPC, int TL>
 struct ScanSmem {
+  static constexpr int CB = 128 / TPC;
   T x[2][TL][CB];
-  T z[2][TL][CB];
   float dt[2][TL][CB];
   float bc[2][TL][2 * N];
   float y[TL][CB];
 };
 
-template <typename T, int N, int TPC, int CB, int TL, int K>
-__global__ void __launch_bounds__(CB *TPC) scan_prefill_kernel(
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+
+// silu with the hardware exponential and a fast divide (x / (1 + e^-x))
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
+template <typename T, int N, int TPC, int TL, int K>
+__global__ void __launch_bounds__(128, (TPC == 1 ? 4 : 6)) scan_prefill_kernel(
     const T *__restrict__ xz, int ld_xz, const float *__restrict__ dtp, int ld_dt, const float *__restrict__ bcp,
     int ld_bc, const T *__restrict__ A_log, const T *__restrict__ Dp, const T *__restrict__ conv_w,
     const T *__restrict__ conv_b, const T *conv_init, const float *ssm_init, T *__restrict__ y, int ld_y,
-    T *conv_final, float *ssm_final, int L, int Es) {
+    T *conv_final, float *ssm_final, int L, int Es, bool vec16) {
+  using S = ScanSmem<T, N, TPC, TL>;
+  constexpr int CB = S::CB;
   constexpr int NS = N / TPC;
-  constexpr int NT = CB * TPC;
+  constexpr int NT = 128;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  auto &sm = *reinterpret_cast<ScanSmem<T, N, TPC, CB, TL> *>(smem_raw);
+  S &sm = *reinterpret_cast<S *>(smem_raw);
 
   const int b = blockIdx.y;
   const int c0 = blockIdx.x * CB;
@@ -98,10 +197,9 @@ __global__ void __launch_bounds__(CB *TPC) scan_prefill_kernel(
   const int sub = threadIdx.x % TPC;
   const int c = c0 + cl;
   const bool live = c < Es;
-  const int ncb = min(CB, Es - c0);  // live channels in this block
+  const int ncb = min(CB, Es - c0);
   const size_t row0 = (size_t)b * L;
 
-  // per-thread constants
   float A2[NS], h[NS];
   float wk[K], win[K - 1];
   float Dv = 0.f, cbias = 0.f;
@@ -121,25 +219,39 @@ __global__ void __launch_bounds__(CB *TPC) scan_prefill_kernel(
     cbias = conv_b ? ldf(conv_b + c) : 0.f;
   }
 
-  // cooperative async load of chunk k into buffer buf (4-byte granules)
   auto load_chunk = [&](int k, int buf) {
     const int t0 = k * TL;
     const int tl = min(TL, L - t0);
-    constexpr int EPW = 4 / sizeof(T);  // elements per 4-byte word for x / z
-    const int wpr = (ncb + EPW - 1) / EPW;  // words per row
-    for (int i = threadIdx.x; i < tl * wpr; i += NT) {
-      const int tt = i / wpr, wi = i % wpr;
-      const size_t r = row0 + t0 + tt;
-      cp_async4(&sm.x[buf][tt][wi * EPW], xz + r * ld_xz + c0 + wi * EPW);
-      cp_async4(&sm.z[buf][tt][wi * EPW], xz + r * ld_xz + Es + c0 + wi * EPW);
-    }
-    for (int i = threadIdx.x; i < tl * ncb; i += NT) {
-      const int tt = i / ncb, ci = i % ncb;
-      cp_async4(&sm.dt[buf][tt][ci], dtp + (row0 + t0 + tt) * ld_dt + c0 + ci);
-    }
-    for (int i = threadIdx.x; i < tl * 2 * N; i += NT) {
-      const int tt = i / (2 * N), j = i % (2 * N);
-      cp_async4(&sm.bc[buf][tt][j], bcp + (row0 + t0 + tt) * ld_bc + j);
+    if (vec16) {  // full channel blocks, 16-byte aligned rows
+      constexpr int XW = CB * (int)sizeof(T) / 16, DW = CB * 4 / 16, BW = 2 * N * 4 / 16;
+      for (int i = threadIdx.x; i < tl * XW; i += NT) {
+        const int tt = i / XW, w = i % XW;
+        cp_async16(reinterpret_cast<char *>(&sm.x[buf][tt][0]) + 16 * w,
+                   reinterpret_cast<const char *>(xz + (row0 + t0 + tt) * ld_xz + c0) + 16 * w);
+      }
+      for (int i = threadIdx.x; i < tl * DW; i += NT) {
+        const int tt = i / DW, w = i % DW;
+        cp_async16(&sm.dt[buf][tt][4 * w], dtp + (row0 + t0 + tt) * ld_dt + c0 + 4 * w);
+      }
+      for (int i = threadIdx.x; i < tl * BW; i += NT) {
+        const int tt = i / BW, w = i % BW;
+        cp_async16(&sm.bc[buf][tt][4 * w], bcp + (row0 + t0 + tt) * ld_bc + 4 * w);
+      }
+    } else {  // 4-byte granules, partial channel blocks
+      constexpr int EPW = 4 / sizeof(T);
+      const int wpr = (ncb + EPW - 1) / EPW;
+      for (int i = threadIdx.x; i < tl * wpr; i += NT) {
+        const int tt = i / wpr, wi = i % wpr;
+        cp_async4(&sm.x[buf][tt][wi * EPW], xz + (row0 + t0 + tt) * ld_xz + c0 + wi * EPW);
+      }
+      for (int i = threadIdx.x; i < tl * ncb; i += NT) {
+        const int tt = i / ncb, ci = i % ncb;
+        cp_async4(&sm.dt[buf][tt][ci], dtp + (row0 + t0 + tt) * ld_dt + c0 + ci);
+      }
+      for (int i = threadIdx.x; i < tl * 2 * N; i += NT) {
+        const int tt = i / (2 * N), j = i % (2 * N);
+        cp_async4(&sm.bc[buf][tt][j], bcp + (row0 + t0 + tt) * ld_bc + j);
+      }
     }
     cp_async_commit();
   };
@@ -157,45 +269,59 @@ __global__ void __launch_bounds__(CB *TPC) scan_prefill_kernel(
     __syncthreads();
     const int t0 = k * TL;
     const int tl = min(TL, L - t0);
-    // every lane runs the loop (the group shuffle needs all 32); lanes past the
-    // last channel read in-bounds shared memory and store nothing
-    {
-      for (int tt = 0; tt < tl; ++tt) {
+    // phase A: conv + SiLU for the chunk (every lane runs it; lanes past the last
+    // channel read in-bounds shared memory and store nothing)
+    float xcs[TL], dts[TL];
+#pragma unroll
+    for (int tt = 0; tt < TL; ++tt) {
+      if (tt < tl) {
         const float xv = ldf(&sm.x[buf][tt][cl]);
         float acc = cbias;
 #pragma unroll
-        for (int j = 0; j < K - 1; ++j) acc += wk[j] * win[j];
-        acc += wk[K - 1] * xv;
+        for (int j = 0; j < K - 1; ++j) acc = fmaf(wk[j], win[j], acc);
+        acc = fmaf(wk[K - 1], xv, acc);
 #pragma unroll
         for (int j = 0; j < K - 2; ++j) win[j] = win[j + 1];
         win[K - 2] = xv;
-        const float xc = silu_f(acc);
-        const float dt = sm.dt[buf][tt][cl];
-        const float *bcr = sm.bc[buf][tt];
-        float yv = 0.f;
+        xcs[tt] = silu_fast(acc);
+        dts[tt] = sm.dt[buf][tt][cl];
+      }
+    }
+    // phase B: recurrence
 #pragma unroll
-        for (int i = 0; i < NS; ++i) {
-          const int n = sub * NS + i;
-          const float dA = ex2_hw(dt * A2[i]);
-          const float dBx = (dt * bcr[n]) * xc;
-          h[i] = fmaf(dA, h[i], dBx);
-          yv = fmaf(bcr[N + n], h[i], yv);
+    for (int tt = 0; tt < TL; ++tt) {
+      if (tt < tl) {
+        const float dt = dts[tt];
+        const float dtx = dt * xcs[tt];
+        const float4 *bv = reinterpret_cast<const float4 *>(&sm.bc[buf][tt][sub * NS]);
+        const float4 *cv = reinterpret_cast<const float4 *>(&sm.bc[buf][tt][N + sub * NS]);
+        float ya[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int q = 0; q < NS / 4; ++q) {
+          const float4 B4 = bv[q], C4 = cv[q];
+          const float Bs[4] = {B4.x, B4.y, B4.z, B4.w}, Cs[4] = {C4.x, C4.y, C4.z, C4.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int i = 4 * q + u;
+            const float dA = ex2_hw(dt * A2[i]);
+            h[i] = fmaf(dA, h[i], Bs[u] * dtx);
+            ya[u] = fmaf(Cs[u], h[i], ya[u]);
+          }
         }
+        float yv = (ya[0] + ya[1]) + (ya[2] + ya[3]);
 #pragma unroll
         for (int o = 1; o < TPC; o <<= 1) yv += __shfl_xor_sync(0xffffffffu, yv, o);
-        if (sub == 0 && live) {
-          const float zv = ldf(&sm.z[buf][tt][cl]);
-          sm.y[tt][cl] = (yv + Dv * xc) * silu_f(zv);
-        }
+        if (sub == 0) sm.y[tt][cl] = fmaf(Dv, xcs[tt], yv);
       }
     }
     __syncthreads();
-    // coalesced store of the chunk's y
+    // phase C: gate with silu(z) and store
     for (int i = threadIdx.x; i < tl * ncb; i += NT) {
       const int tt = i / ncb, ci = i % ncb;
-      stf(y + (row0 + t0 + tt) * ld_y + c0 + ci, sm.y[tt][ci]);
+      const size_t r = row0 + t0 + tt;
+      const float zv = ldf(xz + r * ld_xz + Es + c0 + ci);
+      stf(y + r * ld_y + c0 + ci, sm.y[tt][ci] * silu_fast(zv));
     }
-    // buffer `buf` is refilled by the next iteration's prefetch only after this barrier
     __syncthreads();
   }
   if (live) {
@@ -209,9 +335,13 @@ __global__ void __launch_bounds__(CB *TPC) scan_prefill_kernel(
 }
 
 // ----------------------------------------------------------------- single-token step
-// CTA = CB channels x all B sequences.  dt_proj rows of the block and the
-// dt_low vectors are staged in shared memory; then one thread per (b, c)
-// does conv shift, dt, state update and output, all in place.
+// CTA = CB channels x all B sequences, 256 threads.
+//   phase 0  A * log2(e) of the block's channels into shared memory
+//   phase 1  dt_proj + bias + softplus: one warp per (b, c) pair at a time, lanes
+//            split the dt_rank contraction, shuffle reduction; dt into shared memory
+//   phase 2  N/4 threads per (b, c), 4 states each: conv over [history | x], conv
+//            history shift (one thread), state update in place (float4), C.h reduced
+//            over the 4 threads, D skip and SiLU(z) gate.
 template <typename T, int N, int K, int CB>
 __global__ void __launch_bounds__(256) step_kernel(const T *__restrict__ xz, int ld_xz, const T *__restrict__ dt_low,
                                                    int ld_dl, const T *__restrict__ W_dt, const T *__restrict__ b_dt,
@@ -219,58 +349,76 @@ __global__ void __launch_bounds__(256) step_kernel(const T *__restrict__ xz, int
                                                    const T *__restrict__ Dp, const T *__restrict__ conv_w,
                                                    const T *__restrict__ conv_b, T *conv_state, float *ssm_state,
                                                    T *__restrict__ y, int ld_y, int B, int Es, int R) {
+  constexpr int NS = 4, TPG = N / NS;  // 4 states per thread
   extern __shared__ __align__(16) float ssm_sm[];
-  const int RP = R + 1;  // padded row stride against bank conflicts
-  float *wdt = ssm_sm;               // [CB][RP]
-  float *dl = ssm_sm + CB * RP;      // [B][R]
+  float *a2s = ssm_sm;            // [CB][N]
+  float *dts = ssm_sm + CB * N;   // [B][CB]
   const int c0 = blockIdx.x * CB;
   const int ncb = min(CB, Es - c0);
-  for (int i = threadIdx.x; i < ncb * R; i += blockDim.x) {
-    const int cc = i / R, r = i % R;
-    wdt[cc * RP + r] = ldf(W_dt + (size_t)(c0 + cc) * R + r);
-  }
-  for (int i = threadIdx.x; i < B * R; i += blockDim.x) {
-    const int bb = i / R, r = i % R;
-    dl[bb * R + r] = ldf(dt_low + (size_t)bb * ld_dl + r);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < ncb * N; i += blockDim.x)
+    a2s[i] = -expf(ldf(A_log + (size_t)c0 * N + i)) * kLog2e;
+  for (int p = warp; p < B * ncb; p += blockDim.x >> 5) {
+    const int bb = p / ncb, cc = p % ncb;
+    const T *wr = W_dt + (size_t)(c0 + cc) * R;
+    const T *xr = dt_low + (size_t)bb * ld_dl;
+    float sacc = 0.f;
+    for (int r = lane; r < R; r += 32) sacc = fmaf(ldf(xr + r), ldf(wr + r), sacc);
+    for (int o = 16; o; o >>= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, o);
+    if (lane == 0) dts[bb * CB + cc] = softplus_f(sacc + ldf(b_dt + c0 + cc));
   }
   __syncthreads();
-  for (int p = threadIdx.x; p < B * ncb; p += blockDim.x) {
-    const int bb = p / ncb, cc = p % ncb, c = c0 + cc;
-    // dt_proj + bias + softplus (tp_model.py:162-163)
-    float s = 0.f;
-    const float *wr = wdt + cc * RP;
-    const float *xr = dl + bb * R;
-    for (int r = 0; r < R; ++r) s = fmaf(xr[r], wr[r], s);
-    const float dt = softplus_f(s + ldf(b_dt + c));
-    // conv over [history | x] then shift (tp_model.py:145-157)
-    T *cs = conv_state + ((size_t)bb * Es + c) * (K - 1);
-    const float xv = ldf(xz + (size_t)bb * ld_xz + c);
-    float acc = conv_b ? ldf(conv_b + c) : 0.f;
+  // phase 2: groups of TPG consecutive threads; whole warps iterate together so the
+  // group shuffles always have all 32 lanes present
+  const int items = B * ncb * TPG;
+  const int iters = (items + blockDim.x - 1) / blockDim.x;
+  for (int it = 0; it < iters; ++it) {
+    const int idx = it * blockDim.x + threadIdx.x;
+    const bool act = idx < items;
+    const int g = act ? idx / TPG : 0, sub = idx % TPG;
+    const int bb = g / ncb, cc = g % ncb, c = c0 + cc;
+    float xc = 0.f, zv = 0.f, dt = 0.f, yv = 0.f, xv = 0.f;
     float hist[K - 1];
+    T *cs = conv_state + ((size_t)bb * Es + c) * (K - 1);
+    if (act) {
+      xv = ldf(xz + (size_t)bb * ld_xz + c);
+      float acc = conv_b ? ldf(conv_b + c) : 0.f;
 #pragma unroll
-    for (int j = 0; j < K - 1; ++j) {
-      hist[j] = ldf(cs + j);
-      acc += ldf(conv_w + (size_t)c * K + j) * hist[j];
+      for (int j = 0; j < K - 1; ++j) {
+        hist[j] = ldf(cs + j);
+        acc = fmaf(ldf(conv_w + (size_t)c * K + j), hist[j], acc);
+      }
+      acc = fmaf(ldf(conv_w + (size_t)c * K + K - 1), xv, acc);
+      xc = silu_f(acc);
+      zv = ldf(xz + (size_t)bb * ld_xz + Es + c);
+      dt = dts[bb * CB + cc];
+      const float dtx = dt * xc;
+      float *hs = ssm_state + ((size_t)bb * Es + c) * N + sub * NS;
+      const float *bcr = bcp + (size_t)bb * ld_bc;
+      const float *a2 = a2s + cc * N + sub * NS;
+#pragma unroll
+      for (int q = 0; q < NS; q += 4) {
+        float4 hv = *reinterpret_cast<const float4 *>(hs + q);
+        float hh[4] = {hv.x, hv.y, hv.z, hv.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int n = sub * NS + q + u;
+          const float dA = ex2_hw(dt * a2[q + u]);
+          hh[u] = fmaf(dA, hh[u], bcr[n] * dtx);
+          yv = fmaf(bcr[N + n], hh[u], yv);
+        }
+        *reinterpret_cast<float4 *>(hs + q) = make_float4(hh[0], hh[1], hh[2], hh[3]);
+      }
     }
-    acc += ldf(conv_w + (size_t)c * K + K - 1) * xv;
 #pragma unroll
-    for (int j = 0; j < K - 2; ++j) stf(cs + j, hist[j + 1]);
-    stf(cs + K - 2, xv);
-    const float xc = silu_f(acc);
-    // state update and output (tp_model.py:165-173)
-    float *hs = ssm_state + ((size_t)bb * Es + c) * N;
-    const float *bcr = bcp + (size_t)bb * ld_bc;
-    float yv = 0.f;
+    for (int o = 1; o < TPG; o <<= 1) yv += __shfl_xor_sync(0xffffffffu, yv, o);
+    __syncwarp();  // every lane of the group has read the history before it is shifted
+    if (act && sub == 0) {
 #pragma unroll
-    for (int n = 0; n < N; ++n) {
-      const float a2 = -expf(ldf(A_log + (size_t)c * N + n)) * kLog2e;
-      const float dA = ex2_hw(dt * a2);
-      const float hv = fmaf(dA, hs[n], (dt * bcr[n]) * xc);
-      hs[n] = hv;
-      yv = fmaf(bcr[N + n], hv, yv);
+      for (int j = 0; j < K - 2; ++j) stf(cs + j, hist[j + 1]);
+      stf(cs + K - 2, xv);
     }
-    const float zv = ldf(xz + (size_t)bb * ld_xz + Es + c);
-    stf(y + (size_t)bb * ld_y + c, (yv + ldf(Dp + c) * xc) * silu_f(zv));
+    if (act && sub == 0) stf(y + (size_t)bb * ld_y + c, (yv + ldf(Dp + c) * xc) * silu_f(zv));
   }
 }
 
@@ -279,19 +427,22 @@ static int launch_scan(const void *xz, int ld_xz, const float *dt, int ld_dt, co
                        const void *A_log, const void *Dp, const void *conv_w, const void *conv_b,
                        const void *conv_init, const float *ssm_init, void *y, int ld_y, void *conv_final,
                        float *ssm_final, int B, int L, int Es, cudaStream_t s) {
-  constexpr int CB = 64, TL = 32, K = 4;
-  using S = ScanSmem<T, N, TPC, CB, TL>;
-  auto kern = scan_prefill_kernel<T, N, TPC, CB, TL, K>;
+  constexpr int TL = 16, K = 4;
+  using S = ScanSmem<T, N, TPC, TL>;
+  constexpr int CB = S::CB;
+  auto kern = scan_prefill_kernel<T, N, TPC, TL, K>;
   static bool attr_set = false;  // per template instance
   if (!attr_set) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(S)) != cudaSuccess)
       return check_launch("scan_prefill attr");
     attr_set = true;
   }
+  const bool vec16 = Es % CB == 0 && aligned16(xz) && aligned16(dt) && aligned16(bc) &&
+                     ((size_t)ld_xz * sizeof(T)) % 16 == 0 && ld_dt % 4 == 0 && ld_bc % 4 == 0;
   dim3 grid((Es + CB - 1) / CB, B);
-  kern<<<grid, CB * TPC, sizeof(S), s>>>((const T *)xz, ld_xz, dt, ld_dt, bc, ld_bc, (const T *)A_log,
-                                          (const T *)Dp, (const T *)conv_w, (const T *)conv_b, (const T *)conv_init,
-                                          ssm_init, (T *)y, ld_y, (T *)conv_final, ssm_final, L, Es);
+  kern<<<grid, 128, sizeof(S), s>>>((const T *)xz, ld_xz, dt, ld_dt, bc, ld_bc, (const T *)A_log, (const T *)Dp,
+                                     (const T *)conv_w, (const T *)conv_b, (const T *)conv_init, ssm_init, (T *)y, ld_y,
+                                     (T *)conv_final, ssm_final, L, Es, vec16);
   return check_launch("scan_prefill");
 }
 
@@ -307,9 +458,21 @@ int mtp_conv1d_silu(const void *xz, int ld_xz, const void *conv_w, const void *c
   MTP_REQUIRE(K == 4, "only d_conv == 4 is built");
   MTP_REQUIRE(ld_xz >= 2 * Es && ld_xc >= Es, "leading dimensions too small");
   if (B == 0 || L == 0) return MTP_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t es_b = dtype == MTP_F32 ? 4 : 2;
+  const int V = (int)(16 / es_b);
+  const bool vec = Es % V == 0 && aligned16(xz) && aligned16(xc) && (ld_xz * es_b) % 16 == 0 && (ld_xc * es_b) % 16 == 0;
+  if (vec) {
+    constexpr int TT = 16;
+    const int groups = Es / V;
+    dim3 grid((groups + 63) / 64, (L + TT - 1) / TT, B);
+    MTP_DISPATCH_FB(dtype, T,
+        conv1d_silu_vec_kernel<T, 4, TT><<<grid, 64, 0, s>>>((const T *)xz, ld_xz, (const T *)conv_w,
+                                                              (const T *)conv_b, (const T *)hist, (T *)xc, ld_xc, L, Es));
+    return check_launch("conv1d_silu");
+  }
   constexpr int TT = 8;
   dim3 grid((Es + 127) / 128, (L + TT - 1) / TT, B);
-  cudaStream_t s = (cudaStream_t)stream;
   MTP_DISPATCH_FB(dtype, T,
       conv1d_silu_kernel<T, 4, TT><<<grid, 128, 0, s>>>((const T *)xz, ld_xz, (const T *)conv_w,
                                                          (const T *)conv_b, (const T *)hist, (T *)xc, ld_xc, L, Es));
@@ -334,7 +497,12 @@ int mtp_scan_prefill(const void *xz, int ld_xz, const float *dt, int ld_dt, cons
   // threads per channel: enough resident warps at small channel counts
   const long pairs = (long)B * Es;
   const int sms = num_sms();
-  const int tpc = pairs >= (long)sms * 1024 ? 1 : (pairs >= (long)sms * 384 ? 2 : 4);
+  int tpc = pairs >= (long)sms * 512 ? 1 : (pairs >= (long)sms * 256 ? 2 : 4);
+  // tuning override: MTP_SCAN_TPC = 1, 2 or 4 threads per channel
+  if (const char *env = getenv("MTP_SCAN_TPC")) {
+    const int v = atoi(env);
+    if (v == 1 || v == 2 || v == 4) tpc = v;
+  }
 #define MTP_SCAN_CASE(TT, NN, TP)                                                                          \
   return launch_scan<TT, NN, TP>(xz, ld_xz, dt, ld_dt, bc, ld_bc, A_log, Dp, conv_w, conv_b, conv_init,   \
                                  ssm_init, y, ld_y, conv_final, ssm_final, B, L, Es, s)
@@ -357,11 +525,11 @@ int mtp_step(const void *xz, int ld_xz, const void *dt_low, int ld_dl, const voi
               "null pointer");
   MTP_REQUIRE(K == 4, "only d_conv == 4 is built");
   MTP_REQUIRE(N == 16 || N == 8, "d_state must be 8 or 16");
-  MTP_REQUIRE(B >= 0 && B <= 256 && Es > 0 && R > 0 && R <= 512, "bad sizes");
+  MTP_REQUIRE(B >= 0 && B <= 1024 && Es > 0 && R > 0, "bad sizes");
+  MTP_REQUIRE(aligned16(ssm_state), "ssm_state must be 16-byte aligned");
   if (B == 0) return MTP_OK;
   constexpr int CB = 32;
-  const size_t smem = ((size_t)CB * (R + 1) + (size_t)B * R) * sizeof(float);
-  MTP_REQUIRE(smem <= 200 * 1024, "batch x dt_rank too large for the step kernel");
+  const size_t smem = ((size_t)CB * N + (size_t)B * CB) * sizeof(float);
   cudaStream_t s = (cudaStream_t)stream;
   dim3 grid((Es + CB - 1) / CB);
 #define MTP_STEP_CASE(TT, NN)                                                                               \

@@ -176,6 +176,38 @@ def bench_allreduce(a):
     return res if rank == 0 else None
 
 
+def bench_decode(a):
+    """Eager and graphed decode step of a random-init model of --shape at --batch."""
+    from .checkpoint import random_init_state_dict
+    from .config import shape_config
+    from .cuda_graph import GraphedStepper
+    from .tp_model import TPMambaLM
+    from .tp_utils import build_spec
+
+    cfg = shape_config(a.shape)
+    if a.layers:
+        cfg.n_layer = a.layers
+    spec = a.spec if a.spec != "mixed" else build_spec(
+        {"default": "int8", "overrides": {f"{i}:out_proj": "fp16" for i in (0, cfg.n_layer - 4, cfg.n_layer - 3,
+                                                                             cfg.n_layer - 2, cfg.n_layer - 1)}},
+        cfg.n_layer)
+    sd = random_init_state_dict(cfg, seed=0, dtype=torch.bfloat16, device="cuda")
+    m = TPMambaLM.from_state_dict_shard(cfg, sd, 0, 1, dtype=torch.bfloat16, allreduce_dtype=spec, device="cuda")
+    del sd
+    ids = torch.randint(0, cfg.vocab_size, (a.batch, 64), device="cuda")
+    _, cache = m.prefill(ids)
+    nid = torch.zeros(a.batch, 1, dtype=torch.long, device="cuda")
+    eager_ms = _time(lambda: m.step(nid, cache), a.warmup, a.iters)
+    st = GraphedStepper(m, cache, a.batch, "cuda")
+    st.capture()
+    graph_ms = _time(lambda: st.replay(nid), a.warmup, a.iters)
+    st.release()
+    w_bytes = sum(p.numel() * p.element_size() for p in m.parameters())
+    return {"kernel": "decode_step", "shape": a.shape, "layers": cfg.n_layer, "batch": a.batch,
+            "eager_ms": eager_ms, "graphed_ms": graph_ms, "weight_bytes": w_bytes,
+            "hbm_floor_ms": w_bytes / (peaks()["hbm_gbs"] * 1e9) * 1e3}
+
+
 def main():
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="what", required=True)
@@ -198,12 +230,18 @@ def main():
     r.add_argument("--rows", type=int, default=32768)
     r.add_argument("--cols", type=int, default=2048)
     r.add_argument("--mode", choices=["fp32", "fp16", "int8"], default="int8")
-    for p in (g, s, st, r):
+    dcd = sub.add_parser("decode")
+    dcd.add_argument("--shape", default="1.4b")
+    dcd.add_argument("--layers", type=int, default=0, help="override n_layer (0: the shape's)")
+    dcd.add_argument("--batch", type=int, default=1)
+    dcd.add_argument("--spec", default="mixed")
+    for p in (g, s, st, r, dcd):
         p.add_argument("--warmup", type=int, default=3)
         p.add_argument("--iters", type=int, default=10)
     a = ap.parse_args()
     L.load()
-    res = {"gemm": bench_gemm, "scan": bench_scan, "step": bench_step, "allreduce": bench_allreduce}[a.what](a)
+    res = {"gemm": bench_gemm, "scan": bench_scan, "step": bench_step, "allreduce": bench_allreduce,
+           "decode": bench_decode}[a.what](a)
     if res is not None:
         print(json.dumps(res), flush=True)
 

@@ -117,8 +117,9 @@ def test_scan_prefill_matches_oracle(dtype, b, l, es, nst, init):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, BF])
-def test_conv1d_silu_matches_oracle(dtype):
-    b, l, es = 3, 19, 130
+@pytest.mark.parametrize("es", [130, 256])
+def test_conv1d_silu_matches_oracle(dtype, es):
+    b, l = 3, 19
     x, z, *_ , cw, cb, ci, _ = _ssm_inputs(b, l, es, 16, 9, dtype)
     xc_ref, _ = O.conv_silu_ref(x, cw, cb, ci)
     T = b * l
