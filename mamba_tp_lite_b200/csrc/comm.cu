@@ -20,6 +20,7 @@
 // ranks agree on it.  Receive slots are double-buffered by epoch parity: a rank can run at most one
 // call ahead of a peer, so consecutive calls on one site never write a slot a peer still reads.  Each wait is bounded (globaltimer); on expiry
 // the kernel stores MTP_ERR_TIMEOUT in the context's status word and returns.
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 #include "common.cuh"
@@ -641,19 +642,6 @@ __global__ void dequant_sum_kernel(const uint8_t *__restrict__ pl, int ws, int r
 static float *g_scratch = nullptr;
 static size_t g_scratch_bytes = 0;
 
-// Per-warp row scratch of the reduction kernels.  Grown, never freed: a captured CUDA graph
-// may still hold an older pointer.  The first call (eager, before any capture) sizes it.
-static float *row_scratch(size_t bytes) {
-  if (bytes > g_scratch_bytes) {
-    float *p = nullptr;
-    if (bytes < ((size_t)32 << 20)) bytes = (size_t)32 << 20;
-    if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
-    g_scratch = p;
-    g_scratch_bytes = bytes;
-  }
-  return g_scratch;
-}
-
 template <int EPI>
 static int run_reduce(mtp_comm *c, int site, int mode, const float *partial, int rows, int cols, EpiOut e,
                       cudaStream_t s) {
@@ -693,7 +681,14 @@ static int run_reduce(mtp_comm *c, int site, int mode, const float *partial, int
     CommDev d{};
     if (has_comm) d = c->d;
     const size_t wire_bytes = (size_t)nr * cols * 4;
-    const bool two_shot = has_comm && c->d.ws > 2 && wire_bytes >= ((size_t)1 << 20);
+    bool two_shot = has_comm && c->d.ws > 2 && wire_bytes >= ((size_t)1 << 20);
+    // protocol override (tests, tuning): MTP_COMM_PROTOCOL=oneshot|twoshot
+    if (has_comm) {
+      if (const char *env = getenv("MTP_COMM_PROTOCOL")) {
+        if (!strcmp(env, "twoshot")) two_shot = true;
+        if (!strcmp(env, "oneshot")) two_shot = false;
+      }
+    }
     const float *pp = partial + (size_t)r0 * cols;
     // register-row kernel when the width allows it
     const int vpl = (cols % 4 != 0) ? 0 : cols <= 256 ? 2 : cols <= 512 ? 4 : cols <= 1024 ? 8 : cols <= 2048 ? 16 : cols <= 3072 ? 24 : 0;

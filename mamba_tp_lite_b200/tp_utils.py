@@ -169,14 +169,14 @@ def exchange_handles(mine: bytes, group, ws: int) -> list[bytes]:
     return gathered
 
 
-def get_comm(group, rank: int, ws: int, cols_x: int, cols_out: int) -> Comm | None:
+def get_comm(group, rank: int, ws: int, cols_x: int, cols_out: int, timeout_s: float | None = None) -> Comm | None:
     """Shared context for (group, device, site widths); collective on first use."""
     if ws == 1:
         return None
     key = (_group_key(group), torch.cuda.current_device(), cols_x, cols_out)
     c = _COMMS.get(key)
     if c is None:
-        c = Comm(group, rank, ws, cols_x, cols_out)
+        c = Comm(group, rank, ws, cols_x, cols_out, timeout_s=timeout_s)
         _COMMS[key] = c
     return c
 

@@ -1,0 +1,207 @@
+"""Multi-GPU tests (one process per GPU, NCCL process group for the
+bootstrap): the peer-memory reductions are bit-exact against the oracle in
+every wire mode and protocol, the TP model matches the oracle's TP emulation
+with identical results on every rank, graphed TP decode equals eager decode,
+and a reduction whose peer never arrives ends with a timeout status (bounded
+wait) instead of hanging.  Skipped on boxes with fewer than 2 GPUs."""
+import datetime
+import os
+import tempfile
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+WS = 2
+
+needs2 = pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < WS,
+                            reason="needs 2 GPUs")
+
+
+def _init(rank, init_file):
+    import torch.distributed as dist
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"file://{init_file}", rank=rank, world_size=WS,
+                            timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", rank))
+
+
+def _finish():
+    import torch.distributed as dist
+
+    from mamba_tp_lite_b200.tp_utils import destroy_comms
+
+    torch.cuda.synchronize()
+    dist.barrier()
+    destroy_comms()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _spawn(fn, *args, timeout=300):
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with tempfile.TemporaryDirectory() as d:
+        procs = [ctx.Process(target=fn, args=(r, os.path.join(d, "rdv"), q) + args) for r in range(WS)]
+        for p in procs:
+            p.start()
+        try:
+            res = dict(q.get(timeout=timeout) for _ in range(WS))
+        finally:
+            for p in procs:
+                p.join(timeout=60)
+                if p.is_alive():
+                    p.kill()
+    for r in range(WS):
+        if isinstance(res[r], str):
+            raise AssertionError(f"rank {r}: {res[r]}")
+    return res
+
+
+# ------------------------------------------------------------------ raw reductions
+def _allreduce_worker(rank, init_file, q, protocol):
+    try:
+        if protocol:
+            os.environ["MTP_COMM_PROTOCOL"] = protocol
+        _init(rank, init_file)
+        from mamba_tp_lite_b200 import _lib as L
+        from mamba_tp_lite_b200.tp_utils import get_comm
+
+        out = {}
+        for rows, cols in ((1, 160), (33, 2048), (4096, 768), (20000, 2048), (7, 18)):
+            comm = get_comm(None, rank, WS, cols, cols)
+            xs = [torch.randn(rows, cols, generator=torch.Generator().manual_seed(1000 * r + rows)) * 3 for r in range(WS)]
+            x = xs[rank].cuda()
+            for mode in (L.RED_FP32, L.RED_FP16, L.RED_INT8TOK):
+                y = torch.empty_like(x)
+                for _ in range(2):  # back-to-back calls on one site
+                    L.call("mtp_allreduce", comm.ptr, 1, mode, L.ptr(x), L.ptr(y), rows, cols, L.stream_ptr())
+                torch.cuda.synchronize()
+                out[(rows, cols, mode)] = y.cpu().numpy()
+            comm.check()
+        q.put((rank, out))
+        _finish()
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, f"{type(e).__name__}: {e}"))
+
+
+@needs2
+@pytest.mark.parametrize("protocol", [None, "twoshot"])
+def test_peer_reductions_bit_exact_vs_oracle(protocol):
+    from mamba_tp_lite_b200 import _lib as L
+    from oracle import mamba_oracle as O
+
+    res = _spawn(_allreduce_worker, protocol)
+    names = {L.RED_FP32: "fp32", L.RED_FP16: "fp16", L.RED_INT8TOK: "int8"}
+    for (rows, cols, mode), got in res[0].items():
+        xs = [(torch.randn(rows, cols, generator=torch.Generator().manual_seed(1000 * r + rows)) * 3).numpy()
+              for r in range(WS)]
+        want = O.REDUCE_FNS[names[mode]](xs)
+        assert got.tobytes() == want.astype(np.float32).tobytes(), (rows, cols, names[mode])
+        assert np.array_equal(res[1][(rows, cols, mode)], got)  # every rank identical
+
+
+# ------------------------------------------------------------------ TP model
+def _tp_model_worker(rank, init_file, q, dtype_name):
+    try:
+        _init(rank, init_file)
+        from mamba_tp_lite_b200.checkpoint import random_init_state_dict
+        from mamba_tp_lite_b200.config import MambaConfig
+        from mamba_tp_lite_b200.cuda_graph import GraphedStepper
+        from mamba_tp_lite_b200.tp_model import TPMambaLM
+
+        dtype = getattr(torch, dtype_name)
+        cfg = MambaConfig(d_model=256, n_layer=3, vocab_size=1000, dt_rank=16)
+        sd = random_init_state_dict(cfg, seed=3, dtype=dtype)
+        ids = torch.randint(0, cfg.vocab_size, (2, 72), generator=torch.Generator().manual_seed(4))
+        out = {}
+        for spec in ("fp32", "fp16", "int8"):
+            m = TPMambaLM.from_state_dict_shard(cfg, sd, rank, WS, dtype=dtype, allreduce_dtype=spec, device="cuda")
+            logits, cache = m.prefill(ids.cuda())
+            nxt = torch.zeros(2, 1, dtype=torch.long, device="cuda")
+            eager = [m.step(nxt, cache).clone() for _ in range(3)]
+            _, cg = m.prefill(ids.cuda())
+            st = GraphedStepper(m, cg, 2, "cuda")
+            st.capture()
+            graphed = [st.replay(nxt).clone() for _ in range(3)]
+            st.release()
+            out[spec] = (logits.float().cpu().numpy(), [e.float().cpu().numpy() for e in eager],
+                         all(torch.equal(a, b) for a, b in zip(eager, graphed)), m.layers[0].mixer.comm.count)
+        q.put((rank, out))
+        _finish()
+    except Exception as e:
+        q.put((rank, f"{type(e).__name__}: {e}"))
+
+
+@needs2
+@pytest.mark.parametrize("dtype_name", ["float32", "bfloat16"])
+def test_tp2_model_matches_oracle_and_ranks_agree(dtype_name):
+    from mamba_tp_lite_b200.checkpoint import random_init_state_dict
+    from mamba_tp_lite_b200.config import MambaConfig
+    from oracle import mamba_oracle as O
+
+    res = _spawn(_tp_model_worker, dtype_name)
+    cfg = MambaConfig(d_model=256, n_layer=3, vocab_size=1000, dt_rank=16)
+    sd = random_init_state_dict(cfg, seed=3, dtype=getattr(torch, dtype_name))
+    ids = torch.randint(0, cfg.vocab_size, (2, 72), generator=torch.Generator().manual_seed(4)).numpy()
+    for spec in ("fp32", "fp16", "int8"):
+        lg0, st0, graph_ok, count = res[0][spec]
+        lg1, st1, _, _ = res[1][spec]
+        assert np.array_equal(lg0, lg1), spec          # identical on every rank
+        assert all(np.array_equal(a, b) for a, b in zip(st0, st1)), spec
+        assert graph_ok, spec                          # graph replay == eager, bitwise
+        # host-side count, as the reference's CommCounter: 2 per prefill (x2), 2 per eager step (3),
+        # 2 per graph warm-up step (3) and 2 for the captured step; replays are not counted
+        assert count == 2 * 2 + 2 * 3 + 2 * 3 + 2, count
+        lm = O.OracleLM(O.Cfg(cfg.d_model, cfg.n_layer, cfg.vocab_size, dt_rank=cfg.dt_rank),
+                        O.state_dict_numpy(sd), world_size=WS, spec=spec)
+        ref, _ = lm.prefill(ids)
+        if dtype_name == "float32":
+            tol = {"fp32": 2e-4, "fp16": 2e-3}.get(spec, 2e-2)
+            np.testing.assert_allclose(lg0, ref, atol=tol, rtol=1e-3)
+        else:
+            met = O.quant_metrics(ref, lg0)
+            assert met["kl"].mean() <= 2e-3 and met["top1"].mean() >= 0.95, (spec, met)
+
+
+# ------------------------------------------------------------------ bounded wait: a peer that never arrives
+def _timeout_worker(rank, init_file, q):
+    try:
+        import torch.distributed as dist
+
+        _init(rank, init_file)
+        from mamba_tp_lite_b200 import _lib as L
+        from mamba_tp_lite_b200.tp_utils import Comm
+
+        comm = Comm(None, rank, WS, 64, 64, max_rows=64, timeout_s=1.0)
+        x = torch.ones(8, 64, device="cuda")
+        y = torch.empty_like(x)
+        status = 0
+        if rank == 0:  # rank 1 never enters this reduction: nothing sets rank 0's flag
+            L.call("mtp_allreduce", comm.ptr, 1, L.RED_FP32, L.ptr(x), L.ptr(y), 8, 64, L.stream_ptr())
+            torch.cuda.synchronize()
+            status = comm.status()
+            comm.reset_status()
+            # the context's device is still usable after the bounded wait expired
+            z = (x * 2).sum().item()
+            assert z == 2 * 8 * 64
+        dist.barrier()
+        comm.destroy()
+        q.put((rank, status))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, f"{type(e).__name__}: {e}"))
+
+
+@needs2
+def test_reduction_with_absent_peer_times_out_with_status():
+    from mamba_tp_lite_b200 import _lib as L
+
+    res = _spawn(_timeout_worker)
+    assert res[0] == L.MTP_ERR_TIMEOUT
+    assert res[1] == 0
