@@ -169,6 +169,22 @@ int mtp_reduce_outproj(mtp_comm *c, int mode, const float *partial, int rows, in
 int mtp_allreduce(mtp_comm *c, int site, int mode, const float *in, float *out, int rows, int cols,
                   void *stream);
 
+/* Allocation-free form of the world-size-1 case of mtp_allreduce (no comm
+ * context): the wire-format round trip of `mode` (fp32 copy, fp16 cast,
+ * int8-per-row quantise/dequantise) of in[rows, cols] into out, bit-identical
+ * to mtp_allreduce(NULL, ...).  No counterpart in the reference: it exists for
+ * callers that cannot call cudaMalloc at all -- for instance code running
+ * inside a host-side memory budget or a runtime that owns every device
+ * allocation -- whereas mtp_allreduce may allocate its row scratch on first use.
+ * Its scratch is a fixed 4 MiB file-scope device array (1 Mi floats) that every
+ * GPU loading the library holds until process exit, so rows wider than 131072
+ * values are rejected with MTP_ERR_ARG.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress); make that first call before
+ * any stream capture.  All calls share the array and nothing in it needs to
+ * start at zero (each row is written before it is read), but calls that overlap
+ * on the GPU (different streams, different host threads) race on it. */
+int mtp_allreduce_noalloc(int mode, const float *in, float *out, int rows, int cols, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -47,6 +47,7 @@ _SIGS = {
     "mtp_reduce_xproj": [_vp, _i, _vp, _i, _i, _i, _vp, _i, _vp, _vp],
     "mtp_reduce_outproj": [_vp, _i, _vp, _i, _i, _vp, _vp, _vp, _f, _vp, _i, _vp],
     "mtp_allreduce": [_vp, _i, _i, _vp, _vp, _i, _i, _vp],
+    "mtp_allreduce_noalloc": [_i, _vp, _vp, _i, _i, _vp],
 }
 _RESTYPES = {"mtp_version": C.c_char_p, "mtp_last_error": C.c_char_p, "mtp_launch_count": _u64}
 

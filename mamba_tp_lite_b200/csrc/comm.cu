@@ -642,6 +642,45 @@ __global__ void dequant_sum_kernel(const uint8_t *__restrict__ pl, int ws, int r
 static float *g_scratch = nullptr;
 static size_t g_scratch_bytes = 0;
 
+// Fixed row scratch for mtp_allreduce_noalloc: a file-scope device array, so that
+// entry point never allocates.  Every GPU that loads the library holds these
+// 4 MiB until the process exits.  Host code must not hand the symbol itself to a
+// kernel (in host code it only names a host-side stand-in); the device address
+// comes from cudaGetSymbolAddress, looked up once per device.
+constexpr size_t NOALLOC_SCRATCH_FLOATS = (size_t)1 << 20;
+static __device__ __align__(256) float g_noalloc_scratch[NOALLOC_SCRATCH_FLOATS];
+constexpr int NOALLOC_MAX_DEVICES = 64;
+static float *g_noalloc_ptr[NOALLOC_MAX_DEVICES] = {};
+
+// Device address of g_noalloc_scratch on the current device (set up on first use).
+static int noalloc_scratch(float **out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(MTP_ERR_CUDA, "cudaGetDevice failed");
+  if (dev < 0 || dev >= NOALLOC_MAX_DEVICES) return fail(MTP_ERR_UNSUPPORTED, "device index out of range");
+  if (!g_noalloc_ptr[dev]) {
+    void *p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess)
+      return fail(MTP_ERR_CUDA, std::string("cudaGetSymbolAddress(g_noalloc_scratch): ") + cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = static_cast<float *>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return MTP_OK;
+}
+
+// Per-warp row scratch of the reduction kernels.  Grown, never freed: a captured CUDA graph
+// may still hold an older pointer.  The first call (eager, before any capture) sizes it.
+static float *row_scratch(size_t bytes) {
+  if (bytes > g_scratch_bytes) {
+    float *p = nullptr;
+    if (bytes < ((size_t)32 << 20)) bytes = (size_t)32 << 20;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
+    g_scratch = p;
+    g_scratch_bytes = bytes;
+  }
+  return g_scratch;
+}
+
 template <int EPI>
 static int run_reduce(mtp_comm *c, int site, int mode, const float *partial, int rows, int cols, EpiOut e,
                       cudaStream_t s) {
@@ -856,6 +895,31 @@ int mtp_allreduce(mtp_comm *c, int site, int mode, const float *in, float *out, 
   EpiOut e{};
   e.out = out;
   return run_reduce<EPI_PLAIN>(c, site, mode, in, rows, cols, e, (cudaStream_t)stream);
+}
+
+int mtp_allreduce_noalloc(int mode, const float *in, float *out, int rows, int cols, void *stream) {
+  MTP_REQUIRE(in && out && rows >= 0 && cols > 0, "bad arguments");
+  MTP_REQUIRE(mode == MTP_RED_FP32 || mode == MTP_RED_FP16 || mode == MTP_RED_INT8TOK, "unknown reduction mode");
+  MTP_REQUIRE((size_t)cols <= NOALLOC_SCRATCH_FLOATS / WPB,
+              "mtp_allreduce_noalloc: cols exceeds the fixed scratch (at most 131072 values per row)");
+  if (rows == 0) return MTP_OK;
+  float *scr = nullptr;
+  const int rc = noalloc_scratch(&scr);
+  if (rc) return rc;
+  // rows in flight are bounded by the fixed scratch: G CTAs x WPB warps x cols floats
+  int G = ceil_div(rows, WPB);
+  const int sms = num_sms();
+  if (G > sms) G = sms;
+  const int cap = (int)(NOALLOC_SCRATCH_FLOATS / ((size_t)WPB * cols));
+  if (G > cap) G = cap;
+  EpiOut e{};
+  e.out = out;
+  CommDev d{};
+  cudaStream_t s = (cudaStream_t)stream;
+  if (mode == MTP_RED_FP32) reduce_kernel<MTP_RED_FP32, EPI_PLAIN><<<G, WPB * 32, 0, s>>>(d, false, 1, in, rows, cols, false, scr, e);
+  else if (mode == MTP_RED_FP16) reduce_kernel<MTP_RED_FP16, EPI_PLAIN><<<G, WPB * 32, 0, s>>>(d, false, 1, in, rows, cols, false, scr, e);
+  else reduce_kernel<MTP_RED_INT8TOK, EPI_PLAIN><<<G, WPB * 32, 0, s>>>(d, false, 1, in, rows, cols, false, scr, e);
+  return check_launch("allreduce_noalloc");
 }
 
 int mtp_quantize_rows_int8(const float *in, int rows, int cols, int ld, float *scales, int8_t *q, void *stream) {
