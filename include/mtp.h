@@ -48,7 +48,7 @@ enum {
 };
 
 /* GEMM algorithm selector (mtp_gemm_ex).  AUTO picks TCGEN05 for bf16 with
- * M >= 128 and TMA-compatible strides, GEMV for M <= 64, SIMT otherwise. */
+ * M > 16 and TMA-compatible strides, GEMV for M <= 64 otherwise, SIMT for the rest. */
 enum { MTP_GEMM_AUTO = 0, MTP_GEMM_TCGEN05 = 1, MTP_GEMM_SIMT = 2, MTP_GEMM_GEMV = 3 };
 
 const char *mtp_version(void);
@@ -153,14 +153,17 @@ int mtp_comm_status(mtp_comm *c, int *status);
 int mtp_comm_reset_status(mtp_comm *c);
 
 /* AllReduce #1 epilogue (tp_model.py:106-108, :159-161): sum the fp32
- * partial [rows, R+2N] over ranks in `mode`, then split it: dt_low [rows, R]
- * (dt_dtype, input of dt_proj) and bc [rows, 2N] fp32 (scan input). */
+ * partial [rows, R+2N] over ranks in `mode`, round the sums to dt_dtype (the
+ * reference's reduction returns the model dtype, tp_utils.py:42, :131), then
+ * split: dt_low [rows, R] (dt_dtype, input of dt_proj) and bc [rows, 2N] fp32
+ * (scan input). */
 int mtp_reduce_xproj(mtp_comm *c, int mode, const float *partial, int rows, int R, int N2,
                      void *dt_low, int dt_dtype, float *bc, void *stream);
 /* AllReduce #2 epilogue (tp_model.py:131-134 then the block residual
  * tp_model.py:254-257 and the next RMSNorm): out = sum over ranks of the fp32
- * partial [rows, D] (+ bias), resid += out (fp32, in place), and
- * normed = RMSNorm(resid) * norm_w in out_dtype (skipped when normed is NULL). */
+ * partial [rows, D] rounded to out_dtype (the reduction's return dtype) (+ bias),
+ * resid += out (fp32, in place), and normed = RMSNorm(resid) * norm_w in
+ * out_dtype (skipped when normed is NULL). */
 int mtp_reduce_outproj(mtp_comm *c, int mode, const float *partial, int rows, int D, const void *bias,
                        float *resid, const void *norm_w, float eps, void *normed, int out_dtype,
                        void *stream);

@@ -164,22 +164,30 @@ class MixerKernels:
             raise TypeError(f"conv_state dtype {conv_state.dtype} != model dtype {dt_}")
         xz = torch.empty(Bn, 2 * es, device=dev, dtype=dt_)
         self._gemm(xn, self.in_proj.weight, xz, *((L.EPI_BIAS, self.in_proj.bias) if self.in_proj.bias is not None
-                                                  else (L.EPI_STORE, None)))
+                                                  else (L.EPI_STORE, None)), tag="d_in_proj")
         xc = torch.empty(Bn, es, device=dev, dtype=dt_)
+        ev = _prof_begin()
         L.call("mtp_conv1d_silu", L.ptr(xz), 2 * es, L.ptr(self.conv1d.weight), L.ptr(self.conv1d.bias),
                L.ptr(conv_state), L.ptr(xc), es, Bn, 1, es, k, L.dtype_code(dt_), L.stream_ptr())
+        _prof_end(ev, "d_conv", 0)
         partial_x = torch.empty(Bn, r + 2 * n, device=dev, dtype=torch.float32)
-        self._gemm(xc, self.x_proj.weight, partial_x)
+        self._gemm(xc, self.x_proj.weight, partial_x, tag="d_x_proj")
         dt_low = torch.empty(Bn, r, device=dev, dtype=dt_)
         bc = torch.empty(Bn, 2 * n, device=dev, dtype=torch.float32)
+        ev = _prof_begin()
         self._reduce_x(partial_x, dt_low, bc)
+        _prof_end(ev, "d_reduce_x", 0)
         y = torch.empty(Bn, es, device=dev, dtype=dt_)
+        ev = _prof_begin()
         L.call("mtp_step", L.ptr(xz), 2 * es, L.ptr(dt_low), r, L.ptr(self.dt_proj.weight), L.ptr(self.dt_proj.bias),
                L.ptr(bc), 2 * n, L.ptr(self.A_log), L.ptr(self.D), L.ptr(self.conv1d.weight), L.ptr(self.conv1d.bias),
                L.ptr(conv_state), L.ptr(ssm_state), L.ptr(y), es, Bn, es, n, r, k, L.dtype_code(dt_), L.stream_ptr())
+        _prof_end(ev, "d_step", 0)
         partial_o = torch.empty(Bn, cfg.d_model, device=dev, dtype=torch.float32)
-        self._gemm(y, self.out_proj.weight, partial_o)
+        self._gemm(y, self.out_proj.weight, partial_o, tag="d_out_proj")
+        ev = _prof_begin()
         self._reduce_out(partial_o, resid, norm_w, eps, normed)
+        _prof_end(ev, "d_reduce_out", 0)
 
     # ------------------------------------------------------------ reference-shaped API
     def prefill(self, x: torch.Tensor, cache=None):

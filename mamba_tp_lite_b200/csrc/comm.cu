@@ -191,7 +191,14 @@ struct EpiOut {
   void *normed;         // OUTPROJ [rows, D] or NULL
   float eps;
   int out_dtype;        // OUTPROJ: dtype of bias / norm_w / normed
+  int rdt;              // dtype the reduced values are rounded to (the collective's return dtype)
 };
+
+// Round to the collective's return dtype: the reference's reductions return the
+// model dtype (tp_utils.py:42, :131), so a bf16 model sees bf16-rounded sums.
+__device__ __forceinline__ float rnd_rdt(float x, int rdt) {
+  return rdt == MTP_BF16 ? __bfloat162float(__float2bfloat16_rn(x)) : x;
+}
 
 __device__ __forceinline__ float ld_any(const void *p, int dtype, size_t i) {
   return dtype == MTP_F32 ? ((const float *)p)[i] : __bfloat162float(((const __nv_bfloat16 *)p)[i]);
@@ -279,14 +286,13 @@ __global__ void __launch_bounds__(WPB * 32) reduce_kernel(CommDev d, bool has_co
     for (int r = j * WPB + warp; r < rows; r += G * WPB) {
       const float *row = partial + (size_t)r * cols;
       if (MODE == MTP_RED_FP32) {
-        epilogue_row<EPI>(e, row, r, cols, lane);
-        continue;
-      }
-      if (MODE == MTP_RED_FP16) {
-        for (int c = lane; c < cols; c += 32) wrow[c] = __half2float(__float2half_rn(row[c]));
+        for (int c = lane; c < cols; c += 32) wrow[c] = rnd_rdt(row[c], e.rdt);
+      } else if (MODE == MTP_RED_FP16) {
+        for (int c = lane; c < cols; c += 32) wrow[c] = rnd_rdt(__half2float(__float2half_rn(row[c])), e.rdt);
       } else {
         const float sc = row_scale(row_amax(row, cols, lane));
-        for (int c = lane; c < cols; c += 32) wrow[c] = __fadd_rn(0.f, __fmul_rn((float)quant1(row[c], sc), sc));
+        for (int c = lane; c < cols; c += 32)
+          wrow[c] = rnd_rdt(__fadd_rn(0.f, __fmul_rn((float)quant1(row[c], sc), sc)), e.rdt);
       }
       __syncwarp();
       epilogue_row<EPI>(e, wrow, r, cols, lane);
@@ -339,6 +345,8 @@ __global__ void __launch_bounds__(WPB * 32) reduce_kernel(CommDev d, bool has_co
     for (int r = j * WPB + warp; r < rows; r += G * WPB) {
       reduce_row<MODE>(slots, d.ws, r, rows, cols, lane, wrow);
       __syncwarp();
+      for (int c = lane; c < cols; c += 32) wrow[c] = rnd_rdt(wrow[c], e.rdt);
+      __syncwarp();
       epilogue_row<EPI>(e, wrow, r, cols, lane);
       __syncwarp();
     }
@@ -351,6 +359,8 @@ __global__ void __launch_bounds__(WPB * 32) reduce_kernel(CommDev d, bool has_co
     if (r / chunk != d.rank) continue;
     float *mine = gath_local + (size_t)r * cols;
     reduce_row<MODE>(slots, d.ws, r, rows, cols, lane, mine);
+    __syncwarp();
+    for (int c = lane; c < cols; c += 32) mine[c] = rnd_rdt(mine[c], e.rdt);
     __syncwarp();
     for (int k = 1; k < d.ws; ++k) {
       const int dst = (d.rank + k) % d.ws;
@@ -466,6 +476,49 @@ __device__ __forceinline__ void reduce_v(char *const *slots, int nsrc, int r, in
   }
 }
 
+template <int VPL>
+__device__ __forceinline__ void round_v(RowV<VPL> &R, int rdt) {
+  if (rdt != MTP_BF16) return;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i)
+    R.v[i] = make_float4(rnd_rdt(R.v[i].x, rdt), rnd_rdt(R.v[i].y, rdt), rnd_rdt(R.v[i].z, rdt), rnd_rdt(R.v[i].w, rdt));
+}
+
+// gather rows travel in the result dtype: bf16 (8 bytes per 4 values) or fp32
+template <int VPL>
+__device__ __forceinline__ void store_gather_v(char *g, const RowV<VPL> &R, int r, int cols, int lane, int rdt) {
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = (i * 32 + lane) * 4;
+    if (c >= cols) break;
+    if (rdt == MTP_BF16) {
+      __nv_bfloat162 a = __floats2bfloat162_rn(R.v[i].x, R.v[i].y), b = __floats2bfloat162_rn(R.v[i].z, R.v[i].w);
+      uint2 u;
+      u.x = *reinterpret_cast<uint32_t *>(&a);
+      u.y = *reinterpret_cast<uint32_t *>(&b);
+      *reinterpret_cast<uint2 *>(reinterpret_cast<__nv_bfloat16 *>(g) + (size_t)r * cols + c) = u;
+    } else {
+      *reinterpret_cast<float4 *>(reinterpret_cast<float *>(g) + (size_t)r * cols + c) = R.v[i];
+    }
+  }
+}
+template <int VPL>
+__device__ __forceinline__ void load_gather_v(const char *g, RowV<VPL> &R, int r, int cols, int lane, int rdt) {
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = (i * 32 + lane) * 4;
+    if (c >= cols) { R.v[i] = make_float4(0.f, 0.f, 0.f, 0.f); continue; }
+    if (rdt == MTP_BF16) {
+      const uint2 u = __ldcg(reinterpret_cast<const uint2 *>(reinterpret_cast<const __nv_bfloat16 *>(g) + (size_t)r * cols + c));
+      const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.x));
+      const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.y));
+      R.v[i] = make_float4(lo.x, lo.y, hi.x, hi.y);
+    } else {
+      R.v[i] = __ldcg(reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(g) + (size_t)r * cols + c));
+    }
+  }
+}
+
 template <int EPI, int VPL>
 __device__ __forceinline__ void epilogue_v(const EpiOut &e, RowV<VPL> &R, int r, int cols, int lane) {
   if (EPI == EPI_PLAIN) {
@@ -543,6 +596,7 @@ __global__ void __launch_bounds__(WPB * 32) reduce_rows_kernel(CommDev d, bool h
     for (int r = j * WPB + warp; r < rows; r += G * WPB) {
       load_rowv<false>(partial + (size_t)r * cols, cols, lane, R);
       roundtrip_v<MODE>(R);
+      round_v(R, e.rdt);
       epilogue_v<EPI>(e, R, r, cols, lane);
     }
     return;
@@ -586,6 +640,7 @@ __global__ void __launch_bounds__(WPB * 32) reduce_rows_kernel(CommDev d, bool h
   if (!two_shot) {
     for (int r = j * WPB + warp; r < rows; r += G * WPB) {
       reduce_v<MODE>(slots, d.ws, r, rows, cols, lane, R);
+      round_v(R, e.rdt);
       epilogue_v<EPI>(e, R, r, cols, lane);
     }
     finish();
@@ -594,20 +649,14 @@ __global__ void __launch_bounds__(WPB * 32) reduce_rows_kernel(CommDev d, bool h
   for (int r = j * WPB + warp; r < rows; r += G * WPB) {
     if (r / chunk != d.rank) continue;
     reduce_v<MODE>(slots, d.ws, r, rows, cols, lane, R);
-    for (int k = 0; k < d.ws; ++k) {
-      float *o = reinterpret_cast<float *>(d.peer[(d.rank + k) % d.ws] + d.off_gath[site]) + (size_t)r * cols;
-#pragma unroll
-      for (int i = 0; i < VPL; ++i) {
-        const int c = (i * 32 + lane) * 4;
-        if (c < cols) *reinterpret_cast<float4 *>(o + c) = R.v[i];
-      }
-    }
+    round_v(R, e.rdt);
+    for (int k = 0; k < d.ws; ++k) store_gather_v(d.peer[(d.rank + k) % d.ws] + d.off_gath[site], R, r, cols, lane, e.rdt);
   }
   signal(d, site, 1, epoch, all);
   if (!wait_all(d, site, 1, epoch, all, &abort_sm)) { finish(); return; }
-  const float *gath_local = reinterpret_cast<const float *>(d.peer[d.rank] + d.off_gath[site]);
+  const char *gath_local = d.peer[d.rank] + d.off_gath[site];
   for (int r = j * WPB + warp; r < rows; r += G * WPB) {
-    load_rowv<true>(gath_local + (size_t)r * cols, cols, lane, R);
+    load_gather_v(gath_local, R, r, cols, lane, e.rdt);
     epilogue_v<EPI>(e, R, r, cols, lane);
   }
   finish();
@@ -719,8 +768,16 @@ static int run_reduce(mtp_comm *c, int site, int mode, const float *partial, int
     }
     CommDev d{};
     if (has_comm) d = c->d;
-    const size_t wire_bytes = (size_t)nr * cols * 4;
-    bool two_shot = has_comm && c->d.ws > 2 && wire_bytes >= ((size_t)1 << 20);
+    // protocol: fewer bytes sent per rank wins; small messages stay one-shot (one flag round)
+    const size_t wire_row = mode == MTP_RED_FP32 ? 4 * (size_t)cols : mode == MTP_RED_FP16 ? 2 * (size_t)cols : cols + 4;
+    const size_t rdt_row = (e.rdt == MTP_BF16 ? 2 : 4) * (size_t)cols;
+    bool two_shot = false;
+    if (has_comm) {
+      const int ws = c->d.ws;
+      const double one = (double)(ws - 1) * nr * wire_row;
+      const double two = (double)(ws - 1) / ws * nr * (wire_row + rdt_row);
+      two_shot = two < one && (size_t)nr * wire_row >= ((size_t)1 << 20);
+    }
     // protocol override (tests, tuning): MTP_COMM_PROTOCOL=oneshot|twoshot
     if (has_comm) {
       if (const char *env = getenv("MTP_COMM_PROTOCOL")) {
@@ -872,6 +929,7 @@ int mtp_reduce_xproj(mtp_comm *c, int mode, const float *partial, int rows, int 
   e.bc = bc;
   e.R = R;
   e.dt_dtype = dt_dtype;
+  e.rdt = dt_dtype;
   return run_reduce<EPI_XPROJ>(c, 0, mode, partial, rows, R + N2, e, (cudaStream_t)stream);
 }
 
@@ -887,6 +945,7 @@ int mtp_reduce_outproj(mtp_comm *c, int mode, const float *partial, int rows, in
   e.normed = normed;
   e.eps = eps;
   e.out_dtype = out_dtype;
+  e.rdt = out_dtype;
   return run_reduce<EPI_OUTPROJ>(c, 1, mode, partial, rows, D, e, (cudaStream_t)stream);
 }
 
@@ -894,6 +953,7 @@ int mtp_allreduce(mtp_comm *c, int site, int mode, const float *in, float *out, 
   MTP_REQUIRE(out && (site == 0 || site == 1), "bad arguments");
   EpiOut e{};
   e.out = out;
+  e.rdt = MTP_F32;
   return run_reduce<EPI_PLAIN>(c, site, mode, in, rows, cols, e, (cudaStream_t)stream);
 }
 

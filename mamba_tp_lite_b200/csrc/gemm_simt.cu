@@ -180,7 +180,7 @@ int mtp_gemm_ex(const void *A, const void *B, void *C, int M, int N, int K, int 
   if (M == 0) return MTP_OK;
   cudaStream_t s = (cudaStream_t)stream;
   if (algo == MTP_GEMM_AUTO) {
-    if (ab_dtype == MTP_BF16 && M > 64 && gemm_tc_eligible(A, B, M, N, K, lda, ldb)) algo = MTP_GEMM_TCGEN05;
+    if (ab_dtype == MTP_BF16 && M > 16 && gemm_tc_eligible(A, B, M, N, K, lda, ldb)) algo = MTP_GEMM_TCGEN05;
     else if (M <= 64) algo = MTP_GEMM_GEMV;
     else algo = MTP_GEMM_SIMT;
   }

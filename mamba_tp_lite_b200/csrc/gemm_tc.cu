@@ -13,6 +13,7 @@
 // device word, drains its in-flight copies and MMAs with bounded waits, frees TMEM and returns.
 #include <cuda.h>
 #include "common.cuh"
+#include "tc_common.cuh"
 
 namespace mtp {
 namespace tc {
@@ -38,87 +39,6 @@ struct Params {
   int vec_ok;  // 16-byte vector stores allowed
 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n.reg .pred p;\n"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-      "selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait.  Returns false (and raises the CTA abort flag) on timeout, or
-// false immediately once another role has aborted.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort,
-                                          unsigned long long timeout_ns) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer_ns();
-  uint32_t it = 0;
-  while (!mbar_try_wait(bar, parity)) {
-    if ((++it & 255u) == 0) {
-      if (*abort) return false;
-      if (globaltimer_ns() - t0 > timeout_ns) {
-        *abort = 1;
-        return false;
-      }
-    }
-  }
-  return true;
-}
-
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *tm, uint32_t bar, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
-      "l"(tm), "r"(bar), "r"(x), "r"(y)
-      : "memory");
-}
-
-// Shared-memory matrix descriptor: K-major tile, 128-byte swizzle, rows of 64 bf16,
-// 8-row core groups 1024 bytes apart (SBO), descriptor version 1 (sm_100).
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
-  return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                          uint32_t accumulate) {
-  asm volatile(
-      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
-}
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
 __device__ __forceinline__ void tile_coords(const Params &p, int t, int &mt, int &nt) {
   const int gsize = p.group_m * p.tiles_n;
   const int g = t / gsize;
@@ -133,15 +53,32 @@ __device__ __forceinline__ float load_bias(const Params &p, int n) {
   return p.bias_dtype == MTP_F32 ? ((const float *)p.bias)[n] : __bfloat162float(((const __nv_bfloat16 *)p.bias)[n]);
 }
 
+// 16 bias values for columns [n0, n0+16): vector loads when the whole group is in range.
+__device__ __forceinline__ void load_bias16(const Params &p, int n0, float (&b)[16]) {
+  if (p.bias_dtype == MTP_F32 && n0 + 16 <= p.N && (reinterpret_cast<uintptr_t>((const float *)p.bias + n0) & 15) == 0) {
+    const float4 *bp = reinterpret_cast<const float4 *>((const float *)p.bias + n0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 v = __ldg(bp + i);
+      b[4 * i] = v.x; b[4 * i + 1] = v.y; b[4 * i + 2] = v.z; b[4 * i + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) b[i] = (n0 + i < p.N) ? load_bias(p, n0 + i) : 0.f;
+  }
+}
+
 // Apply the epilogue to 16 accumulator columns [n0, n0+16) of row `row` and store.
-__device__ __forceinline__ void epilogue_store(const Params &p, int row, int n0, float (&v)[16]) {
-  if (p.epi != MTP_EPI_STORE) {
+__device__ __forceinline__ void epilogue_store(const Params &p, int row, int n0, float (&v)[16], const float (&b)[16]) {
+  if (p.epi == MTP_EPI_BIAS_SOFTPLUS) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      const int n = n0 + i;
-      const float t = v[i] + (n < p.N ? load_bias(p, n) : 0.f);
-      v[i] = p.epi == MTP_EPI_BIAS_SOFTPLUS ? (t > 20.f ? t : log1pf(__expf(t))) : t;
+      const float t = v[i] + b[i];
+      v[i] = t > 20.f ? t : log1pf(__expf(t));
     }
+  } else if (p.epi == MTP_EPI_BIAS) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] += b[i];
   }
   if (row >= p.M) return;
   const bool full = p.vec_ok && (n0 + 16 <= p.N);
@@ -151,7 +88,9 @@ __device__ __forceinline__ void epilogue_store(const Params &p, int row, int n0,
 #pragma unroll
       for (int i = 0; i < 16; i += 4) *(float4 *)(c + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
     } else {
-      for (int i = 0; i < 16 && n0 + i < p.N; ++i) c[i] = v[i];
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (n0 + i < p.N) c[i] = v[i];
     }
   } else {
     __nv_bfloat16 *c = (__nv_bfloat16 *)p.C + (size_t)row * p.ldc + n0;
@@ -165,7 +104,9 @@ __device__ __forceinline__ void epilogue_store(const Params &p, int row, int n0,
       *(uint4 *)c = make_uint4(w[0], w[1], w[2], w[3]);
       *(uint4 *)(c + 8) = make_uint4(w[4], w[5], w[6], w[7]);
     } else {
-      for (int i = 0; i < 16 && n0 + i < p.N; ++i) c[i] = __float2bfloat16_rn(v[i]);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (n0 + i < p.N) c[i] = __float2bfloat16_rn(v[i]);
     }
   }
 }
@@ -297,10 +238,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int row = mt * BM + q * 32 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN_MAX);
       for (int j = half * 16; j < p.bn; j += 32) {
+        const int n0 = nt * p.bn + j;
+        float b[16];
+        if (p.epi != MTP_EPI_STORE && n0 < p.N) load_bias16(p, n0, b);  // issued before the TMEM read
         float v[16];
         tmem_ld16(tbase + (uint32_t)j, v);
-        const int n0 = nt * p.bn + j;
-        if (n0 < p.N) epilogue_store(p, row, n0, v);
+        if (n0 < p.N) epilogue_store(p, row, n0, v, b);
       }
       tc_fence_before();
       __syncwarp();
@@ -315,38 +258,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 }
 
 // ------------------------------------------------------------------ host side
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
-    void *ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = (EncodeTiledFn)ptr;
-  }
-  return fn;
-}
-
-// 2-D bf16 tensor map over a row-major [rows, cols] matrix with leading dimension ld
-// (elements); box = box_rows x 64 columns, 128-byte swizzle, zero fill out of bounds.
-static int make_tmap(CUtensorMap *tm, const void *ptr, int rows, int cols, int ld, int box_rows) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) return fail(MTP_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(MTP_ERR_ARG, "cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
-  return MTP_OK;
-}
-
 static int *device_err_word() {
   static int *w = nullptr;  // one word per process (single device per process)
   if (!w) {
@@ -383,6 +294,9 @@ int gemm_tc(const void *A, const void *B, void *C, int M, int N, int K, int lda,
   p.epi = epi;
   p.bn = N <= BN_MAX ? ((N + 15) / 16) * 16 : BN_MAX;
   p.tiles_m = ceil_div(M, BM);
+  // few M tiles (small batches): narrower N tiles so the grid still covers the SMs
+  const int sms_avail = num_sms();
+  while (p.bn > 32 && (long)p.tiles_m * ceil_div(N, p.bn) < sms_avail) p.bn = ((p.bn / 2 + 15) / 16) * 16;
   p.tiles_n = ceil_div(N, p.bn);
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.group_m = 32;

@@ -7,6 +7,7 @@
 // restating mamba_lite/tp_model.py:93-129 (prefill) and :145-173 (step).
 #include <cstdlib>
 #include "common.cuh"
+#include "tc_common.cuh"
 
 namespace mtp {
 
@@ -156,15 +157,16 @@ __global__ void conv1d_silu_vec_kernel(const T *__restrict__ xz, int ld_xz, cons
 // ----------------------------------------------------------------- fused prefill scan
 // CTA = 128 threads = (128 / TPC) channels of one sequence b; TPC threads share
 // a channel, each holding N/TPC states in registers.  The sequence is walked in
-// chunks of TL positions; raw x, dt and B|C of the next chunk are staged in
+// chunks of TL positions; raw x, z, dt and B|C of the next chunk are staged in
 // shared memory by cp.async while the current one is processed.  Per chunk:
 //   phase A  conv1d + SiLU of the TL positions (independent of the state: ILP)
 //   phase B  the recurrence over the TL positions
-//   phase C  coalesced store y = (C.h + D.xc) * silu(z), z read straight from global.
+//   phase C  coalesced store y = (C.h + D.xc) * silu(z).
 template <typename T, int N, int TPC, int TL>
 struct ScanSmem {
   static constexpr int CB = 128 / TPC;
   T x[2][TL][CB];
+  T z[2][TL][CB];
   float dt[2][TL][CB];
   float bc[2][TL][2 * N];
   float y[TL][CB];
@@ -226,8 +228,10 @@ __global__ void __launch_bounds__(128, (TPC == 1 ? 4 : 6)) scan_prefill_kernel(
       constexpr int XW = CB * (int)sizeof(T) / 16, DW = CB * 4 / 16, BW = 2 * N * 4 / 16;
       for (int i = threadIdx.x; i < tl * XW; i += NT) {
         const int tt = i / XW, w = i % XW;
-        cp_async16(reinterpret_cast<char *>(&sm.x[buf][tt][0]) + 16 * w,
-                   reinterpret_cast<const char *>(xz + (row0 + t0 + tt) * ld_xz + c0) + 16 * w);
+        const T *src = xz + (row0 + t0 + tt) * ld_xz + c0;
+        cp_async16(reinterpret_cast<char *>(&sm.x[buf][tt][0]) + 16 * w, reinterpret_cast<const char *>(src) + 16 * w);
+        cp_async16(reinterpret_cast<char *>(&sm.z[buf][tt][0]) + 16 * w,
+                   reinterpret_cast<const char *>(src + Es) + 16 * w);
       }
       for (int i = threadIdx.x; i < tl * DW; i += NT) {
         const int tt = i / DW, w = i % DW;
@@ -243,6 +247,7 @@ __global__ void __launch_bounds__(128, (TPC == 1 ? 4 : 6)) scan_prefill_kernel(
       for (int i = threadIdx.x; i < tl * wpr; i += NT) {
         const int tt = i / wpr, wi = i % wpr;
         cp_async4(&sm.x[buf][tt][wi * EPW], xz + (row0 + t0 + tt) * ld_xz + c0 + wi * EPW);
+        cp_async4(&sm.z[buf][tt][wi * EPW], xz + (row0 + t0 + tt) * ld_xz + Es + c0 + wi * EPW);
       }
       for (int i = threadIdx.x; i < tl * ncb; i += NT) {
         const int tt = i / ncb, ci = i % ncb;
@@ -319,8 +324,7 @@ __global__ void __launch_bounds__(128, (TPC == 1 ? 4 : 6)) scan_prefill_kernel(
     for (int i = threadIdx.x; i < tl * ncb; i += NT) {
       const int tt = i / ncb, ci = i % ncb;
       const size_t r = row0 + t0 + tt;
-      const float zv = ldf(xz + r * ld_xz + Es + c0 + ci);
-      stf(y + r * ld_y + c0 + ci, sm.y[tt][ci] * silu_fast(zv));
+      stf(y + r * ld_y + c0 + ci, sm.y[tt][ci] * silu_fast(ldf(&sm.z[buf][tt][ci])));
     }
     __syncthreads();
   }
@@ -332,6 +336,273 @@ __global__ void __launch_bounds__(128, (TPC == 1 ? 4 : 6)) scan_prefill_kernel(
       for (int j = 0; j < K - 1; ++j) stf(conv_final + ((size_t)b * Es + c) * (K - 1) + j, win[j]);
     }
   }
+}
+
+// ----------------------------------------------------------------- fused dt_proj + scan (bf16)
+// The scan above with dt_proj (+ bias + softplus) computed inside the kernel on
+// the tensor cores: per chunk of TL positions, D[128 channels x TL positions] =
+// W_dt[c0:c0+128, :R] . dt_low[rows, :R]^T as tcgen05.mma (M=128, N=TL, K=16 per
+// instruction), operands staged by TMA with 128-byte swizzle, fp32 accumulators
+// double-buffered in TMEM.  TMEM lane i holds channel c0+i, so tcgen05.ld 32x32b
+// gives each thread its own channel's dt for the chunk.  Thread 0 issues the TMA
+// loads (two chunks ahead) and the MMA of chunk k+1 while chunk k is scanned.
+// Every mbarrier wait is bounded; a timeout sets a device status word and all
+// threads leave the chunk loop together.
+template <int TL, int KA>
+struct FusedSmem {
+  uint8_t w[KA][128 * 128];     // W_dt tile: 128 rows x 64 columns per atom (1024-aligned)
+  uint8_t dl[2][KA][TL * 128];  // dt_low tiles of two chunks
+  __nv_bfloat16 x[2][TL][128];
+  __nv_bfloat16 z[2][TL][128];
+  float bc[2][TL][32];
+  float y[TL][128];
+  uint64_t bar_w, bar_dl[2], bar_mma[2];
+  uint32_t tmem;
+  int abort;
+};
+
+template <int TL, int KA, int K>
+__global__ void __launch_bounds__(128, 3) scan_fused_kernel(
+    const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_dl,
+    const __nv_bfloat16 *__restrict__ xz, int ld_xz, const __nv_bfloat16 *__restrict__ b_dt,
+    const float *__restrict__ bcp, int ld_bc, const __nv_bfloat16 *__restrict__ A_log,
+    const __nv_bfloat16 *__restrict__ Dp, const __nv_bfloat16 *__restrict__ conv_w,
+    const __nv_bfloat16 *__restrict__ conv_b, const __nv_bfloat16 *conv_init, const float *ssm_init,
+    __nv_bfloat16 *__restrict__ y, int ld_y, __nv_bfloat16 *conv_final, float *ssm_final, int L, int Es, int *err,
+    unsigned long long timeout_ns) {
+  using namespace tc;
+  constexpr int N = 16, CB = 128, NT = 128;
+  using S = FusedSmem<TL, KA>;
+  extern __shared__ __align__(1024) unsigned char smem_dyn[];
+  const uint32_t raw = smem_u32(smem_dyn);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  S &sm = *reinterpret_cast<S *>(smem_dyn + (base - raw));
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int b = blockIdx.y, c0 = blockIdx.x * CB, c = c0 + tid;
+  const size_t row0 = (size_t)b * L;
+  const int nchunks = (L + TL - 1) / TL;
+  constexpr uint32_t W_BYTES = KA * 128 * 128, DL_BYTES = KA * TL * 128;
+  const uint32_t idesc = idesc_bf16(128, TL);
+  volatile int *abort = &sm.abort;
+
+  if (tid == 0) {
+    mbar_init(smem_u32(&sm.bar_w), 1);
+    for (int j = 0; j < 2; ++j) {
+      mbar_init(smem_u32(&sm.bar_dl[j]), 1);
+      mbar_init(smem_u32(&sm.bar_mma[j]), 1);
+    }
+    sm.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sm.tmem)), "r"(32));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem;
+
+  auto issue_dl = [&](int chunk, int bufi) {  // thread 0
+    mbar_expect_tx(smem_u32(&sm.bar_dl[bufi]), DL_BYTES);
+    for (int a = 0; a < KA; ++a)
+      tma_load_2d(smem_u32(&sm.dl[bufi][a][0]), &tm_dl, smem_u32(&sm.bar_dl[bufi]), 64 * a, (int)(row0 + chunk * TL));
+  };
+  auto issue_mma = [&](int bufi) {  // thread 0, after the chunk's dt_low landed
+    const uint32_t d = tmem + (uint32_t)(bufi * TL);
+    for (int a = 0; a < KA; ++a) {
+      const uint64_t ad = sw128_desc(smem_u32(&sm.w[a][0])), bd = sw128_desc(smem_u32(&sm.dl[bufi][a][0]));
+#pragma unroll
+      for (int k = 0; k < 4; ++k) umma_bf16(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (a | k) != 0);
+    }
+    umma_commit(smem_u32(&sm.bar_mma[bufi]));
+  };
+
+  if (tid == 0) {
+    mbar_expect_tx(smem_u32(&sm.bar_w), W_BYTES);
+    for (int a = 0; a < KA; ++a) tma_load_2d(smem_u32(&sm.w[a][0]), &tm_w, smem_u32(&sm.bar_w), 64 * a, c0);
+    issue_dl(0, 0);
+    if (nchunks > 1) issue_dl(1, 1);
+    if (mbar_wait(smem_u32(&sm.bar_w), 0, abort, timeout_ns) && mbar_wait(smem_u32(&sm.bar_dl[0]), 0, abort, timeout_ns)) {
+      tc_fence_after();
+      issue_mma(0);
+    } else {
+      *abort = 1;
+    }
+  }
+
+  // per-thread constants
+  float A2[N], h[N], wk[K], win[K - 1];
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    A2[i] = -expf(__bfloat162float(A_log[(size_t)c * N + i])) * kLog2e;
+    h[i] = ssm_init ? ssm_init[((size_t)b * Es + c) * N + i] : 0.f;
+  }
+#pragma unroll
+  for (int j = 0; j < K; ++j) wk[j] = __bfloat162float(conv_w[(size_t)c * K + j]);
+#pragma unroll
+  for (int j = 0; j < K - 1; ++j) win[j] = conv_init ? __bfloat162float(conv_init[((size_t)b * Es + c) * (K - 1) + j]) : 0.f;
+  const float Dv = __bfloat162float(Dp[c]);
+  const float cbias = conv_b ? __bfloat162float(conv_b[c]) : 0.f;
+  const float bdt = __bfloat162float(b_dt[c]);
+
+  auto load_chunk = [&](int k, int bufi) {
+    const int t0 = k * TL;
+    const int tl = min(TL, L - t0);
+    constexpr int XW = CB * 2 / 16, BW = 2 * N * 4 / 16;
+    for (int i = tid; i < tl * XW; i += NT) {
+      const int tt = i / XW, w = i % XW;
+      const __nv_bfloat16 *src = xz + (row0 + t0 + tt) * ld_xz + c0;
+      cp_async16(reinterpret_cast<char *>(&sm.x[bufi][tt][0]) + 16 * w, reinterpret_cast<const char *>(src) + 16 * w);
+      cp_async16(reinterpret_cast<char *>(&sm.z[bufi][tt][0]) + 16 * w, reinterpret_cast<const char *>(src + Es) + 16 * w);
+    }
+    for (int i = tid; i < tl * BW; i += NT) {
+      const int tt = i / BW, w = i % BW;
+      cp_async16(&sm.bc[bufi][tt][4 * w], bcp + (row0 + t0 + tt) * ld_bc + 4 * w);
+    }
+    cp_async_commit();
+  };
+
+  load_chunk(0, 0);
+  for (int k = 0; k < nchunks; ++k) {
+    const int buf = k & 1;
+    if (k + 1 < nchunks) {
+      load_chunk(k + 1, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    // dt of this chunk from TMEM
+    if (!mbar_wait(smem_u32(&sm.bar_mma[buf]), (uint32_t)((k >> 1) & 1), abort, timeout_ns)) *abort = 1;
+    __syncthreads();
+    if (*abort) break;
+    tc_fence_after();
+    float dts[TL];
+    tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(buf * TL), dts);
+    if (tid == 0) {
+      // the MMA of chunk k read dl[buf]: refill it two chunks ahead, then start chunk k+1's MMA
+      if (k + 2 < nchunks) issue_dl(k + 2, buf);
+      if (k + 1 < nchunks) {
+        if (mbar_wait(smem_u32(&sm.bar_dl[buf ^ 1]), (uint32_t)(((k + 1) >> 1) & 1), abort, timeout_ns)) {
+          tc_fence_after();
+          issue_mma(buf ^ 1);
+        } else {
+          *abort = 1;
+        }
+      }
+    }
+#pragma unroll
+    for (int tt = 0; tt < TL; ++tt) {
+      const float t = dts[tt] + bdt;
+      dts[tt] = t > 20.f ? t : log1pf(__expf(t));
+    }
+    const int t0 = k * TL;
+    const int tl = min(TL, L - t0);
+    float xcs[TL];
+#pragma unroll
+    for (int tt = 0; tt < TL; ++tt) {
+      if (tt < tl) {
+        const float xv = __bfloat162float(sm.x[buf][tt][tid]);
+        float acc = cbias;
+#pragma unroll
+        for (int j = 0; j < K - 1; ++j) acc = fmaf(wk[j], win[j], acc);
+        acc = fmaf(wk[K - 1], xv, acc);
+#pragma unroll
+        for (int j = 0; j < K - 2; ++j) win[j] = win[j + 1];
+        win[K - 2] = xv;
+        xcs[tt] = silu_fast(acc);
+      }
+    }
+#pragma unroll
+    for (int tt = 0; tt < TL; ++tt) {
+      if (tt < tl) {
+        const float dt = dts[tt];
+        const float dtx = dt * xcs[tt];
+        const float4 *bv = reinterpret_cast<const float4 *>(&sm.bc[buf][tt][0]);
+        const float4 *cv = reinterpret_cast<const float4 *>(&sm.bc[buf][tt][N]);
+        float ya[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int q = 0; q < N / 4; ++q) {
+          const float4 B4 = bv[q], C4 = cv[q];
+          const float Bs[4] = {B4.x, B4.y, B4.z, B4.w}, Cs[4] = {C4.x, C4.y, C4.z, C4.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int i = 4 * q + u;
+            const float dA = ex2_hw(dt * A2[i]);
+            h[i] = fmaf(dA, h[i], Bs[u] * dtx);
+            ya[u] = fmaf(Cs[u], h[i], ya[u]);
+          }
+        }
+        sm.y[tt][tid] = fmaf(Dv, xcs[tt], (ya[0] + ya[1]) + (ya[2] + ya[3]));
+      }
+    }
+    __syncthreads();
+    for (int i = tid; i < tl * CB; i += NT) {
+      const int tt = i / CB, ci = i % CB;
+      const size_t r = row0 + t0 + tt;
+      y[r * ld_y + c0 + ci] = __float2bfloat16_rn(sm.y[tt][ci] * silu_fast(__bfloat162float(sm.z[buf][tt][ci])));
+    }
+    tc_fence_before();
+    __syncthreads();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (*abort) {
+    if (tid == 0) {
+      atomicExch(err, MTP_ERR_TIMEOUT);
+      const unsigned long long t0 = globaltimer_ns();  // let copies / MMAs in flight finish
+      while (globaltimer_ns() - t0 < 1000000ull) {}
+    }
+    __syncthreads();
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) ssm_final[((size_t)b * Es + c) * N + i] = h[i];
+#pragma unroll
+    for (int j = 0; j < K - 1; ++j) conv_final[((size_t)b * Es + c) * (K - 1) + j] = __float2bfloat16_rn(win[j]);
+  }
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(32));
+}
+
+static int *scan_err_word() {
+  static int *w = nullptr;
+  if (!w) {
+    if (cudaMalloc(&w, sizeof(int)) != cudaSuccess) return nullptr;
+    cudaMemset(w, 0, sizeof(int));
+  }
+  return w;
+}
+
+template <int KA>
+static int launch_scan_fused(const void *xz, int ld_xz, const void *dt_low, int ld_dl, const void *W_dt,
+                             const void *b_dt, const float *bc, int ld_bc, const void *A_log, const void *Dp,
+                             const void *conv_w, const void *conv_b, const void *conv_init, const float *ssm_init,
+                             void *y, int ld_y, void *conv_final, float *ssm_final, int B, int L, int Es, int R,
+                             cudaStream_t s) {
+  constexpr int TL = 16, K = 4;
+  using S = FusedSmem<TL, KA>;
+  const int smem = (int)sizeof(S) + 1024;
+  auto kern = scan_fused_kernel<TL, KA, K>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return check_launch("scan_fused attr");
+    attr_set = true;
+  }
+  CUtensorMap tw, td;
+  int rc = tc::make_tmap(&tw, W_dt, Es, R, R, 128);
+  if (rc) return rc;
+  rc = tc::make_tmap(&td, dt_low, B * L, R, ld_dl, TL);
+  if (rc) return rc;
+  int *err = scan_err_word();
+  if (!err) return fail(MTP_ERR_CUDA, "could not allocate the scan status word");
+  dim3 grid(Es / 128, B);
+  kern<<<grid, 128, smem, s>>>(tw, td, (const __nv_bfloat16 *)xz, ld_xz, (const __nv_bfloat16 *)b_dt, bc, ld_bc,
+                               (const __nv_bfloat16 *)A_log, (const __nv_bfloat16 *)Dp, (const __nv_bfloat16 *)conv_w,
+                               (const __nv_bfloat16 *)conv_b, (const __nv_bfloat16 *)conv_init, ssm_init,
+                               (__nv_bfloat16 *)y, ld_y, (__nv_bfloat16 *)conv_final, ssm_final, L, Es, err,
+                               2000000000ull);
+  return check_launch("scan_fused");
 }
 
 // ----------------------------------------------------------------- single-token step
@@ -515,6 +786,41 @@ int mtp_scan_prefill(const void *xz, int ld_xz, const float *dt, int ld_dt, cons
   }
 #undef MTP_SCAN_CASE
   return fail(MTP_ERR_UNSUPPORTED, "scan_prefill: dtype must be F32 or BF16");
+}
+
+int mtp_scan_prefill_fused(const void *xz, int ld_xz, const void *dt_low, int ld_dl, const void *W_dt,
+                           const void *b_dt, const float *bc, int ld_bc, const void *A_log, const void *Dp,
+                           const void *conv_w, const void *conv_b, const void *conv_init, const float *ssm_init,
+                           void *y, int ld_y, void *conv_final, float *ssm_final, int B, int L, int Es, int N, int R,
+                           int K, void *stream) {
+  MTP_REQUIRE(xz && dt_low && W_dt && b_dt && bc && A_log && Dp && conv_w && y && conv_final && ssm_final,
+              "null pointer");
+  MTP_REQUIRE(B >= 0 && L >= 0 && Es > 0 && R > 0, "bad sizes");
+  MTP_REQUIRE(K == 4 && N == 16, "the fused scan is built for d_conv 4, d_state 16");
+  MTP_REQUIRE(Es % 128 == 0, "the fused scan needs d_inner per rank divisible by 128");
+  MTP_REQUIRE(R % 8 == 0 && R <= 256 && ld_dl % 8 == 0 && ld_dl >= R, "dt_rank must be a multiple of 8, at most 256");
+  MTP_REQUIRE(aligned16(xz) && aligned16(dt_low) && aligned16(W_dt) && aligned16(bc) && ld_xz % 8 == 0 && ld_bc % 4 == 0 &&
+                  ld_bc >= 2 * N && ld_xz >= 2 * Es && ld_y >= Es,
+              "fused scan needs 16-byte aligned rows");
+  if (B == 0 || L == 0) return MTP_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int ka = (R + 63) / 64;
+#define MTP_FS(KA_)                                                                                          \
+  return launch_scan_fused<KA_>(xz, ld_xz, dt_low, ld_dl, W_dt, b_dt, bc, ld_bc, A_log, Dp, conv_w, conv_b, \
+                                conv_init, ssm_init, y, ld_y, conv_final, ssm_final, B, L, Es, R, s)
+  if (ka == 1) MTP_FS(1);
+  if (ka == 2) MTP_FS(2);
+  if (ka == 3) MTP_FS(3);
+  MTP_FS(4);
+#undef MTP_FS
+}
+
+int mtp_scan_status(int *status) {
+  MTP_REQUIRE(status, "null argument");
+  int *w = scan_err_word();
+  if (!w) return fail(MTP_ERR_CUDA, "no status word");
+  if (cudaMemcpy(status, w, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return fail(MTP_ERR_CUDA, "read status");
+  return MTP_OK;
 }
 
 int mtp_step(const void *xz, int ld_xz, const void *dt_low, int ld_dl, const void *W_dt, const void *b_dt,

@@ -53,10 +53,12 @@ def bench_gemm(a):
     odt = torch.bfloat16 if a.out == "bf16" else torch.float32
     C = torch.empty(M, N, device="cuda", dtype=odt)
     algo = {"tc": L.GEMM_TCGEN05, "simt": L.GEMM_SIMT, "gemv": L.GEMM_GEMV, "auto": L.GEMM_AUTO}[a.algo]
+    epi = {"store": L.EPI_STORE, "softplus": L.EPI_BIAS_SOFTPLUS, "bias": L.EPI_BIAS}[a.epi]
+    bias = torch.randn(N, device="cuda") - 3 if epi != L.EPI_STORE else None
 
     def run():
-        L.call("mtp_gemm_ex", L.ptr(A), L.ptr(W), L.ptr(C), M, N, K, K, K, N, L.BF16, L.dtype_code(odt), L.EPI_STORE,
-               None, 0, algo, L.stream_ptr())
+        L.call("mtp_gemm_ex", L.ptr(A), L.ptr(W), L.ptr(C), M, N, K, K, K, N, L.BF16, L.dtype_code(odt), epi,
+               L.ptr(bias), L.F32, algo, L.stream_ptr())
 
     ms = _time(run, a.warmup, a.iters)
     tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
@@ -198,6 +200,13 @@ def bench_decode(a):
     _, cache = m.prefill(ids)
     nid = torch.zeros(a.batch, 1, dtype=torch.long, device="cuda")
     eager_ms = _time(lambda: m.step(nid, cache), a.warmup, a.iters)
+    # per-launch device time of one eager step (events around each launch)
+    from . import _mixer
+    _mixer.PROFILE = {}
+    m.step(nid, cache)
+    torch.cuda.synchronize()
+    prof, _mixer.PROFILE = _mixer.PROFILE, None
+    per_kernel = {k: sum(s.elapsed_time(e) for s, e, _ in v) * 1e3 / cfg.n_layer for k, v in prof.items()}
     st = GraphedStepper(m, cache, a.batch, "cuda")
     st.capture()
     graph_ms = _time(lambda: st.replay(nid), a.warmup, a.iters)
@@ -205,6 +214,7 @@ def bench_decode(a):
     w_bytes = sum(p.numel() * p.element_size() for p in m.parameters())
     return {"kernel": "decode_step", "shape": a.shape, "layers": cfg.n_layer, "batch": a.batch,
             "eager_ms": eager_ms, "graphed_ms": graph_ms, "weight_bytes": w_bytes,
+            "us_per_layer_by_kernel_eager": per_kernel,
             "hbm_floor_ms": w_bytes / (peaks()["hbm_gbs"] * 1e9) * 1e3}
 
 
@@ -218,6 +228,7 @@ def main():
     g.add_argument("--out", choices=["bf16", "f32"], default="bf16")
     g.add_argument("--algo", choices=["tc", "simt", "gemv", "auto"], default="tc")
     g.add_argument("--check", action="store_true")
+    g.add_argument("--epi", choices=["store", "softplus", "bias"], default="store")
     s = sub.add_parser("scan")
     s.add_argument("--batch", type=int, default=32)
     s.add_argument("--seqlen", type=int, default=1024)
