@@ -98,6 +98,22 @@ int mtp_scan_prefill(const void *xz, int ld_xz, const float *dt, int ld_dt, cons
                      const void *conv_init, const float *ssm_init, void *y, int ld_y, void *conv_final,
                      float *ssm_final, int B, int L, int Es, int N, int K, int dtype, void *stream);
 
+/* The fused prefill above with dt_proj folded in (bf16 models): dt = softplus(
+ * dt_low . W_dt^T + b_dt) is computed inside the kernel on the tensor cores
+ * (tcgen05.mma, TMEM accumulators) instead of being read from memory.
+ * dt_low [B*L, ld_dl] bf16 (R values per row), W_dt [Es, R] bf16, b_dt [Es] bf16;
+ * other arguments as mtp_scan_prefill (all bf16 except bc / ssm states).  Needs
+ * d_state 16, Es % 128 == 0, R % 8 == 0 and R <= 256.  Replaces
+ * tp_model.py:110-129 (model.py:216-238).  A bounded internal wait that expires
+ * sets the status read by mtp_scan_status. */
+int mtp_scan_prefill_fused(const void *xz, int ld_xz, const void *dt_low, int ld_dl, const void *W_dt,
+                           const void *b_dt, const float *bc, int ld_bc, const void *A_log, const void *Dp,
+                           const void *conv_w, const void *conv_b, const void *conv_init, const float *ssm_init,
+                           void *y, int ld_y, void *conv_final, float *ssm_final, int B, int L, int Es, int N, int R,
+                           int K, void *stream);
+/* Device status of the fused scan (0, or MTP_ERR_TIMEOUT after an expired wait). */
+int mtp_scan_status(int *status);
+
 /* Single-token recurrent step, in place: conv history shift, SiLU, dt_proj
  * (dt_low . W_dt^T + b) and softplus, state update, y = C.h + D.x, SiLU(z) gate.
  * xz [B, ld_xz]; dt_low [B, ld_dl] (R values, dtype) ; W_dt [Es,R], b_dt [Es];

@@ -31,6 +31,9 @@ _SIGS = {
     "mtp_conv1d_silu": [_vp, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp],
     "mtp_scan_prefill": [_vp, _i, _vp, _i, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _vp,
                          _i, _i, _i, _i, _i, _i, _vp],
+    "mtp_scan_prefill_fused": [_vp, _i, _vp, _i, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp,
+                               _vp, _i, _i, _i, _i, _i, _i, _vp],
+    "mtp_scan_status": [C.POINTER(_i)],
     "mtp_step": [_vp, _i, _vp, _i, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,
                  _i, _i, _i, _i, _i, _i, _vp],
     "mtp_embedding": [_vp, _i, _vp, _i, _i, _vp, _vp],

@@ -21,6 +21,8 @@ partials, dt, B, C and the SSM state are fp32.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from . import _lib as L
@@ -109,6 +111,15 @@ class MixerKernels:
         L.call("mtp_reduce_outproj", ctx, mode, L.ptr(partial), rows, d, L.ptr(bias), L.ptr(resid), L.ptr(norm_w),
                float(eps), L.ptr(normed), L.dtype_code(odt), L.stream_ptr())
 
+    def _fused_dt_ok(self) -> bool:
+        """The fused dt_proj + scan kernel (opt-in, MTP_FUSED_DT=1): bf16 models
+        with d_state 16, d_inner per rank divisible by 128 and dt_rank divisible
+        by 8.  Off by default: on B200 the separate dt_proj GEMM plus the scan is
+        faster at the 1.4b prefill shape (191k vs 180k tok/s)."""
+        cfg = self.cfg
+        return (self._dt() == torch.bfloat16 and cfg.d_state == 16 and cfg.d_conv == 4 and self.es % 128 == 0
+                and cfg.dt_rank % 8 == 0 and cfg.dt_rank <= 256 and os.environ.get("MTP_FUSED_DT", "0") == "1")
+
     # ------------------------------------------------------------ prefill core
     def _prefill_core(self, xn, B, Lq, conv_init, ssm_init, resid, norm_w=None, eps=0.0, normed=None):
         """xn [T, D] (model dtype, RMS-normed block input).  Adds the mixer
@@ -132,17 +143,29 @@ class MixerKernels:
         dt_low = torch.empty(T, r, device=dev, dtype=dt_)
         bc = torch.empty(T, 2 * n, device=dev, dtype=torch.float32)
         self._reduce_x(partial_x, dt_low, bc)
-        dt = torch.empty(T, es, device=dev, dtype=torch.float32)
-        self._gemm(dt_low, self.dt_proj.weight, dt, L.EPI_BIAS_SOFTPLUS, self.dt_proj.bias, tag="dt_proj")
         y = torch.empty(T, es, device=dev, dtype=dt_)
         conv_final = torch.empty(B, es, k - 1, device=dev, dtype=dt_)
         ssm_final = torch.empty(B, es, n, device=dev, dtype=torch.float32)
+        esz = xz.element_size()
+        if self._fused_dt_ok():
+            # dt_proj + softplus inside the scan kernel (tensor cores); no dt round trip
+            ev = _prof_begin()
+            L.call("mtp_scan_prefill_fused", L.ptr(xz), 2 * es, L.ptr(dt_low), r, L.ptr(self.dt_proj.weight),
+                   L.ptr(self.dt_proj.bias), L.ptr(bc), 2 * n, L.ptr(self.A_log), L.ptr(self.D), L.ptr(conv_w),
+                   L.ptr(conv_b), L.ptr(conv_init), L.ptr(ssm_init), L.ptr(y), es, L.ptr(conv_final),
+                   L.ptr(ssm_final), B, Lq, es, n, r, k, L.stream_ptr())
+            _prof_end(ev, "scan", T * (es * 3 * esz + (r + 2 * n) * 4) + B * es * (2 * n * 4 + 2 * (k - 1) * esz))
+            partial_o = torch.empty(T, cfg.d_model, device=dev, dtype=torch.float32)
+            self._gemm(y, self.out_proj.weight, partial_o, tag="out_proj")
+            self._reduce_out(partial_o, resid, norm_w, eps, normed)
+            return conv_final, ssm_final
+        dt = torch.empty(T, es, device=dev, dtype=torch.float32)
+        self._gemm(dt_low, self.dt_proj.weight, dt, L.EPI_BIAS_SOFTPLUS, self.dt_proj.bias, tag="dt_proj")
         ev = _prof_begin()
         L.call("mtp_scan_prefill", L.ptr(xz), 2 * es, L.ptr(dt), es, L.ptr(bc), 2 * n, L.ptr(self.A_log), L.ptr(self.D),
                L.ptr(conv_w), L.ptr(conv_b), L.ptr(conv_init), L.ptr(ssm_init), L.ptr(y), es, L.ptr(conv_final),
                L.ptr(ssm_final), B, Lq, es, n, k, L.dtype_code(dt_), L.stream_ptr())
         # algorithmic bytes: x, z, y in the model dtype, dt fp32, B|C fp32 (+ per-sequence state I/O)
-        esz = xz.element_size()
         _prof_end(ev, "scan", T * (es * (3 * esz + 4) + 2 * n * 4) + B * es * (2 * n * 4 + 2 * (k - 1) * esz))
         partial_o = torch.empty(T, cfg.d_model, device=dev, dtype=torch.float32)
         self._gemm(y, self.out_proj.weight, partial_o, tag="out_proj")

@@ -24,32 +24,11 @@
 #include <cstring>
 #include <vector>
 #include "common.cuh"
+#include "comm_dev.cuh"
 
 namespace mtp {
 
-constexpr int MAX_WS = 8;
-constexpr int G_MAX = 256;
 constexpr int WPB = 8;  // warps (rows in flight) per CTA
-
-struct CommDev {
-  char *peer[MAX_WS];  // base of each rank's allocation (peer[rank] = own)
-  size_t off_flags, off_epoch, off_done, off_status, off_recv[2], off_gath[2], slot_bytes[2];
-  int rank, ws;
-  unsigned long long timeout_ns;
-};
-
-}  // namespace mtp
-
-struct mtp_comm {
-  mtp::CommDev d;
-  char *base = nullptr;
-  size_t total = 0;
-  int max_rows = 0, cols[2] = {0, 0};
-  bool opened = false;
-  cudaIpcMemHandle_t handle;
-};
-
-namespace mtp {
 
 // ----------------------------------------------------------------- device helpers
 __device__ __forceinline__ float warp_max(float v) {
@@ -239,9 +218,6 @@ __device__ __forceinline__ void epilogue_row(const EpiOut &e, const float *val, 
 }
 
 // ----------------------------------------------------------------- flags
-__device__ __forceinline__ uint32_t *flag_ptr(char *base, const CommDev &d, int site, int phase, int src, int j) {
-  return reinterpret_cast<uint32_t *>(base + d.off_flags) + (((size_t)(site * 2 + phase) * MAX_WS + src) * G_MAX + j);
-}
 
 // Signal phase `phase` of CTA j to `targets` (bitmask of ranks), after all threads' stores.
 __device__ __forceinline__ void signal(const CommDev &d, int site, int phase, uint32_t epoch, uint32_t targets) {
@@ -276,6 +252,8 @@ __device__ __forceinline__ bool wait_all(const CommDev &d, int site, int phase, 
 template <int MODE, int EPI>
 __global__ void __launch_bounds__(WPB * 32) reduce_kernel(CommDev d, bool has_comm, int site, const float *__restrict__ partial,
                                                           int rows, int cols, bool two_shot, float *scratch, EpiOut e) {
+  MTP_PDL_WAIT();
+  MTP_PDL_TRIGGER();
   __shared__ int abort_sm;
   __shared__ uint32_t epoch_sm;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -587,6 +565,8 @@ template <int MODE, int EPI, int VPL>
 __global__ void __launch_bounds__(WPB * 32) reduce_rows_kernel(CommDev d, bool has_comm, int site,
                                                                const float *__restrict__ partial, int rows, int cols,
                                                                bool two_shot, EpiOut e) {
+  MTP_PDL_WAIT();
+  MTP_PDL_TRIGGER();
   __shared__ int abort_sm;
   __shared__ uint32_t epoch_sm;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -664,6 +644,8 @@ __global__ void __launch_bounds__(WPB * 32) reduce_rows_kernel(CommDev d, bool h
 
 // ----------------------------------------------------------------- standalone quantiser / dequant
 __global__ void quantize_rows_kernel(const float *__restrict__ in, int rows, int cols, int ld, float *scales, int8_t *q) {
+  MTP_PDL_WAIT();
+  MTP_PDL_TRIGGER();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= rows) return;
   const float *row = in + (size_t)warp * ld;
@@ -673,6 +655,8 @@ __global__ void quantize_rows_kernel(const float *__restrict__ in, int rows, int
 }
 
 __global__ void dequant_sum_kernel(const uint8_t *__restrict__ pl, int ws, int rows, int cols, float *out) {
+  MTP_PDL_WAIT();
+  MTP_PDL_TRIGGER();
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (size_t)rows * cols) return;
   const int r = (int)(i / cols);
@@ -792,7 +776,7 @@ static int run_reduce(mtp_comm *c, int site, int mode, const float *partial, int
       int Gv = ceil_div(nr, WPB);
       const int cap = has_comm ? (sms < G_MAX ? sms : G_MAX) : sms * 8;
       if (Gv > cap) Gv = cap;
-#define MTP_RV(M, V) reduce_rows_kernel<M, EPI, V><<<Gv, WPB * 32, 0, s>>>(d, has_comm, site, pp, nr, cols, two_shot, ee)
+#define MTP_RV(M, V) launch_pdl(reduce_rows_kernel<M, EPI, V>, dim3(Gv), dim3(WPB * 32), 0, s, d, has_comm, site, pp, nr, cols, two_shot, ee)
 #define MTP_RV_MODE(V)                                      \
   do {                                                      \
     if (mode == MTP_RED_FP32) MTP_RV(MTP_RED_FP32, V);      \
@@ -810,7 +794,7 @@ static int run_reduce(mtp_comm *c, int site, int mode, const float *partial, int
 #undef MTP_RV
     } else {
 #define MTP_RED_LAUNCH(M) \
-  reduce_kernel<M, EPI><<<G, WPB * 32, 0, s>>>(d, has_comm, site, pp, nr, cols, two_shot, scr, ee)
+  launch_pdl(reduce_kernel<M, EPI>, dim3(G), dim3(WPB * 32), 0, s, d, has_comm, site, pp, nr, cols, two_shot, scr, ee)
       if (mode == MTP_RED_FP32) MTP_RED_LAUNCH(MTP_RED_FP32);
       else if (mode == MTP_RED_FP16) MTP_RED_LAUNCH(MTP_RED_FP16);
       else MTP_RED_LAUNCH(MTP_RED_INT8TOK);
@@ -976,16 +960,16 @@ int mtp_allreduce_noalloc(int mode, const float *in, float *out, int rows, int c
   e.out = out;
   CommDev d{};
   cudaStream_t s = (cudaStream_t)stream;
-  if (mode == MTP_RED_FP32) reduce_kernel<MTP_RED_FP32, EPI_PLAIN><<<G, WPB * 32, 0, s>>>(d, false, 1, in, rows, cols, false, scr, e);
-  else if (mode == MTP_RED_FP16) reduce_kernel<MTP_RED_FP16, EPI_PLAIN><<<G, WPB * 32, 0, s>>>(d, false, 1, in, rows, cols, false, scr, e);
-  else reduce_kernel<MTP_RED_INT8TOK, EPI_PLAIN><<<G, WPB * 32, 0, s>>>(d, false, 1, in, rows, cols, false, scr, e);
+  if (mode == MTP_RED_FP32) launch_pdl(reduce_kernel<MTP_RED_FP32, EPI_PLAIN>, dim3(G), dim3(WPB * 32), 0, s, d, false, 1, in, rows, cols, false, scr, e);
+  else if (mode == MTP_RED_FP16) launch_pdl(reduce_kernel<MTP_RED_FP16, EPI_PLAIN>, dim3(G), dim3(WPB * 32), 0, s, d, false, 1, in, rows, cols, false, scr, e);
+  else launch_pdl(reduce_kernel<MTP_RED_INT8TOK, EPI_PLAIN>, dim3(G), dim3(WPB * 32), 0, s, d, false, 1, in, rows, cols, false, scr, e);
   return check_launch("allreduce_noalloc");
 }
 
 int mtp_quantize_rows_int8(const float *in, int rows, int cols, int ld, float *scales, int8_t *q, void *stream) {
   MTP_REQUIRE(in && scales && q && rows >= 0 && cols > 0 && ld >= cols, "bad arguments");
   if (rows == 0) return MTP_OK;
-  quantize_rows_kernel<<<ceil_div(rows, 8), 256, 0, (cudaStream_t)stream>>>(in, rows, cols, ld, scales, q);
+  launch_pdl(quantize_rows_kernel, dim3(ceil_div(rows, 8)), dim3(256), 0, (cudaStream_t)stream, in, rows, cols, ld, scales, q);
   return check_launch("quantize_rows_int8");
 }
 
@@ -993,7 +977,7 @@ int mtp_dequant_sum(const uint8_t *payloads, int ws, int rows, int cols, float *
   MTP_REQUIRE(payloads && out && ws >= 1 && rows >= 0 && cols > 0, "bad arguments");
   if (rows == 0) return MTP_OK;
   const size_t n = (size_t)rows * cols;
-  dequant_sum_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(payloads, ws, rows, cols, out);
+  launch_pdl(dequant_sum_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, (cudaStream_t)stream, payloads, ws, rows, cols, out);
   return check_launch("dequant_sum");
 }
 

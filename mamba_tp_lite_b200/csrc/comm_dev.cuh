@@ -1,0 +1,38 @@
+// Layout of a comm context (one cudaMalloc per rank, mapped by its peers over CUDA IPC),
+// shared by the reduction kernels (comm.cu) and the persistent decode kernel (decode.cu).
+//   flags   u32 [site 2][phase 2][src MAX_WS][G_MAX]   value = epoch of the last push
+//   epoch   u32 [site 2]                              last completed epoch per site
+//   done    u32 [site 2]                              CTA exit counter of a reduction launch
+//   status  int                                        MTP_OK or MTP_ERR_TIMEOUT
+//   recv[s] 2 halves (epoch parity) x ws slots of slot_bytes[s]: the wire rows pushed by each rank
+//   gath[s] max_rows x cols[s] fp32: reduced rows of the two-shot protocol
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mtp {
+
+constexpr int MAX_WS = 8;
+constexpr int G_MAX = 256;
+
+struct CommDev {
+  char *peer[MAX_WS];  // base of each rank's allocation (peer[rank] = own)
+  size_t off_flags, off_epoch, off_done, off_status, off_recv[2], off_gath[2], slot_bytes[2];
+  int rank, ws;
+  unsigned long long timeout_ns;
+};
+
+__device__ __forceinline__ uint32_t *flag_ptr(char *base, const CommDev &d, int site, int phase, int src, int j) {
+  return reinterpret_cast<uint32_t *>(base + d.off_flags) + (((size_t)(site * 2 + phase) * MAX_WS + src) * G_MAX + j);
+}
+
+}  // namespace mtp
+
+struct mtp_comm {
+  mtp::CommDev d;
+  char *base = nullptr;
+  size_t total = 0;
+  int max_rows = 0, cols[2] = {0, 0};
+  bool opened = false;
+  cudaIpcMemHandle_t handle;
+};

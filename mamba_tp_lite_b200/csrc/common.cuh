@@ -50,6 +50,18 @@ template <typename T> __device__ __forceinline__ void stf(T *p, float v) { Elem<
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 __device__ __forceinline__ float softplus_f(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
 
+// softplus(x) = max(x, 0) + log1p(exp(-|x|)), torch's threshold 20.  log1p(u) for
+// u in (0, 1] by Goldberg's identity log1p(u) = log(1+u) * u / ((1+u) - 1), which
+// keeps the relative accuracy of the hardware logarithm for small u.
+__device__ __forceinline__ float softplus_fast(float x) {
+  if (x > 20.f) return x;
+  const float u = __expf(-fabsf(x));
+  const float w = 1.0f + u;
+  const float l = (w == 1.0f) ? u : __logf(w) * __fdividef(u, w - 1.0f);
+  return fmaxf(x, 0.f) + l;
+}
+
+
 // ----------------------------------------------------------------- timing / waits
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
@@ -64,6 +76,34 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
 }
 __device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// ----------------------------------------------------------------- programmatic dependent launch
+// Every kernel of the library is launched with programmatic stream serialization
+// allowed, so the next kernel's launch and prologue overlap the tail of the
+// current one.  Each kernel therefore executes MTP_PDL_WAIT() before its first
+// global-memory access (it returns once the previous kernel has completed and
+// its writes are visible) and MTP_PDL_TRIGGER() to let its dependent launch.
+// Without a programmatic predecessor both are no-ops.  MTP_PDL=0 turns it off.
+#define MTP_PDL_WAIT() asm volatile("griddepcontrol.wait;" ::: "memory")
+#define MTP_PDL_TRIGGER() asm volatile("griddepcontrol.launch_dependents;" ::: "memory")
+
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
 // dispatch on a runtime dtype code

@@ -31,6 +31,8 @@ __device__ __forceinline__ void epi_store(const EpiArgs &e, int m, int n, float 
 template <typename T>
 __global__ void __launch_bounds__(256) gemm_simt_kernel(const T *__restrict__ A, const T *__restrict__ B, int M, int N,
                                                         int K, int lda, int ldb, EpiArgs e) {
+  MTP_PDL_WAIT();
+  MTP_PDL_TRIGGER();
   __shared__ float As[16][68];
   __shared__ float Bs[16][68];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -100,6 +102,8 @@ __device__ __forceinline__ void load8(const T *p, int k, int K, bool vec, float 
 template <typename T, int MT, int ROWS>
 __global__ void __launch_bounds__(256) gemv_kernel(const T *__restrict__ X, int ldx, const T *__restrict__ W, int ldw,
                                                    int M, int N, int K, bool vec, EpiArgs e) {
+  MTP_PDL_WAIT();
+  MTP_PDL_TRIGGER();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_base = (blockIdx.x * (blockDim.x >> 5) + warp) * ROWS;
   const int m0 = blockIdx.y * MT;
@@ -109,25 +113,34 @@ __global__ void __launch_bounds__(256) gemv_kernel(const T *__restrict__ X, int 
   for (int r = 0; r < ROWS; ++r)
 #pragma unroll
     for (int m = 0; m < MT; ++m) acc[r][m] = 0.f;
-  for (int k = lane * 8; k < K; k += 256) {
-    float w[ROWS][8];
+  constexpr int U = MT <= 2 ? 4 : 1;  // k-steps of weight loads in flight per lane
+  for (int k0 = lane * 8; k0 < K; k0 += 256 * U) {
+    float w[U][ROWS][8];
 #pragma unroll
-    for (int r = 0; r < ROWS; ++r) {
-      if (n_base + r < N) load8(W + (size_t)(n_base + r) * ldw, k, K, vec, w[r]);
-      else {
+    for (int u = 0; u < U; ++u)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) w[r][i] = 0.f;
+      for (int r = 0; r < ROWS; ++r) {
+        const int k = k0 + 256 * u;
+        if (n_base + r < N && k < K) load8(W + (size_t)(n_base + r) * ldw, k, K, vec, w[u][r]);
+        else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) w[u][r][i] = 0.f;
+        }
       }
-    }
 #pragma unroll
-    for (int m = 0; m < MT; ++m) {
-      if (m0 + m >= M) break;
-      float x[8];
-      load8(X + (size_t)(m0 + m) * ldx, k, K, vec, x);
+    for (int u = 0; u < U; ++u) {
+      const int k = k0 + 256 * u;
+      if (k >= K) break;
 #pragma unroll
-      for (int r = 0; r < ROWS; ++r)
+      for (int m = 0; m < MT; ++m) {
+        if (m0 + m >= M) break;
+        float x[8];
+        load8(X + (size_t)(m0 + m) * ldx, k, K, vec, x);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[r][m] = fmaf(w[r][i], x[i], acc[r][m]);
+        for (int r = 0; r < ROWS; ++r)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[r][m] = fmaf(w[u][r][i], x[i], acc[r][m]);
+      }
     }
   }
 #pragma unroll
@@ -148,16 +161,91 @@ __global__ void __launch_bounds__(256) gemv_kernel(const T *__restrict__ X, int 
   }
 }
 
+// Block-split-K GEMV for small N: a CTA of 256 threads owns RB output rows and
+// all MT tokens; its threads stride over K (8 elements each, 16-byte loads, U
+// loads in flight), then the partial sums are reduced across the 8 warps in
+// shared memory in a fixed order.
+template <typename T, int MT, int RB>
+__global__ void __launch_bounds__(256) gemv_splitk_kernel(const T *__restrict__ X, int ldx, const T *__restrict__ W,
+                                                          int ldw, int M, int N, int K, bool vec, EpiArgs e) {
+  MTP_PDL_WAIT();
+  MTP_PDL_TRIGGER();
+  __shared__ float red[8][RB][MT];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * RB, m0 = blockIdx.y * MT;
+  float acc[RB][MT];
+#pragma unroll
+  for (int r = 0; r < RB; ++r)
+#pragma unroll
+    for (int m = 0; m < MT; ++m) acc[r][m] = 0.f;
+  constexpr int U = 2;
+  for (int k0 = threadIdx.x * 8; k0 < K; k0 += 2048 * U) {
+    float w[U][RB][8];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+      for (int r = 0; r < RB; ++r) {
+        const int k = k0 + 2048 * u;
+        if (n0 + r < N && k < K) load8(W + (size_t)(n0 + r) * ldw, k, K, vec, w[u][r]);
+        else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) w[u][r][i] = 0.f;
+        }
+      }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int k = k0 + 2048 * u;
+      if (k >= K) break;
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        if (m0 + m >= M) break;
+        float x[8];
+        load8(X + (size_t)(m0 + m) * ldx, k, K, vec, x);
+#pragma unroll
+        for (int r = 0; r < RB; ++r)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[r][m] = fmaf(w[u][r][i], x[i], acc[r][m]);
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < RB; ++r)
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      float v = acc[r][m];
+#pragma unroll
+      for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) red[warp][r][m] = v;
+    }
+  __syncthreads();
+  if (threadIdx.x < RB * MT) {
+    const int r = threadIdx.x / MT, m = threadIdx.x % MT;
+    float v = 0.f;
+#pragma unroll
+    for (int wi = 0; wi < 8; ++wi) v += red[wi][r][m];
+    if (n0 + r < N && m0 + m < M) epi_store(e, m0 + m, n0 + r, v);
+  }
+}
+
 template <typename T>
 static int launch_gemv(const T *X, int ldx, const T *W, int ldw, int M, int N, int K, EpiArgs e, cudaStream_t s) {
   constexpr int ROWS = 2;
   const bool vec = aligned16(X) && aligned16(W) && (ldx % 8 == 0) && (ldw % 8 == 0);
+  if (N <= 4096 && K >= 512 && M <= 8) {  // small N: every CTA splits K over its 256 threads
+    constexpr int RB = 2;
+    dim3 g(ceil_div(N, RB));
+    if (M <= 1) launch_pdl(gemv_splitk_kernel<T, 1, RB>, dim3(g), dim3(256), 0, s, X, ldx, W, ldw, M, N, K, vec, e);
+    else if (M <= 2) launch_pdl(gemv_splitk_kernel<T, 2, RB>, dim3(g), dim3(256), 0, s, X, ldx, W, ldw, M, N, K, vec, e);
+    else if (M <= 4) launch_pdl(gemv_splitk_kernel<T, 4, RB>, dim3(g), dim3(256), 0, s, X, ldx, W, ldw, M, N, K, vec, e);
+    else launch_pdl(gemv_splitk_kernel<T, 8, RB>, dim3(g), dim3(256), 0, s, X, ldx, W, ldw, M, N, K, vec, e);
+    return check_launch("gemv_splitk");
+  }
   const int rows_per_block = 8 * ROWS;
   dim3 grid(ceil_div(N, rows_per_block));
-  if (M <= 1) { grid.y = 1; gemv_kernel<T, 1, ROWS><<<grid, 256, 0, s>>>(X, ldx, W, ldw, M, N, K, vec, e); }
-  else if (M <= 2) { grid.y = 1; gemv_kernel<T, 2, ROWS><<<grid, 256, 0, s>>>(X, ldx, W, ldw, M, N, K, vec, e); }
-  else if (M <= 4) { grid.y = 1; gemv_kernel<T, 4, ROWS><<<grid, 256, 0, s>>>(X, ldx, W, ldw, M, N, K, vec, e); }
-  else { grid.y = ceil_div(M, 8); gemv_kernel<T, 8, ROWS><<<grid, 256, 0, s>>>(X, ldx, W, ldw, M, N, K, vec, e); }
+  if (M <= 1) { grid.y = 1; launch_pdl(gemv_kernel<T, 1, ROWS>, dim3(grid), dim3(256), 0, s, X, ldx, W, ldw, M, N, K, vec, e); }
+  else if (M <= 2) { grid.y = 1; launch_pdl(gemv_kernel<T, 2, ROWS>, dim3(grid), dim3(256), 0, s, X, ldx, W, ldw, M, N, K, vec, e); }
+  else if (M <= 4) { grid.y = 1; launch_pdl(gemv_kernel<T, 4, ROWS>, dim3(grid), dim3(256), 0, s, X, ldx, W, ldw, M, N, K, vec, e); }
+  else { grid.y = ceil_div(M, 8); launch_pdl(gemv_kernel<T, 8, ROWS>, dim3(grid), dim3(256), 0, s, X, ldx, W, ldw, M, N, K, vec, e); }
   return check_launch("gemv");
 }
 
@@ -196,9 +284,9 @@ int mtp_gemm_ex(const void *A, const void *B, void *C, int M, int N, int K, int 
   if (algo == MTP_GEMM_SIMT) {
     dim3 grid(ceil_div(N, 64), ceil_div(M, 64));
     if (ab_dtype == MTP_F32)
-      gemm_simt_kernel<float><<<grid, 256, 0, s>>>((const float *)A, (const float *)B, M, N, K, lda, ldb, e);
+      launch_pdl(gemm_simt_kernel<float>, dim3(grid), dim3(256), 0, s, (const float *)A, (const float *)B, M, N, K, lda, ldb, e);
     else
-      gemm_simt_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16 *)A, (const __nv_bfloat16 *)B, M, N,
+      launch_pdl(gemm_simt_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, s, (const __nv_bfloat16 *)A, (const __nv_bfloat16 *)B, M, N,
                                                            K, lda, ldb, e);
     return check_launch("gemm_simt");
   }

@@ -73,8 +73,7 @@ __device__ __forceinline__ void epilogue_store(const Params &p, int row, int n0,
   if (p.epi == MTP_EPI_BIAS_SOFTPLUS) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      const float t = v[i] + b[i];
-      v[i] = t > 20.f ? t : log1pf(__expf(t));
+      v[i] = softplus_fast(v[i] + b[i]);
     }
   } else if (p.epi == MTP_EPI_BIAS) {
 #pragma unroll
@@ -151,6 +150,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  MTP_PDL_WAIT();  // barrier init and TMEM allocation above overlap the previous kernel
+  MTP_PDL_TRIGGER();
   const uint32_t tmem_base = *tmem_holder;
   const int num_kb = (p.K + BK - 1) / BK;
   const uint32_t tx_bytes = (uint32_t)(A_BYTES + p.bn * BK * 2);
@@ -317,7 +318,7 @@ int gemm_tc(const void *A, const void *B, void *C, int M, int N, int K, int lda,
     attr = true;
   }
   const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
-  gemm_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, p);
+  launch_pdl(gemm_tc_kernel, dim3(grid), dim3(NUM_THREADS), SMEM_BYTES, stream, ta, tb, p);
   return check_launch("gemm_tc");
 }
 

@@ -1,5 +1,6 @@
 // Host error plumbing, embedding gather, RMSNorm, row argmax.
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 #include "common.cuh"
 
@@ -22,6 +23,15 @@ int check_launch(const char *what) {
   return MTP_OK;
 }
 
+bool pdl_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char *e = getenv("MTP_PDL");
+    on = (e && e[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
 int num_sms() {
   int dev = 0, n = 0;
   cudaGetDevice(&dev);
@@ -33,6 +43,8 @@ int num_sms() {
 template <typename T>
 __global__ void embedding_kernel(const int64_t *__restrict__ ids, const T *__restrict__ table, int D,
                                  float *__restrict__ out) {
+  MTP_PDL_WAIT();
+  MTP_PDL_TRIGGER();
   const int t = blockIdx.x;
   const T *row = table + (size_t)ids[t] * D;
   for (int i = threadIdx.x; i < D; i += blockDim.x) out[(size_t)t * D + i] = ldf(row + i);
@@ -52,6 +64,8 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
 template <typename TW, typename TO>
 __global__ void rmsnorm_kernel(const float *__restrict__ x, int D, const TW *__restrict__ w, float eps,
                                TO *__restrict__ out) {
+  MTP_PDL_WAIT();
+  MTP_PDL_TRIGGER();
   __shared__ float red[32];
   const float *row = x + (size_t)blockIdx.x * D;
   float ss = 0.f;
@@ -64,6 +78,8 @@ __global__ void rmsnorm_kernel(const float *__restrict__ x, int D, const TW *__r
 
 template <typename T>
 __global__ void argmax_kernel(const T *__restrict__ logits, int V, int ld, int64_t *__restrict__ out) {
+  MTP_PDL_WAIT();
+  MTP_PDL_TRIGGER();
   __shared__ float bv[32];
   __shared__ int bi[32];
   const T *row = logits + (size_t)blockIdx.x * ld;
@@ -102,7 +118,7 @@ int mtp_embedding(const int64_t *ids, int T, const void *table, int D, int dtype
   MTP_REQUIRE(T >= 0 && D > 0 && ids && table && out, "bad arguments");
   if (T == 0) return MTP_OK;
   cudaStream_t s = (cudaStream_t)stream;
-  MTP_DISPATCH_FB(dtype, TT, embedding_kernel<TT><<<T, 256, 0, s>>>(ids, (const TT *)table, D, out));
+  MTP_DISPATCH_FB(dtype, TT, launch_pdl(embedding_kernel<TT>, dim3(T), dim3(256), 0, s, ids, (const TT *)table, D, out));
   return check_launch("embedding");
 }
 
@@ -112,7 +128,7 @@ int mtp_rmsnorm(const float *x, int T, int D, const void *w, int w_dtype, float 
   if (T == 0) return MTP_OK;
   cudaStream_t s = (cudaStream_t)stream;
   MTP_DISPATCH_FB(w_dtype, TW, MTP_DISPATCH_FB(out_dtype, TO,
-      rmsnorm_kernel<TW, TO><<<T, 256, 0, s>>>(x, D, (const TW *)w, eps, (TO *)out)));
+      launch_pdl(rmsnorm_kernel<TW, TO>, dim3(T), dim3(256), 0, s, x, D, (const TW *)w, eps, (TO *)out)));
   return check_launch("rmsnorm");
 }
 
@@ -120,7 +136,7 @@ int mtp_argmax_rows(const void *logits, int T, int V, int ld, int dtype, int64_t
   MTP_REQUIRE(T >= 0 && V > 0 && ld >= V && logits && out, "bad arguments");
   if (T == 0) return MTP_OK;
   cudaStream_t s = (cudaStream_t)stream;
-  MTP_DISPATCH_FB(dtype, TT, argmax_kernel<TT><<<T, 512, 0, s>>>((const TT *)logits, V, ld, out));
+  MTP_DISPATCH_FB(dtype, TT, launch_pdl(argmax_kernel<TT>, dim3(T), dim3(512), 0, s, (const TT *)logits, V, ld, out));
   return check_launch("argmax");
 }
 

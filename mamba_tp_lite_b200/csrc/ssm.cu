@@ -36,6 +36,8 @@ template <typename T, int K, int TT>
 __global__ void conv1d_silu_kernel(const T *__restrict__ xz, int ld_xz, const T *__restrict__ w,
                                    const T *__restrict__ bias, const T *__restrict__ hist, T *__restrict__ xc,
                                    int ld_xc, int L, int Es) {
+  MTP_PDL_WAIT();
+  MTP_PDL_TRIGGER();
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   const int t0 = blockIdx.y * TT;
   const int b = blockIdx.z;
@@ -108,6 +110,8 @@ template <typename T, int K, int TT>
 __global__ void conv1d_silu_vec_kernel(const T *__restrict__ xz, int ld_xz, const T *__restrict__ w,
                                        const T *__restrict__ bias, const T *__restrict__ hist, T *__restrict__ xc,
                                        int ld_xc, int L, int Es) {
+  MTP_PDL_WAIT();
+  MTP_PDL_TRIGGER();
   constexpr int V = Pack16<T>::V;
   const int c = (blockIdx.x * blockDim.x + threadIdx.x) * V;
   const int t0 = blockIdx.y * TT;
@@ -160,8 +164,8 @@ __global__ void conv1d_silu_vec_kernel(const T *__restrict__ xz, int ld_xz, cons
 // chunks of TL positions; raw x, z, dt and B|C of the next chunk are staged in
 // shared memory by cp.async while the current one is processed.  Per chunk:
 //   phase A  conv1d + SiLU of the TL positions (independent of the state: ILP)
-//   phase B  the recurrence over the TL positions
-//   phase C  coalesced store y = (C.h + D.xc) * silu(z).
+//   phase B  the recurrence over the TL positions, storing y = (C.h + D.xc) * silu(z)
+//            (a warp writes 32 consecutive channels of a position).
 template <typename T, int N, int TPC, int TL>
 struct ScanSmem {
   static constexpr int CB = 128 / TPC;
@@ -169,7 +173,6 @@ struct ScanSmem {
   T z[2][TL][CB];
   float dt[2][TL][CB];
   float bc[2][TL][2 * N];
-  float y[TL][CB];
 };
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
@@ -180,12 +183,15 @@ __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
 // silu with the hardware exponential and a fast divide (x / (1 + e^-x))
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
+
 template <typename T, int N, int TPC, int TL, int K>
 __global__ void __launch_bounds__(128, (TPC == 1 ? 4 : 6)) scan_prefill_kernel(
     const T *__restrict__ xz, int ld_xz, const float *__restrict__ dtp, int ld_dt, const float *__restrict__ bcp,
     int ld_bc, const T *__restrict__ A_log, const T *__restrict__ Dp, const T *__restrict__ conv_w,
     const T *__restrict__ conv_b, const T *conv_init, const float *ssm_init, T *__restrict__ y, int ld_y,
     T *conv_final, float *ssm_final, int L, int Es, bool vec16) {
+  MTP_PDL_WAIT();
+  MTP_PDL_TRIGGER();
   using S = ScanSmem<T, N, TPC, TL>;
   constexpr int CB = S::CB;
   constexpr int NS = N / TPC;
@@ -316,16 +322,11 @@ __global__ void __launch_bounds__(128, (TPC == 1 ? 4 : 6)) scan_prefill_kernel(
         float yv = (ya[0] + ya[1]) + (ya[2] + ya[3]);
 #pragma unroll
         for (int o = 1; o < TPC; o <<= 1) yv += __shfl_xor_sync(0xffffffffu, yv, o);
-        if (sub == 0) sm.y[tt][cl] = fmaf(Dv, xcs[tt], yv);
+        if (sub == 0 && live)
+          stf(y + (row0 + t0 + tt) * ld_y + c, fmaf(Dv, xcs[tt], yv) * silu_fast(ldf(&sm.z[buf][tt][cl])));
       }
     }
-    __syncthreads();
-    // phase C: gate with silu(z) and store
-    for (int i = threadIdx.x; i < tl * ncb; i += NT) {
-      const int tt = i / ncb, ci = i % ncb;
-      const size_t r = row0 + t0 + tt;
-      stf(y + r * ld_y + c0 + ci, sm.y[tt][ci] * silu_fast(ldf(&sm.z[buf][tt][ci])));
-    }
+    // buffer `buf` is refilled by the next iteration's prefetch only after this barrier
     __syncthreads();
   }
   if (live) {
@@ -355,14 +356,13 @@ struct FusedSmem {
   __nv_bfloat16 x[2][TL][128];
   __nv_bfloat16 z[2][TL][128];
   float bc[2][TL][32];
-  float y[TL][128];
   uint64_t bar_w, bar_dl[2], bar_mma[2];
   uint32_t tmem;
   int abort;
 };
 
 template <int TL, int KA, int K>
-__global__ void __launch_bounds__(128, 3) scan_fused_kernel(
+__global__ void __launch_bounds__(128, 4) scan_fused_kernel(
     const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_dl,
     const __nv_bfloat16 *__restrict__ xz, int ld_xz, const __nv_bfloat16 *__restrict__ b_dt,
     const float *__restrict__ bcp, int ld_bc, const __nv_bfloat16 *__restrict__ A_log,
@@ -401,6 +401,8 @@ __global__ void __launch_bounds__(128, 3) scan_fused_kernel(
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  MTP_PDL_WAIT();  // barrier init and TMEM allocation above overlap the previous kernel
+  MTP_PDL_TRIGGER();
   const uint32_t tmem = sm.tmem;
 
   auto issue_dl = [&](int chunk, int bufi) {  // thread 0
@@ -492,10 +494,7 @@ __global__ void __launch_bounds__(128, 3) scan_fused_kernel(
       }
     }
 #pragma unroll
-    for (int tt = 0; tt < TL; ++tt) {
-      const float t = dts[tt] + bdt;
-      dts[tt] = t > 20.f ? t : log1pf(__expf(t));
-    }
+    for (int tt = 0; tt < TL; ++tt) dts[tt] = softplus_fast(dts[tt] + bdt);
     const int t0 = k * TL;
     const int tl = min(TL, L - t0);
     float xcs[TL];
@@ -533,14 +532,9 @@ __global__ void __launch_bounds__(128, 3) scan_fused_kernel(
             ya[u] = fmaf(Cs[u], h[i], ya[u]);
           }
         }
-        sm.y[tt][tid] = fmaf(Dv, xcs[tt], (ya[0] + ya[1]) + (ya[2] + ya[3]));
+        const float yv = fmaf(Dv, xcs[tt], (ya[0] + ya[1]) + (ya[2] + ya[3]));
+        y[(row0 + t0 + tt) * ld_y + c] = __float2bfloat16_rn(yv * silu_fast(__bfloat162float(sm.z[buf][tt][tid])));
       }
-    }
-    __syncthreads();
-    for (int i = tid; i < tl * CB; i += NT) {
-      const int tt = i / CB, ci = i % CB;
-      const size_t r = row0 + t0 + tt;
-      y[r * ld_y + c0 + ci] = __float2bfloat16_rn(sm.y[tt][ci] * silu_fast(__bfloat162float(sm.z[buf][tt][ci])));
     }
     tc_fence_before();
     __syncthreads();
@@ -597,7 +591,7 @@ static int launch_scan_fused(const void *xz, int ld_xz, const void *dt_low, int 
   int *err = scan_err_word();
   if (!err) return fail(MTP_ERR_CUDA, "could not allocate the scan status word");
   dim3 grid(Es / 128, B);
-  kern<<<grid, 128, smem, s>>>(tw, td, (const __nv_bfloat16 *)xz, ld_xz, (const __nv_bfloat16 *)b_dt, bc, ld_bc,
+  launch_pdl(kern, dim3(grid), dim3(128), smem, s, tw, td, (const __nv_bfloat16 *)xz, ld_xz, (const __nv_bfloat16 *)b_dt, bc, ld_bc,
                                (const __nv_bfloat16 *)A_log, (const __nv_bfloat16 *)Dp, (const __nv_bfloat16 *)conv_w,
                                (const __nv_bfloat16 *)conv_b, (const __nv_bfloat16 *)conv_init, ssm_init,
                                (__nv_bfloat16 *)y, ld_y, (__nv_bfloat16 *)conv_final, ssm_final, L, Es, err,
@@ -606,91 +600,87 @@ static int launch_scan_fused(const void *xz, int ld_xz, const void *dt_low, int 
 }
 
 // ----------------------------------------------------------------- single-token step
-// CTA = CB channels x all B sequences, 256 threads.
-//   phase 0  A * log2(e) of the block's channels into shared memory
-//   phase 1  dt_proj + bias + softplus: one warp per (b, c) pair at a time, lanes
-//            split the dt_rank contraction, shuffle reduction; dt into shared memory
-//   phase 2  N/4 threads per (b, c), 4 states each: conv over [history | x], conv
-//            history shift (one thread), state update in place (float4), C.h reduced
-//            over the 4 threads, D skip and SiLU(z) gate.
-template <typename T, int N, int K, int CB>
+// CTA = 32 channels x BB sequences, one thread per (sequence, channel) holding
+// all N states.  The block's dt_proj rows are staged transposed in shared memory
+// ([R][33]: conflict-free across the 32 channels of a warp) with the BB dt_low
+// vectors and A * log2(e); each thread then does its dt_proj dot product,
+// softplus, the conv over [history | x] with the history shift, the state
+// update (float4), C.h, the D skip and the SiLU(z) gate, all in place.
+template <typename T, int N, int K>
 __global__ void __launch_bounds__(256) step_kernel(const T *__restrict__ xz, int ld_xz, const T *__restrict__ dt_low,
                                                    int ld_dl, const T *__restrict__ W_dt, const T *__restrict__ b_dt,
                                                    const float *__restrict__ bcp, int ld_bc, const T *__restrict__ A_log,
                                                    const T *__restrict__ Dp, const T *__restrict__ conv_w,
                                                    const T *__restrict__ conv_b, T *conv_state, float *ssm_state,
-                                                   T *__restrict__ y, int ld_y, int B, int Es, int R) {
-  constexpr int NS = 4, TPG = N / NS;  // 4 states per thread
+                                                   T *__restrict__ y, int ld_y, int B, int Es, int R, int BB) {
+  MTP_PDL_WAIT();
+  MTP_PDL_TRIGGER();
+  constexpr int CB = 32;
   extern __shared__ __align__(16) float ssm_sm[];
-  float *a2s = ssm_sm;            // [CB][N]
-  float *dts = ssm_sm + CB * N;   // [B][CB]
-  const int c0 = blockIdx.x * CB;
-  const int ncb = min(CB, Es - c0);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // staging uses all 256 threads; the first 32 x BB threads then own one (sequence, channel) each
+  float *wt = ssm_sm;                   // [R][CB + 1]
+  float *dls = wt + R * (CB + 1);       // [BB][R]
+  float *a2s = dls + BB * R;            // [CB][N]
+  const int c0 = blockIdx.x * CB, b0 = blockIdx.y * BB;
+  const int ncb = min(CB, Es - c0), nbb = min(BB, B - b0);
+  for (int i = threadIdx.x; i < ncb * R; i += blockDim.x) {
+    const int cc = i / R, r = i % R;
+    wt[r * (CB + 1) + cc] = ldf(W_dt + (size_t)(c0 + cc) * R + r);
+  }
+  for (int i = threadIdx.x; i < nbb * R; i += blockDim.x) {
+    const int bb = i / R, r = i % R;
+    dls[bb * R + r] = ldf(dt_low + (size_t)(b0 + bb) * ld_dl + r);
+  }
   for (int i = threadIdx.x; i < ncb * N; i += blockDim.x)
     a2s[i] = -expf(ldf(A_log + (size_t)c0 * N + i)) * kLog2e;
-  for (int p = warp; p < B * ncb; p += blockDim.x >> 5) {
-    const int bb = p / ncb, cc = p % ncb;
-    const T *wr = W_dt + (size_t)(c0 + cc) * R;
-    const T *xr = dt_low + (size_t)bb * ld_dl;
-    float sacc = 0.f;
-    for (int r = lane; r < R; r += 32) sacc = fmaf(ldf(xr + r), ldf(wr + r), sacc);
-    for (int o = 16; o; o >>= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, o);
-    if (lane == 0) dts[bb * CB + cc] = softplus_f(sacc + ldf(b_dt + c0 + cc));
-  }
   __syncthreads();
-  // phase 2: groups of TPG consecutive threads; whole warps iterate together so the
-  // group shuffles always have all 32 lanes present
-  const int items = B * ncb * TPG;
-  const int iters = (items + blockDim.x - 1) / blockDim.x;
-  for (int it = 0; it < iters; ++it) {
-    const int idx = it * blockDim.x + threadIdx.x;
-    const bool act = idx < items;
-    const int g = act ? idx / TPG : 0, sub = idx % TPG;
-    const int bb = g / ncb, cc = g % ncb, c = c0 + cc;
-    float xc = 0.f, zv = 0.f, dt = 0.f, yv = 0.f, xv = 0.f;
-    float hist[K - 1];
-    T *cs = conv_state + ((size_t)bb * Es + c) * (K - 1);
-    if (act) {
-      xv = ldf(xz + (size_t)bb * ld_xz + c);
-      float acc = conv_b ? ldf(conv_b + c) : 0.f;
+  const int bl = threadIdx.x / CB, cl = threadIdx.x % CB;
+  const int b = b0 + bl, c = c0 + cl;
+  if (bl >= BB || bl >= nbb || cl >= ncb) return;
+  // dt_proj + bias + softplus (tp_model.py:162-163)
+  float dot = 0.f;
+  const float *dr = dls + bl * R;
+#pragma unroll 8
+  for (int r = 0; r < R; ++r) dot = fmaf(dr[r], wt[r * (CB + 1) + cl], dot);
+  const float dt = softplus_f(dot + ldf(b_dt + c));
+  // conv over [history | x] and the history shift (tp_model.py:145-157)
+  T *cs = conv_state + ((size_t)b * Es + c) * (K - 1);
+  const float xv = ldf(xz + (size_t)b * ld_xz + c);
+  float hist[K - 1];
+  float acc = conv_b ? ldf(conv_b + c) : 0.f;
 #pragma unroll
-      for (int j = 0; j < K - 1; ++j) {
-        hist[j] = ldf(cs + j);
-        acc = fmaf(ldf(conv_w + (size_t)c * K + j), hist[j], acc);
-      }
-      acc = fmaf(ldf(conv_w + (size_t)c * K + K - 1), xv, acc);
-      xc = silu_f(acc);
-      zv = ldf(xz + (size_t)bb * ld_xz + Es + c);
-      dt = dts[bb * CB + cc];
-      const float dtx = dt * xc;
-      float *hs = ssm_state + ((size_t)bb * Es + c) * N + sub * NS;
-      const float *bcr = bcp + (size_t)bb * ld_bc;
-      const float *a2 = a2s + cc * N + sub * NS;
-#pragma unroll
-      for (int q = 0; q < NS; q += 4) {
-        float4 hv = *reinterpret_cast<const float4 *>(hs + q);
-        float hh[4] = {hv.x, hv.y, hv.z, hv.w};
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int n = sub * NS + q + u;
-          const float dA = ex2_hw(dt * a2[q + u]);
-          hh[u] = fmaf(dA, hh[u], bcr[n] * dtx);
-          yv = fmaf(bcr[N + n], hh[u], yv);
-        }
-        *reinterpret_cast<float4 *>(hs + q) = make_float4(hh[0], hh[1], hh[2], hh[3]);
-      }
-    }
-#pragma unroll
-    for (int o = 1; o < TPG; o <<= 1) yv += __shfl_xor_sync(0xffffffffu, yv, o);
-    __syncwarp();  // every lane of the group has read the history before it is shifted
-    if (act && sub == 0) {
-#pragma unroll
-      for (int j = 0; j < K - 2; ++j) stf(cs + j, hist[j + 1]);
-      stf(cs + K - 2, xv);
-    }
-    if (act && sub == 0) stf(y + (size_t)bb * ld_y + c, (yv + ldf(Dp + c) * xc) * silu_f(zv));
+  for (int j = 0; j < K - 1; ++j) {
+    hist[j] = ldf(cs + j);
+    acc = fmaf(ldf(conv_w + (size_t)c * K + j), hist[j], acc);
   }
+  acc = fmaf(ldf(conv_w + (size_t)c * K + K - 1), xv, acc);
+#pragma unroll
+  for (int j = 0; j < K - 2; ++j) stf(cs + j, hist[j + 1]);
+  stf(cs + K - 2, xv);
+  const float xc = silu_f(acc);
+  // state update and output (tp_model.py:165-173)
+  const float dtx = dt * xc;
+  float *hs = ssm_state + ((size_t)b * Es + c) * N;
+  const float4 *bc4 = reinterpret_cast<const float4 *>(bcp + (size_t)b * ld_bc);
+  const float *a2 = a2s + cl * N;
+  float ya[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int q = 0; q < N / 4; ++q) {
+    float4 hv = *reinterpret_cast<const float4 *>(hs + 4 * q);
+    const float4 B4 = __ldg(bc4 + q), C4 = __ldg(bc4 + N / 4 + q);
+    float hh[4] = {hv.x, hv.y, hv.z, hv.w};
+    const float Bs[4] = {B4.x, B4.y, B4.z, B4.w}, Cs[4] = {C4.x, C4.y, C4.z, C4.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float dA = ex2_hw(dt * a2[4 * q + u]);
+      hh[u] = fmaf(dA, hh[u], Bs[u] * dtx);
+      ya[u] = fmaf(Cs[u], hh[u], ya[u]);
+    }
+    *reinterpret_cast<float4 *>(hs + 4 * q) = make_float4(hh[0], hh[1], hh[2], hh[3]);
+  }
+  const float zv = ldf(xz + (size_t)b * ld_xz + Es + c);
+  const float yv = (ya[0] + ya[1]) + (ya[2] + ya[3]);
+  stf(y + (size_t)b * ld_y + c, fmaf(ldf(Dp + c), xc, yv) * silu_f(zv));
 }
 
 template <typename T, int N, int TPC>
@@ -711,7 +701,7 @@ static int launch_scan(const void *xz, int ld_xz, const float *dt, int ld_dt, co
   const bool vec16 = Es % CB == 0 && aligned16(xz) && aligned16(dt) && aligned16(bc) &&
                      ((size_t)ld_xz * sizeof(T)) % 16 == 0 && ld_dt % 4 == 0 && ld_bc % 4 == 0;
   dim3 grid((Es + CB - 1) / CB, B);
-  kern<<<grid, 128, sizeof(S), s>>>((const T *)xz, ld_xz, dt, ld_dt, bc, ld_bc, (const T *)A_log, (const T *)Dp,
+  launch_pdl(kern, dim3(grid), dim3(128), sizeof(S), s, (const T *)xz, ld_xz, dt, ld_dt, bc, ld_bc, (const T *)A_log, (const T *)Dp,
                                      (const T *)conv_w, (const T *)conv_b, (const T *)conv_init, ssm_init, (T *)y, ld_y,
                                      (T *)conv_final, ssm_final, L, Es, vec16);
   return check_launch("scan_prefill");
@@ -738,14 +728,14 @@ int mtp_conv1d_silu(const void *xz, int ld_xz, const void *conv_w, const void *c
     const int groups = Es / V;
     dim3 grid((groups + 63) / 64, (L + TT - 1) / TT, B);
     MTP_DISPATCH_FB(dtype, T,
-        conv1d_silu_vec_kernel<T, 4, TT><<<grid, 64, 0, s>>>((const T *)xz, ld_xz, (const T *)conv_w,
+        launch_pdl(conv1d_silu_vec_kernel<T, 4, TT>, dim3(grid), dim3(64), 0, s, (const T *)xz, ld_xz, (const T *)conv_w,
                                                               (const T *)conv_b, (const T *)hist, (T *)xc, ld_xc, L, Es));
     return check_launch("conv1d_silu");
   }
   constexpr int TT = 8;
   dim3 grid((Es + 127) / 128, (L + TT - 1) / TT, B);
   MTP_DISPATCH_FB(dtype, T,
-      conv1d_silu_kernel<T, 4, TT><<<grid, 128, 0, s>>>((const T *)xz, ld_xz, (const T *)conv_w,
+      launch_pdl(conv1d_silu_kernel<T, 4, TT>, dim3(grid), dim3(128), 0, s, (const T *)xz, ld_xz, (const T *)conv_w,
                                                          (const T *)conv_b, (const T *)hist, (T *)xc, ld_xc, L, Es));
   return check_launch("conv1d_silu");
 }
@@ -832,24 +822,26 @@ int mtp_step(const void *xz, int ld_xz, const void *dt_low, int ld_dl, const voi
   MTP_REQUIRE(K == 4, "only d_conv == 4 is built");
   MTP_REQUIRE(N == 16 || N == 8, "d_state must be 8 or 16");
   MTP_REQUIRE(B >= 0 && B <= 1024 && Es > 0 && R > 0, "bad sizes");
-  MTP_REQUIRE(aligned16(ssm_state), "ssm_state must be 16-byte aligned");
+  MTP_REQUIRE(aligned16(ssm_state) && aligned16(bc) && ld_bc % 4 == 0, "ssm_state / bc must be 16-byte aligned");
   if (B == 0) return MTP_OK;
   constexpr int CB = 32;
-  const size_t smem = ((size_t)CB * N + (size_t)B * CB) * sizeof(float);
+  const int BB = B >= 8 ? 8 : (B >= 4 ? 4 : (B >= 2 ? 2 : 1));
+  const size_t smem = ((size_t)R * (CB + 1) + (size_t)BB * R + (size_t)CB * N) * sizeof(float);
+  MTP_REQUIRE(smem <= 200 * 1024, "dt_rank too large for the step kernel");
   cudaStream_t s = (cudaStream_t)stream;
-  dim3 grid((Es + CB - 1) / CB);
+  dim3 grid((Es + CB - 1) / CB, (B + BB - 1) / BB);
 #define MTP_STEP_CASE(TT, NN)                                                                               \
   do {                                                                                                     \
-    auto kern = step_kernel<TT, NN, 4, CB>;                                                                \
+    auto kern = step_kernel<TT, NN, 4>;                                                                    \
     static bool attr_set = false;                                                                          \
     if (!attr_set) {                                                                                       \
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);                 \
       attr_set = true;                                                                                     \
     }                                                                                                      \
-    kern<<<grid, 256, smem, s>>>((const TT *)xz, ld_xz, (const TT *)dt_low, ld_dl, (const TT *)W_dt,       \
+    launch_pdl(kern, dim3(grid), dim3(256), smem, s, (const TT *)xz, ld_xz, (const TT *)dt_low, ld_dl, (const TT *)W_dt,       \
                                  (const TT *)b_dt, bc, ld_bc, (const TT *)A_log, (const TT *)Dp,          \
                                  (const TT *)conv_w, (const TT *)conv_b, (TT *)conv_state, ssm_state,     \
-                                 (TT *)y, ld_y, B, Es, R);                                                 \
+                                 (TT *)y, ld_y, B, Es, R, BB);                                             \
     return check_launch("step");                                                                           \
   } while (0)
   if (dtype == MTP_F32) { if (N == 16) MTP_STEP_CASE(float, 16); MTP_STEP_CASE(float, 8); }

@@ -85,16 +85,29 @@ def bench_scan(a):
     cf = torch.empty(B, es, 3, device="cuda", dtype=dt_)
     sf = torch.empty(B, es, n, device="cuda")
 
+    R = a.rank
+    dl = torch.randn(T, R, device="cuda", dtype=dt_)
+    Wdt = torch.randn(es, R, device="cuda", dtype=dt_) * 0.05
+    bdt = (torch.rand(es, device="cuda") * 4 - 7).to(dt_)
+
     def run():
-        L.call("mtp_scan_prefill", L.ptr(xz), 2 * es, L.ptr(dt), es, L.ptr(bc), 2 * n, L.ptr(A_log), L.ptr(Dp),
-               L.ptr(cw), L.ptr(cb), None, None, L.ptr(y), es, L.ptr(cf), L.ptr(sf), B, Lq, es, n, 4, L.BF16,
-               L.stream_ptr())
+        if a.fused:
+            L.call("mtp_scan_prefill_fused", L.ptr(xz), 2 * es, L.ptr(dl), R, L.ptr(Wdt), L.ptr(bdt), L.ptr(bc), 2 * n,
+                   L.ptr(A_log), L.ptr(Dp), L.ptr(cw), L.ptr(cb), None, None, L.ptr(y), es, L.ptr(cf), L.ptr(sf), B,
+                   Lq, es, n, R, 4, L.stream_ptr())
+        else:
+            L.call("mtp_scan_prefill", L.ptr(xz), 2 * es, L.ptr(dt), es, L.ptr(bc), 2 * n, L.ptr(A_log), L.ptr(Dp),
+                   L.ptr(cw), L.ptr(cb), None, None, L.ptr(y), es, L.ptr(cf), L.ptr(sf), B, Lq, es, n, 4, L.BF16,
+                   L.stream_ptr())
 
     ms = _time(run, a.warmup, a.iters)
-    nbytes = T * (es * (3 * 2 + 4) + 2 * n * 4) + B * es * (n * 4 + 3 * 2)
+    # algorithmic bytes: x, z, y (bf16) and dt fp32 (or dt_low bf16 when fused), B|C fp32, states
+    dt_bytes = R * 2 if a.fused else es * 4
+    nbytes = T * (es * 3 * 2 + dt_bytes + 2 * n * 4) + B * es * (n * 4 + 3 * 2)
     gbs = nbytes / (ms / 1e3) / 1e9
     exps = T * es * n
-    return {"kernel": "scan_prefill", "B": B, "L": Lq, "Es": es, "avg_ms": ms, "GBps": gbs,
+    return {"kernel": "scan_prefill_fused" if a.fused else "scan_prefill", "B": B, "L": Lq, "Es": es, "avg_ms": ms,
+            "GBps": gbs,
             "frac_of_hbm": gbs / peaks()["hbm_gbs"], "algorithmic_bytes": nbytes, "Gexp_per_s": exps / (ms / 1e3) / 1e9}
 
 
@@ -170,6 +183,23 @@ def bench_allreduce(a):
            "protocol": "two-shot" if two_shot else "one-shot", "nvlink_bytes_sent_per_rank": sent,
            "nvlink_GBps_per_direction": sent / (ms / 1e3) / 1e9 if sent else 0.0,
            "frac_of_770": (sent / (ms / 1e3) / 1e9) / 770.0 if sent else 0.0}
+    if ws > 1 and a.nccl:
+        # the reference's collective on NCCL for the same tensor (tp_utils.py:27, :41, :120)
+        xb = x.clone()
+        if a.mode == "fp32":
+            fn = lambda: dist.all_reduce(xb, op=dist.ReduceOp.SUM)
+        elif a.mode == "fp16":
+            xh = x.half()
+            fn = lambda: dist.all_reduce(xh, op=dist.ReduceOp.SUM)
+        else:
+            payload = torch.empty(rows * (4 + cols), dtype=torch.uint8, device="cuda")
+            gathered = torch.empty(ws * payload.numel(), dtype=torch.uint8, device="cuda")
+            fn = lambda: dist.all_gather_into_tensor(gathered, payload)
+        dist.barrier()
+        nms = _time(fn, a.warmup, a.iters)
+        t = torch.tensor([nms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        res["nccl_collective_us"] = t.item() * 1e3
     if comm is not None:
         comm.check()
         comm.destroy()
@@ -233,6 +263,8 @@ def main():
     s.add_argument("--batch", type=int, default=32)
     s.add_argument("--seqlen", type=int, default=1024)
     s.add_argument("--channels", type=int, default=4096)
+    s.add_argument("--rank", type=int, default=128, help="dt_rank (fused variant)")
+    s.add_argument("--fused", action="store_true", help="dt_proj + softplus inside the scan (tcgen05)")
     st = sub.add_parser("step")
     st.add_argument("--batch", type=int, default=32)
     st.add_argument("--channels", type=int, default=4096)
@@ -241,6 +273,7 @@ def main():
     r.add_argument("--rows", type=int, default=32768)
     r.add_argument("--cols", type=int, default=2048)
     r.add_argument("--mode", choices=["fp32", "fp16", "int8"], default="int8")
+    r.add_argument("--nccl", action="store_true", help="also time the NCCL collective of the reference path")
     dcd = sub.add_parser("decode")
     dcd.add_argument("--shape", default="1.4b")
     dcd.add_argument("--layers", type=int, default=0, help="override n_layer (0: the shape's)")

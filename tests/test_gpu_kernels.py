@@ -62,7 +62,8 @@ def test_tcgen05_gemm_is_deterministic():
 
 @pytest.mark.parametrize("algo", [L.GEMM_SIMT, L.GEMM_GEMV])
 @pytest.mark.parametrize("dtype", [torch.float32, BF])
-@pytest.mark.parametrize("M,N,K", [(1, 300, 200), (3, 1024, 2048), (8, 160, 96), (32, 517, 333), (70, 64, 16)])
+@pytest.mark.parametrize("M,N,K", [(1, 300, 200), (3, 1024, 2048), (8, 160, 96), (32, 517, 333), (70, 64, 16),
+                                   (1, 160, 4096), (2, 2048, 4096), (5, 161, 1000), (1, 8192, 2048)])
 def test_cuda_core_gemms_match_fp32_torch(algo, dtype, M, N, K):
     a = torch.randn(M, K, device=dev(), dtype=dtype)
     w = torch.randn(N, K, device=dev(), dtype=dtype) * 0.05
@@ -115,6 +116,39 @@ def test_scan_prefill_matches_oracle(dtype, b, l, es, nst, init):
     np.testing.assert_allclose(n(y).reshape(b, l, es), y_ref, atol=tol, rtol=tol)
     np.testing.assert_allclose(n(cf), cf_ref, atol=1e-6, rtol=0)
     np.testing.assert_allclose(n(sf), sf_ref, atol=tol, rtol=tol)
+
+
+@pytest.mark.parametrize("b,l,es,R,init", [(2, 37, 128, 48, True), (3, 70, 256, 128, True), (1, 16, 384, 160, False),
+                                          (2, 5, 128, 64, True), (4, 129, 512, 256, True)])
+def test_fused_dt_scan_matches_oracle(b, l, es, R, init):
+    """dt_proj + softplus inside the scan (tcgen05) vs the oracle: bf16 operands,
+    fp32 accumulation, bf16 output."""
+    x, z, _, Bm, Cm, A_log, Dp, cw, cb, ci, si = _ssm_inputs(b, l, es, 16, 17, BF)
+    if not init:
+        ci = si = None
+    dl = O.bf16_round(_rand((b * l, R), 18))
+    W = O.bf16_round(_rand((es, R), 19, 0.1))
+    bd = O.bf16_round(_rand((es,), 20) - 3)
+    dt = O.softplus((dl @ W.T + bd).astype(np.float32)).reshape(b, l, es)
+    y_ref, cf_ref, sf_ref = O.scan_ref(x, z, dt, Bm, Cm, A_log, Dp, cw, cb, ci, si)
+    T = b * l
+    xz = t(np.concatenate([x, z], -1).reshape(T, 2 * es), BF)
+    bc = t(np.concatenate([Bm, Cm], -1).reshape(T, 32))
+    dl_t, w_t, bd_t = t(dl, BF), t(W, BF), t(bd, BF)
+    args = [t(A_log, BF), t(Dp, BF), t(cw, BF), t(cb, BF), None if ci is None else t(ci, BF), None if si is None else t(si)]
+    y = torch.empty(T, es, device=dev(), dtype=BF)
+    cf = torch.empty(b, es, 3, device=dev(), dtype=BF)
+    sf = torch.empty(b, es, 16, device=dev(), dtype=torch.float32)
+    L.call("mtp_scan_prefill_fused", L.ptr(xz), 2 * es, L.ptr(dl_t), R, L.ptr(w_t), L.ptr(bd_t), L.ptr(bc), 32,
+           *[L.ptr(a) for a in args], L.ptr(y), es, L.ptr(cf), L.ptr(sf), b, l, es, 16, R, 4, L.stream_ptr())
+    torch.cuda.synchronize()
+    import ctypes
+    st = ctypes.c_int(0)
+    L.call("mtp_scan_status", ctypes.byref(st))
+    assert st.value == 0
+    np.testing.assert_allclose(n(y).reshape(b, l, es), y_ref, atol=3e-2, rtol=3e-2)
+    np.testing.assert_allclose(n(cf), cf_ref, atol=1e-6, rtol=0)
+    np.testing.assert_allclose(n(sf), sf_ref, atol=2e-2, rtol=2e-2)
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, BF])

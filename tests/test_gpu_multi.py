@@ -205,3 +205,40 @@ def test_reduction_with_absent_peer_times_out_with_status():
     res = _spawn(_timeout_worker)
     assert res[0] == L.MTP_ERR_TIMEOUT
     assert res[1] == 0
+
+
+# ------------------------------------------------------------------ protocols agree (out_proj epilogue, bf16 gather)
+def _protocol_worker(rank, init_file, q):
+    try:
+        _init(rank, init_file)
+        from mamba_tp_lite_b200 import _lib as L
+        from mamba_tp_lite_b200.tp_utils import get_comm
+
+        rows, d = 3000, 1024
+        comm = get_comm(None, rank, WS, 48, d)
+        part = torch.randn(rows, d, generator=torch.Generator().manual_seed(7 + rank)).cuda() * 2
+        w = torch.randn(d, generator=torch.Generator().manual_seed(9)).cuda().to(torch.bfloat16)
+        res = {}
+        for proto in ("oneshot", "twoshot"):
+            os.environ["MTP_COMM_PROTOCOL"] = proto
+            for mode in (L.RED_FP32, L.RED_FP16, L.RED_INT8TOK):
+                resid = torch.ones(rows, d, device="cuda")
+                normed = torch.empty(rows, d, device="cuda", dtype=torch.bfloat16)
+                L.call("mtp_reduce_outproj", comm.ptr, mode, L.ptr(part), rows, d, None, L.ptr(resid), L.ptr(w),
+                       1e-5, L.ptr(normed), L.BF16, L.stream_ptr())
+                torch.cuda.synchronize()
+                res[(proto, mode)] = (resid.cpu().numpy(), normed.float().cpu().numpy())
+        comm.check()
+        q.put((rank, res))
+        _finish()
+    except Exception as e:
+        q.put((rank, f"{type(e).__name__}: {e}"))
+
+
+@needs2
+def test_two_shot_bf16_gather_equals_one_shot():
+    res = _spawn(_protocol_worker)
+    for mode in (0, 1, 2):
+        a, b = res[0][("oneshot", mode)], res[0][("twoshot", mode)]
+        assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1]), mode
+        assert np.array_equal(res[1][("twoshot", mode)][0], b[0])
