@@ -4,8 +4,8 @@
  *
  * Every entry point takes plain device pointers, sizes and a cudaStream_t
  * (passed as void*), returns an int status (0 = ok, see MTP_ERR_*), allocates
- * no device memory (the comm context allocates once, in mtp_comm_create), and
- * launches only on the given stream, so all of them can be recorded in a CUDA
+ * no device memory outside the create / bind calls (mtp_comm_create,
+ * mtp_decode_plan_create, mtp_decode_bind_cache), and launches only on the given stream, so all of them can be recorded in a CUDA
  * graph.  No torch types appear here; the Python package binds this header
  * with ctypes.
  *
@@ -203,6 +203,55 @@ int mtp_allreduce(mtp_comm *c, int site, int mode, const float *in, float *out, 
  * start at zero (each row is written before it is read), but calls that overlap
  * on the GPU (different streams, different host threads) race on it. */
 int mtp_allreduce_noalloc(int mode, const float *in, float *out, int rows, int cols, void *stream);
+
+/* ---------------------------------------------------------------- persistent decode
+ * One cooperative launch per decode step runs every layer of the model for a batch
+ * of single tokens: embedding gather (tp_model.py:318), per layer the block's
+ * RMSNorm and residual (tp_model.py:259-262) around the TPMambaMixer.step sequence
+ * (tp_model.py:137-179) with both AllReduces in the layer's wire format over the
+ * comm context (tp_utils.py:23-42, :103-131), and finally norm_f (tp_model.py:321);
+ * the caller runs the lm_head GEMM on `normed`.  It replaces the loop over layers of
+ * TPMambaLM.step / MambaLM.step (tp_model.py:317-322, model.py:343-353): one launch
+ * instead of seven per layer.  bf16 models, d_state 16, d_conv 4, batch <= 32. */
+typedef struct mtp_decode_plan mtp_decode_plan;
+typedef struct mtp_decode_cache mtp_decode_cache;
+
+typedef struct {
+  const void *norm_w;          /* [D]        RMSNorm weight in front of the mixer        */
+  const void *in_w, *in_b;     /* [2Es, D]   in_proj (this rank's x rows then z rows); bias or NULL */
+  const void *conv_w, *conv_b; /* [Es, K], [Es] or NULL                                   */
+  const void *x_w;             /* [R+2N, Es] x_proj (this rank's input columns)            */
+  const void *dt_w, *dt_b;     /* [Es, R], [Es]                                            */
+  const void *A_log, *Dp;      /* [Es, N], [Es]                                            */
+  const void *out_w, *out_b;   /* [D, Es] out_proj (this rank's input columns); bias or NULL */
+  int mode_x, mode_out;        /* MTP_RED_* wire format of AllReduce #1 / #2               */
+} mtp_decode_layer;
+
+/* Validates shapes, copies the layer table to the device and allocates the step's
+ * scratch for up to max_batch tokens.  comm NULL (or world size 1) runs each
+ * AllReduce as its wire format's round trip. */
+int mtp_decode_plan_create(const mtp_decode_layer *layers, int n_layer, const void *norm_f, const void *embedding,
+                           int d_model, int d_inner, int d_state, int dt_rank, int d_conv, float eps, int max_batch,
+                           int dtype, mtp_comm *comm, mtp_decode_plan **out);
+/* Binds per-layer cache tensors: conv_state[l] [batch][Es][K-1] (model dtype) and
+ * ssm_state[l] [batch][Es][N] fp32, both updated in place by each step. */
+int mtp_decode_bind_cache(mtp_decode_plan *plan, void *const *conv_state, float *const *ssm_state, int batch,
+                          mtp_decode_cache **out);
+/* ids: device int64 [batch]; normed: device [batch][D] model dtype, receives
+ * norm_f(residual stream) of the step. */
+int mtp_decode_step(mtp_decode_plan *plan, mtp_decode_cache *cache, const int64_t *ids, void *normed, void *stream);
+/* MTP_OK, or MTP_ERR_TIMEOUT after a barrier or peer wait gave up (synchronous read). */
+int mtp_decode_status(mtp_decode_plan *plan, int *status);
+/* Clears the barrier, abort and status words after a timeout. */
+int mtp_decode_reset(mtp_decode_plan *plan);
+/* Phase timing of later steps (off by default): with tracing on, each step stores
+ * %globaltimer stamps, nb = 2 + 5 n_layer barriers: out[0] = start, out[k] = when
+ * CTA 0 left barrier k, out[nb + k] = when the last CTA arrived at barrier k
+ * (k = 1..nb-1; barrier 1 ends the embedding phase, then five per layer). */
+int mtp_decode_set_trace(mtp_decode_plan *plan, int on);
+int mtp_decode_read_trace(mtp_decode_plan *plan, uint64_t *out, int capacity, int *n_out);
+void mtp_decode_cache_destroy(mtp_decode_cache *cache);
+void mtp_decode_plan_destroy(mtp_decode_plan *plan);
 
 #ifdef __cplusplus
 }

@@ -51,8 +51,25 @@ _SIGS = {
     "mtp_reduce_outproj": [_vp, _i, _vp, _i, _i, _vp, _vp, _vp, _f, _vp, _i, _vp],
     "mtp_allreduce": [_vp, _i, _i, _vp, _vp, _i, _i, _vp],
     "mtp_allreduce_noalloc": [_i, _vp, _vp, _i, _i, _vp],
+    "mtp_decode_plan_create": [_vp, _i, _vp, _vp, _i, _i, _i, _i, _i, _f, _i, _i, _vp, C.POINTER(_vp)],
+    "mtp_decode_bind_cache": [_vp, _vp, _vp, _i, C.POINTER(_vp)],
+    "mtp_decode_step": [_vp, _vp, _vp, _vp, _vp],
+    "mtp_decode_status": [_vp, C.POINTER(_i)],
+    "mtp_decode_reset": [_vp],
+    "mtp_decode_set_trace": [_vp, _i],
+    "mtp_decode_read_trace": [_vp, C.POINTER(_u64), _i, C.POINTER(_i)],
+    "mtp_decode_cache_destroy": [_vp],
+    "mtp_decode_plan_destroy": [_vp],
 }
-_RESTYPES = {"mtp_version": C.c_char_p, "mtp_last_error": C.c_char_p, "mtp_launch_count": _u64}
+_RESTYPES = {"mtp_version": C.c_char_p, "mtp_last_error": C.c_char_p, "mtp_launch_count": _u64,
+             "mtp_decode_cache_destroy": None, "mtp_decode_plan_destroy": None}
+
+
+class DecodeLayer(C.Structure):
+    """mtp_decode_layer of include/mtp.h."""
+    _fields_ = [(n, C.c_void_p) for n in ("norm_w", "in_w", "in_b", "conv_w", "conv_b", "x_w", "dt_w", "dt_b",
+                                           "A_log", "Dp", "out_w", "out_b")] + [("mode_x", C.c_int),
+                                                                                ("mode_out", C.c_int)]
 
 _lib = None
 
@@ -89,7 +106,9 @@ def check(rc: int) -> None:
 
 
 def call(name: str, *args) -> None:
-    check(getattr(load(), name)(*args))
+    rc = getattr(load(), name)(*args)
+    if _RESTYPES.get(name, _i) is _i:
+        check(rc)
 
 
 def launch_count() -> int:

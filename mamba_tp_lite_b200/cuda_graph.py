@@ -2,8 +2,9 @@
 ``GraphedStepper(model, cache, batch_size, device, n_warmup=3)`` with
 ``capture()`` / ``replay(next_id)`` and ``CUDAGraphUnsupported``.
 
-One ``model.step`` of this package is ~7 libmtp launches per layer plus the
-embedding and lm_head; all of them (reductions over peer memory included) are
+One ``model.step`` of this package is one persistent decode launch plus the
+lm_head GEMM for bf16 models (else ~7 libmtp launches per layer plus the
+embedding and lm_head); all of it (reductions over peer memory included) is
 captured in a single graph.  Every libmtp call takes the current stream and
 allocates nothing itself during capture; the peer-signalling epochs live in
 device memory and are advanced by the kernels, so replays stay in step across
@@ -57,6 +58,9 @@ class GraphedStepper:
             for _ in range(self.n_warmup):
                 self.model.step(self.static_ids, warm)
         torch.cuda.current_stream().wait_stream(side)
+        prepare = getattr(self.model, "prepare_step", None)
+        if prepare is not None:  # first-use allocations for the captured cache, outside the capture
+            prepare(self.cache, self.static_ids.shape[0])
         torch.cuda.synchronize()
         self.graph = torch.cuda.CUDAGraph()
         try:

@@ -237,6 +237,15 @@ def bench_decode(a):
     torch.cuda.synchronize()
     prof, _mixer.PROFILE = _mixer.PROFILE, None
     per_kernel = {k: sum(s.elapsed_time(e) for s, e, _ in v) * 1e3 / cfg.n_layer for k, v in prof.items()}
+    phases = None
+    plan = getattr(m, "_mtp_decode", None)
+    if plan is not None:  # persistent decode kernel: barrier timestamps of one step
+        plan.set_trace(True)
+        for _ in range(3):
+            m.step(nid, cache)
+        torch.cuda.synchronize()
+        phases = {k: round(v, 2) for k, v in plan.phase_times_us().items()}
+        plan.set_trace(False)
     st = GraphedStepper(m, cache, a.batch, "cuda")
     st.capture()
     graph_ms = _time(lambda: st.replay(nid), a.warmup, a.iters)
@@ -244,7 +253,7 @@ def bench_decode(a):
     w_bytes = sum(p.numel() * p.element_size() for p in m.parameters())
     return {"kernel": "decode_step", "shape": a.shape, "layers": cfg.n_layer, "batch": a.batch,
             "eager_ms": eager_ms, "graphed_ms": graph_ms, "weight_bytes": w_bytes,
-            "us_per_layer_by_kernel_eager": per_kernel,
+            "us_per_layer_by_kernel_eager": per_kernel, "decode_kernel_phase_us": phases,
             "hbm_floor_ms": w_bytes / (peaks()["hbm_gbs"] * 1e9) * 1e3}
 
 

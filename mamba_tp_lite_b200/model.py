@@ -183,8 +183,51 @@ class _LMKernels:
         logits = self._lm_head(normed)
         return logits.view(b, l, -1), MambaCache(new_layers)
 
+    def _decode_plan(self, b: int, cache):
+        """(plan, binding) of the persistent decode kernel, or None for the per-layer chain."""
+        from . import _decode
+
+        if b > _decode.fused_max_batch() or _decode.supported(self) is not None:
+            return None
+        key = _decode.plan_key(self)
+        plan = getattr(self, "_mtp_decode", None)
+        capturing = torch.cuda.is_current_stream_capturing()
+        if plan is None or plan.key != key:
+            if capturing:  # creating a plan allocates: not inside a capture (prepare_step does it before)
+                return None
+            if plan is not None:  # a captured graph may still launch it: retire, do not free
+                self.__dict__.setdefault("_mtp_decode_retired", []).append(plan)
+            plan = self._mtp_decode = _decode.DecodePlan(self, key)
+        binding = plan.binding(cache, b, create=not capturing)
+        return None if binding is None else (plan, binding)
+
+    def prepare_step(self, cache, batch_size: int) -> None:
+        """Creates what ``step`` allocates on first use for this cache (the decode
+        plan and its cache binding), so that a CUDA-graph capture of ``step``
+        allocates nothing."""
+        self._decode_plan(batch_size, cache)
+
+    def _count_step_collectives(self, b: int) -> None:
+        from .tp_utils import count_collective
+
+        for blk in self.layers:
+            m = blk.mixer
+            if m._site_modes is not None:
+                count_collective(m.comm, m._site_modes["x_proj"], (b, self.cfg.dt_rank + 2 * self.cfg.d_state),
+                                 m._dt())
+                count_collective(m.comm, m._site_modes["out_proj"], (b, self.cfg.d_model), m._dt())
+
     def _forward_step(self, input_ids: torch.Tensor, cache):
         b = input_ids.shape[0]
+        fused = self._decode_plan(b, cache)
+        if fused is not None:
+            plan, binding = fused
+            L.require_cuda(input_ids, "input_ids")
+            ids = input_ids[:, :1].reshape(-1).to(torch.int64).contiguous()
+            normed = torch.empty(b, self.cfg.d_model, device=ids.device, dtype=self._param_dtype())
+            self._count_step_collectives(b)
+            plan.step(binding, ids, normed)
+            return self._lm_head(normed).view(b, 1, -1)
         resid = self._embed(input_ids[:, :1])
         normed = torch.empty(resid.shape, device=resid.device, dtype=self._param_dtype())
         self._norm_into(resid, self.layers[0].norm.weight, normed)

@@ -129,8 +129,16 @@ def _tp_model_worker(rank, init_file, q, dtype_name):
             st.capture()
             graphed = [st.replay(nxt).clone() for _ in range(3)]
             st.release()
+            count = m.layers[0].mixer.comm.count
+            # the same steps through the per-layer kernel chain (bf16: the persistent decode
+            # kernel ran above; both ranks switch paths together)
+            os.environ["MTP_DECODE_FUSED"] = "0"
+            _, cc = m.prefill(ids.cuda())
+            chain = [m.step(nxt, cc).float().cpu().numpy() for _ in range(3)]
+            os.environ.pop("MTP_DECODE_FUSED")
             out[spec] = (logits.float().cpu().numpy(), [e.float().cpu().numpy() for e in eager],
-                         all(torch.equal(a, b) for a, b in zip(eager, graphed)), m.layers[0].mixer.comm.count)
+                         all(torch.equal(a, b) for a, b in zip(eager, graphed)), count, chain,
+                         getattr(m, "_mtp_decode", None) is not None)
         q.put((rank, out))
         _finish()
     except Exception as e:
@@ -149,8 +157,12 @@ def test_tp2_model_matches_oracle_and_ranks_agree(dtype_name):
     sd = random_init_state_dict(cfg, seed=3, dtype=getattr(torch, dtype_name))
     ids = torch.randint(0, cfg.vocab_size, (2, 72), generator=torch.Generator().manual_seed(4)).numpy()
     for spec in ("fp32", "fp16", "int8"):
-        lg0, st0, graph_ok, count = res[0][spec]
-        lg1, st1, _, _ = res[1][spec]
+        lg0, st0, graph_ok, count, chain0, fused = res[0][spec]
+        lg1, st1, _, _, chain1, _ = res[1][spec]
+        assert fused == (dtype_name == "bfloat16"), spec   # bf16 steps ran the persistent decode kernel
+        assert all(np.array_equal(a, b) for a, b in zip(chain0, chain1)), spec
+        for a, c in zip(st0, chain0):                      # fused == chain up to accumulation order
+            assert np.abs(a - c).max() <= 2e-2 * np.abs(c).max(), spec
         assert np.array_equal(lg0, lg1), spec          # identical on every rank
         assert all(np.array_equal(a, b) for a, b in zip(st0, st1)), spec
         assert graph_ok, spec                          # graph replay == eager, bitwise
@@ -205,6 +217,57 @@ def test_reduction_with_absent_peer_times_out_with_status():
     res = _spawn(_timeout_worker)
     assert res[0] == L.MTP_ERR_TIMEOUT
     assert res[1] == 0
+
+
+# ------------------------------------------------------------------ persistent decode: a peer that never steps
+def _decode_timeout_worker(rank, init_file, q):
+    try:
+        import time
+
+        import torch.distributed as dist
+
+        os.environ["MTP_COMM_TIMEOUT_S"] = "1"
+        _init(rank, init_file)
+        from mamba_tp_lite_b200.checkpoint import random_init_state_dict
+        from mamba_tp_lite_b200.config import MambaConfig
+        from mamba_tp_lite_b200.tp_model import TPMambaLM
+        from mamba_tp_lite_b200.tp_utils import get_comm
+
+        cfg = MambaConfig(d_model=256, n_layer=2, vocab_size=512, dt_rank=16)
+        sd = random_init_state_dict(cfg, seed=5, dtype=torch.bfloat16)
+        m = TPMambaLM.from_state_dict_shard(cfg, sd, rank, WS, dtype=torch.bfloat16, allreduce_dtype="int8",
+                                            device="cuda")
+        ids = torch.randint(0, cfg.vocab_size, (2, 16), generator=torch.Generator().manual_seed(6)).cuda()
+        _, cache = m.prefill(ids)  # both ranks: creates the comm context
+        m.prepare_step(cache, 2)
+        torch.cuda.synchronize()
+        dist.barrier()
+        result = (0, 0, 0.0)
+        if rank == 0:  # rank 1 never steps: rank 0's AllReduce #1 wait must expire
+            comm = get_comm(None, rank, WS, cfg.dt_rank + 2 * cfg.d_state, cfg.d_model)
+            t0 = time.time()
+            m.step(torch.zeros(2, 1, dtype=torch.long, device="cuda"), cache)
+            torch.cuda.synchronize()
+            result = (m._mtp_decode.status(), comm.status(), time.time() - t0)
+            m._mtp_decode.reset()
+            comm.reset_status()
+            assert (torch.ones(8, device="cuda") * 2).sum().item() == 16  # context still usable
+        dist.barrier()
+        q.put((rank, result))
+        _finish()
+    except Exception as e:
+        q.put((rank, f"{type(e).__name__}: {e}"))
+
+
+@needs2
+def test_decode_kernel_with_absent_peer_times_out_with_status():
+    from mamba_tp_lite_b200 import _lib as L
+
+    res = _spawn(_decode_timeout_worker)
+    plan_status, comm_status, elapsed = res[0]
+    assert plan_status == L.MTP_ERR_TIMEOUT and comm_status == L.MTP_ERR_TIMEOUT
+    assert 0.5 < elapsed < 30
+    assert res[1] == (0, 0, 0.0)
 
 
 # ------------------------------------------------------------------ protocols agree (out_proj epilogue, bf16 gather)
