@@ -85,7 +85,8 @@ int mtp_conv1d_silu(const void *xz, int ld_xz, const void *conv_w, const void *c
                     void *stream);
 
 /* Fused prefill: causal conv1d + SiLU + selective scan + D skip + SiLU(z) gate.
- * xz: [B*L, ld_xz] (x | z); dt: [B*L, ld_dt] fp32, softplus already applied;
+ * xz: [B*L, ld_xz] (x | z); dt: [B*L, ld_dt] in dt_dtype (F32, or the model dtype
+ * as the reference's bf16 dt_proj output), softplus already applied;
  * bc: [B*L, ld_bc] fp32 with B in columns [0,N) and C in [N,2N);
  * A_log [Es,N], D [Es], conv_w [Es,K], conv_b [Es] in dtype;
  * conv_init [B,Es,K-1] (dtype) / ssm_init [B,Es,N] (fp32) or NULL for zeros;
@@ -93,7 +94,7 @@ int mtp_conv1d_silu(const void *xz, int ld_xz, const void *conv_w, const void *c
  * conv_final may alias conv_init and ssm_final may alias ssm_init (in-place
  * chunked prefill).  Replaces tp_model.py:93-103 and :113-129
  * (model.py:199-241), the Python loop over t at tp_model.py:124-126. */
-int mtp_scan_prefill(const void *xz, int ld_xz, const float *dt, int ld_dt, const float *bc, int ld_bc,
+int mtp_scan_prefill(const void *xz, int ld_xz, const void *dt, int ld_dt, int dt_dtype, const float *bc, int ld_bc,
                      const void *A_log, const void *Dp, const void *conv_w, const void *conv_b,
                      const void *conv_init, const float *ssm_init, void *y, int ld_y, void *conv_final,
                      float *ssm_final, int B, int L, int Es, int N, int K, int dtype, void *stream);

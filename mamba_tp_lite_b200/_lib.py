@@ -29,7 +29,7 @@ _SIGS = {
     "mtp_gemm": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _i, _vp],
     "mtp_gemm_ex": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _i, _i, _vp],
     "mtp_conv1d_silu": [_vp, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp],
-    "mtp_scan_prefill": [_vp, _i, _vp, _i, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _vp,
+    "mtp_scan_prefill": [_vp, _i, _vp, _i, _i, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _vp,
                          _i, _i, _i, _i, _i, _i, _vp],
     "mtp_scan_prefill_fused": [_vp, _i, _vp, _i, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp,
                                _vp, _i, _i, _i, _i, _i, _i, _vp],

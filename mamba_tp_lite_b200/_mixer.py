@@ -159,14 +159,16 @@ class MixerKernels:
             self._gemm(y, self.out_proj.weight, partial_o, tag="out_proj")
             self._reduce_out(partial_o, resid, norm_w, eps, normed)
             return conv_final, ssm_final
-        dt = torch.empty(T, es, device=dev, dtype=torch.float32)
+        # dt = softplus(dt_proj(dt_low)) in the model dtype, as the reference's dt_proj output
+        # (tp_model.py:110-111); the scan widens it to fp32
+        dt = torch.empty(T, es, device=dev, dtype=dt_)
         self._gemm(dt_low, self.dt_proj.weight, dt, L.EPI_BIAS_SOFTPLUS, self.dt_proj.bias, tag="dt_proj")
         ev = _prof_begin()
-        L.call("mtp_scan_prefill", L.ptr(xz), 2 * es, L.ptr(dt), es, L.ptr(bc), 2 * n, L.ptr(self.A_log), L.ptr(self.D),
-               L.ptr(conv_w), L.ptr(conv_b), L.ptr(conv_init), L.ptr(ssm_init), L.ptr(y), es, L.ptr(conv_final),
-               L.ptr(ssm_final), B, Lq, es, n, k, L.dtype_code(dt_), L.stream_ptr())
-        # algorithmic bytes: x, z, y in the model dtype, dt fp32, B|C fp32 (+ per-sequence state I/O)
-        _prof_end(ev, "scan", T * (es * (3 * esz + 4) + 2 * n * 4) + B * es * (2 * n * 4 + 2 * (k - 1) * esz))
+        L.call("mtp_scan_prefill", L.ptr(xz), 2 * es, L.ptr(dt), es, L.dtype_code(dt_), L.ptr(bc), 2 * n,
+               L.ptr(self.A_log), L.ptr(self.D), L.ptr(conv_w), L.ptr(conv_b), L.ptr(conv_init), L.ptr(ssm_init),
+               L.ptr(y), es, L.ptr(conv_final), L.ptr(ssm_final), B, Lq, es, n, k, L.dtype_code(dt_), L.stream_ptr())
+        # algorithmic bytes: x, z, dt, y in the model dtype, B|C fp32 (+ per-sequence state I/O)
+        _prof_end(ev, "scan", T * (es * 4 * esz + 2 * n * 4) + B * es * (2 * n * 4 + 2 * (k - 1) * esz))
         partial_o = torch.empty(T, cfg.d_model, device=dev, dtype=torch.float32)
         self._gemm(y, self.out_proj.weight, partial_o, tag="out_proj")
         self._reduce_out(partial_o, resid, norm_w, eps, normed)

@@ -53,12 +53,14 @@ __device__ __forceinline__ float softplus_f(float x) { return x > 20.0f ? x : lo
 // softplus(x) = max(x, 0) + log1p(exp(-|x|)), torch's threshold 20.  log1p(u) for
 // u in (0, 1] by Goldberg's identity log1p(u) = log(1+u) * u / ((1+u) - 1), which
 // keeps the relative accuracy of the hardware logarithm for small u.
+// Written without branches (selects only) so a thread's many independent
+// elements overlap their MUFU latencies.
 __device__ __forceinline__ float softplus_fast(float x) {
-  if (x > 20.f) return x;
   const float u = __expf(-fabsf(x));
   const float w = 1.0f + u;
-  const float l = (w == 1.0f) ? u : __logf(w) * __fdividef(u, w - 1.0f);
-  return fmaxf(x, 0.f) + l;
+  const float lg = __logf(w) * __fdividef(u, w - 1.0f);  // w == 1: not selected below
+  const float r = fmaxf(x, 0.f) + ((w == 1.0f) ? u : lg);
+  return x > 20.f ? x : r;
 }
 
 

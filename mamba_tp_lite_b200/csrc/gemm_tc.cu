@@ -238,13 +238,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tile_coords(p, t, mt, nt);
       const int row = mt * BM + q * 32 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN_MAX);
-      for (int j = half * 16; j < p.bn; j += 32) {
+      // this warp's 16-column chunks are j, j + 32, j + 64, ...: two per TMEM wait
+      for (int j = half * 16; j < p.bn; j += 64) {
         const int n0 = nt * p.bn + j;
-        float b[16];
-        if (p.epi != MTP_EPI_STORE && n0 < p.N) load_bias16(p, n0, b);  // issued before the TMEM read
-        float v[16];
-        tmem_ld16(tbase + (uint32_t)j, v);
+        const bool two = j + 32 < p.bn;  // warp-uniform
+        float b[16], b2[16];
+        if (p.epi != MTP_EPI_STORE) {  // issued before the TMEM read
+          if (n0 < p.N) load_bias16(p, n0, b);
+          if (two && n0 + 32 < p.N) load_bias16(p, n0 + 32, b2);
+        }
+        float v[16], v2[16];
+        if (two) {
+          tmem_ld16x2(tbase + (uint32_t)j, tbase + (uint32_t)(j + 32), v, v2);
+        } else {
+          tmem_ld16(tbase + (uint32_t)j, v);
+        }
         if (n0 < p.N) epilogue_store(p, row, n0, v, b);
+        if (two && n0 + 32 < p.N) epilogue_store(p, row, n0 + 32, v2, b2);
       }
       tc_fence_before();
       __syncwarp();

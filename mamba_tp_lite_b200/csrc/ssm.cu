@@ -166,12 +166,12 @@ __global__ void conv1d_silu_vec_kernel(const T *__restrict__ xz, int ld_xz, cons
 //   phase A  conv1d + SiLU of the TL positions (independent of the state: ILP)
 //   phase B  the recurrence over the TL positions, storing y = (C.h + D.xc) * silu(z)
 //            (a warp writes 32 consecutive channels of a position).
-template <typename T, int N, int TPC, int TL>
+template <typename T, typename TD, int N, int TPC, int TL>
 struct ScanSmem {
   static constexpr int CB = 128 / TPC;
   T x[2][TL][CB];
   T z[2][TL][CB];
-  float dt[2][TL][CB];
+  TD dt[2][TL][CB];
   float bc[2][TL][2 * N];
 };
 
@@ -184,15 +184,15 @@ __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 
-template <typename T, int N, int TPC, int TL, int K>
+template <typename T, typename TD, int N, int TPC, int TL, int K>
 __global__ void __launch_bounds__(128, (TPC == 1 ? 4 : 6)) scan_prefill_kernel(
-    const T *__restrict__ xz, int ld_xz, const float *__restrict__ dtp, int ld_dt, const float *__restrict__ bcp,
+    const T *__restrict__ xz, int ld_xz, const TD *__restrict__ dtp, int ld_dt, const float *__restrict__ bcp,
     int ld_bc, const T *__restrict__ A_log, const T *__restrict__ Dp, const T *__restrict__ conv_w,
     const T *__restrict__ conv_b, const T *conv_init, const float *ssm_init, T *__restrict__ y, int ld_y,
     T *conv_final, float *ssm_final, int L, int Es, bool vec16) {
   MTP_PDL_WAIT();
   MTP_PDL_TRIGGER();
-  using S = ScanSmem<T, N, TPC, TL>;
+  using S = ScanSmem<T, TD, N, TPC, TL>;
   constexpr int CB = S::CB;
   constexpr int NS = N / TPC;
   constexpr int NT = 128;
@@ -231,7 +231,8 @@ __global__ void __launch_bounds__(128, (TPC == 1 ? 4 : 6)) scan_prefill_kernel(
     const int t0 = k * TL;
     const int tl = min(TL, L - t0);
     if (vec16) {  // full channel blocks, 16-byte aligned rows
-      constexpr int XW = CB * (int)sizeof(T) / 16, DW = CB * 4 / 16, BW = 2 * N * 4 / 16;
+      constexpr int XW = CB * (int)sizeof(T) / 16, DW = CB * (int)sizeof(TD) / 16, BW = 2 * N * 4 / 16;
+      constexpr int DE = 16 / (int)sizeof(TD);  // dt elements per 16-byte granule
       for (int i = threadIdx.x; i < tl * XW; i += NT) {
         const int tt = i / XW, w = i % XW;
         const T *src = xz + (row0 + t0 + tt) * ld_xz + c0;
@@ -241,7 +242,7 @@ __global__ void __launch_bounds__(128, (TPC == 1 ? 4 : 6)) scan_prefill_kernel(
       }
       for (int i = threadIdx.x; i < tl * DW; i += NT) {
         const int tt = i / DW, w = i % DW;
-        cp_async16(&sm.dt[buf][tt][4 * w], dtp + (row0 + t0 + tt) * ld_dt + c0 + 4 * w);
+        cp_async16(&sm.dt[buf][tt][DE * w], dtp + (row0 + t0 + tt) * ld_dt + c0 + DE * w);
       }
       for (int i = threadIdx.x; i < tl * BW; i += NT) {
         const int tt = i / BW, w = i % BW;
@@ -255,9 +256,11 @@ __global__ void __launch_bounds__(128, (TPC == 1 ? 4 : 6)) scan_prefill_kernel(
         cp_async4(&sm.x[buf][tt][wi * EPW], xz + (row0 + t0 + tt) * ld_xz + c0 + wi * EPW);
         cp_async4(&sm.z[buf][tt][wi * EPW], xz + (row0 + t0 + tt) * ld_xz + Es + c0 + wi * EPW);
       }
-      for (int i = threadIdx.x; i < tl * ncb; i += NT) {
-        const int tt = i / ncb, ci = i % ncb;
-        cp_async4(&sm.dt[buf][tt][ci], dtp + (row0 + t0 + tt) * ld_dt + c0 + ci);
+      constexpr int DPW = 4 / sizeof(TD);
+      const int dpr = (ncb + DPW - 1) / DPW;
+      for (int i = threadIdx.x; i < tl * dpr; i += NT) {
+        const int tt = i / dpr, wi = i % dpr;
+        cp_async4(&sm.dt[buf][tt][wi * DPW], dtp + (row0 + t0 + tt) * ld_dt + c0 + wi * DPW);
       }
       for (int i = threadIdx.x; i < tl * 2 * N; i += NT) {
         const int tt = i / (2 * N), j = i % (2 * N);
@@ -295,7 +298,7 @@ __global__ void __launch_bounds__(128, (TPC == 1 ? 4 : 6)) scan_prefill_kernel(
         for (int j = 0; j < K - 2; ++j) win[j] = win[j + 1];
         win[K - 2] = xv;
         xcs[tt] = silu_fast(acc);
-        dts[tt] = sm.dt[buf][tt][cl];
+        dts[tt] = ldf(&sm.dt[buf][tt][cl]);
       }
     }
     // phase B: recurrence
@@ -683,15 +686,16 @@ __global__ void __launch_bounds__(256) step_kernel(const T *__restrict__ xz, int
   stf(y + (size_t)b * ld_y + c, fmaf(ldf(Dp + c), xc, yv) * silu_f(zv));
 }
 
-template <typename T, int N, int TPC>
-static int launch_scan(const void *xz, int ld_xz, const float *dt, int ld_dt, const float *bc, int ld_bc,
+template <typename T, typename TD, int N, int TPC>
+static int launch_scan(const void *xz, int ld_xz, const void *dt_v, int ld_dt, const float *bc, int ld_bc,
                        const void *A_log, const void *Dp, const void *conv_w, const void *conv_b,
                        const void *conv_init, const float *ssm_init, void *y, int ld_y, void *conv_final,
                        float *ssm_final, int B, int L, int Es, cudaStream_t s) {
   constexpr int TL = 16, K = 4;
-  using S = ScanSmem<T, N, TPC, TL>;
+  using S = ScanSmem<T, TD, N, TPC, TL>;
   constexpr int CB = S::CB;
-  auto kern = scan_prefill_kernel<T, N, TPC, TL, K>;
+  auto kern = scan_prefill_kernel<T, TD, N, TPC, TL, K>;
+  const TD *dt = (const TD *)dt_v;
   static bool attr_set = false;  // per template instance
   if (!attr_set) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(S)) != cudaSuccess)
@@ -699,7 +703,8 @@ static int launch_scan(const void *xz, int ld_xz, const float *dt, int ld_dt, co
     attr_set = true;
   }
   const bool vec16 = Es % CB == 0 && aligned16(xz) && aligned16(dt) && aligned16(bc) &&
-                     ((size_t)ld_xz * sizeof(T)) % 16 == 0 && ld_dt % 4 == 0 && ld_bc % 4 == 0;
+                     ((size_t)ld_xz * sizeof(T)) % 16 == 0 && ((size_t)ld_dt * sizeof(TD)) % 16 == 0 &&
+                     ld_bc % 4 == 0;
   dim3 grid((Es + CB - 1) / CB, B);
   launch_pdl(kern, dim3(grid), dim3(128), sizeof(S), s, (const T *)xz, ld_xz, dt, ld_dt, bc, ld_bc, (const T *)A_log, (const T *)Dp,
                                      (const T *)conv_w, (const T *)conv_b, (const T *)conv_init, ssm_init, (T *)y, ld_y,
@@ -740,7 +745,7 @@ int mtp_conv1d_silu(const void *xz, int ld_xz, const void *conv_w, const void *c
   return check_launch("conv1d_silu");
 }
 
-int mtp_scan_prefill(const void *xz, int ld_xz, const float *dt, int ld_dt, const float *bc, int ld_bc,
+int mtp_scan_prefill(const void *xz, int ld_xz, const void *dt, int ld_dt, int dt_dtype, const float *bc, int ld_bc,
                      const void *A_log, const void *Dp, const void *conv_w, const void *conv_b, const void *conv_init,
                      const float *ssm_init, void *y, int ld_y, void *conv_final, float *ssm_final, int B, int L,
                      int Es, int N, int K, int dtype, void *stream) {
@@ -753,6 +758,8 @@ int mtp_scan_prefill(const void *xz, int ld_xz, const float *dt, int ld_dt, cons
   // 4-byte cp.async granules: x/z words must be 4-byte aligned
   MTP_REQUIRE(aligned(xz, 4) && aligned(dt, 4) && aligned(bc, 4), "inputs must be 4-byte aligned");
   MTP_REQUIRE(es == 4 || (ld_xz % 2 == 0 && Es % 2 == 0), "bf16 x|z rows need even Es and ld_xz");
+  MTP_REQUIRE(dt_dtype == MTP_F32 || dt_dtype == dtype, "dt must be F32 or the model dtype");
+  MTP_REQUIRE(dt_dtype == MTP_F32 || (ld_dt % 2 == 0 && Es % 2 == 0), "bf16 dt rows need even Es and ld_dt");
   if (B == 0 || L == 0) return MTP_OK;
   cudaStream_t s = (cudaStream_t)stream;
   // threads per channel: enough resident warps at small channel counts
@@ -764,15 +771,19 @@ int mtp_scan_prefill(const void *xz, int ld_xz, const float *dt, int ld_dt, cons
     const int v = atoi(env);
     if (v == 1 || v == 2 || v == 4) tpc = v;
   }
-#define MTP_SCAN_CASE(TT, NN, TP)                                                                          \
-  return launch_scan<TT, NN, TP>(xz, ld_xz, dt, ld_dt, bc, ld_bc, A_log, Dp, conv_w, conv_b, conv_init,   \
-                                 ssm_init, y, ld_y, conv_final, ssm_final, B, L, Es, s)
+#define MTP_SCAN_CASE(TT, TDD, NN, TP)                                                                     \
+  return launch_scan<TT, TDD, NN, TP>(xz, ld_xz, dt, ld_dt, bc, ld_bc, A_log, Dp, conv_w, conv_b, conv_init, \
+                                      ssm_init, y, ld_y, conv_final, ssm_final, B, L, Es, s)
+  using bf16 = __nv_bfloat16;
   if (dtype == MTP_F32) {
-    if (N == 16) { if (tpc == 1) MTP_SCAN_CASE(float, 16, 1); if (tpc == 2) MTP_SCAN_CASE(float, 16, 2); MTP_SCAN_CASE(float, 16, 4); }
-    MTP_SCAN_CASE(float, 8, 2);
+    if (N == 16) { if (tpc == 1) MTP_SCAN_CASE(float, float, 16, 1); if (tpc == 2) MTP_SCAN_CASE(float, float, 16, 2); MTP_SCAN_CASE(float, float, 16, 4); }
+    MTP_SCAN_CASE(float, float, 8, 2);
+  } else if (dtype == MTP_BF16 && dt_dtype == MTP_F32) {
+    if (N == 16) { if (tpc == 1) MTP_SCAN_CASE(bf16, float, 16, 1); if (tpc == 2) MTP_SCAN_CASE(bf16, float, 16, 2); MTP_SCAN_CASE(bf16, float, 16, 4); }
+    MTP_SCAN_CASE(bf16, float, 8, 2);
   } else if (dtype == MTP_BF16) {
-    if (N == 16) { if (tpc == 1) MTP_SCAN_CASE(__nv_bfloat16, 16, 1); if (tpc == 2) MTP_SCAN_CASE(__nv_bfloat16, 16, 2); MTP_SCAN_CASE(__nv_bfloat16, 16, 4); }
-    MTP_SCAN_CASE(__nv_bfloat16, 8, 2);
+    if (N == 16) { if (tpc == 1) MTP_SCAN_CASE(bf16, bf16, 16, 1); if (tpc == 2) MTP_SCAN_CASE(bf16, bf16, 16, 2); MTP_SCAN_CASE(bf16, bf16, 16, 4); }
+    MTP_SCAN_CASE(bf16, bf16, 8, 2);
   }
 #undef MTP_SCAN_CASE
   return fail(MTP_ERR_UNSUPPORTED, "scan_prefill: dtype must be F32 or BF16");

@@ -75,7 +75,7 @@ def bench_scan(a):
     T = B * Lq
     dt_ = torch.bfloat16
     xz = torch.randn(T, 2 * es, device="cuda", dtype=dt_)
-    dt = torch.rand(T, es, device="cuda") * 0.1
+    dt = (torch.rand(T, es, device="cuda") * 0.1).to(torch.float32 if a.dt == "f32" else dt_)
     bc = torch.randn(T, 2 * n, device="cuda")
     A_log = torch.log(torch.arange(1, n + 1, device="cuda", dtype=torch.float32)).repeat(es, 1).to(dt_)
     Dp = torch.ones(es, device="cuda", dtype=dt_)
@@ -96,13 +96,13 @@ def bench_scan(a):
                    L.ptr(A_log), L.ptr(Dp), L.ptr(cw), L.ptr(cb), None, None, L.ptr(y), es, L.ptr(cf), L.ptr(sf), B,
                    Lq, es, n, R, 4, L.stream_ptr())
         else:
-            L.call("mtp_scan_prefill", L.ptr(xz), 2 * es, L.ptr(dt), es, L.ptr(bc), 2 * n, L.ptr(A_log), L.ptr(Dp),
-                   L.ptr(cw), L.ptr(cb), None, None, L.ptr(y), es, L.ptr(cf), L.ptr(sf), B, Lq, es, n, 4, L.BF16,
-                   L.stream_ptr())
+            L.call("mtp_scan_prefill", L.ptr(xz), 2 * es, L.ptr(dt), es, L.dtype_code(dt.dtype), L.ptr(bc), 2 * n,
+                   L.ptr(A_log), L.ptr(Dp), L.ptr(cw), L.ptr(cb), None, None, L.ptr(y), es, L.ptr(cf), L.ptr(sf), B, Lq,
+                   es, n, 4, L.BF16, L.stream_ptr())
 
     ms = _time(run, a.warmup, a.iters)
     # algorithmic bytes: x, z, y (bf16) and dt fp32 (or dt_low bf16 when fused), B|C fp32, states
-    dt_bytes = R * 2 if a.fused else es * 4
+    dt_bytes = R * 2 if a.fused else es * dt.element_size()
     nbytes = T * (es * 3 * 2 + dt_bytes + 2 * n * 4) + B * es * (n * 4 + 3 * 2)
     gbs = nbytes / (ms / 1e3) / 1e9
     exps = T * es * n
@@ -274,6 +274,7 @@ def main():
     s.add_argument("--channels", type=int, default=4096)
     s.add_argument("--rank", type=int, default=128, help="dt_rank (fused variant)")
     s.add_argument("--fused", action="store_true", help="dt_proj + softplus inside the scan (tcgen05)")
+    s.add_argument("--dt", choices=["bf16", "f32"], default="bf16", help="dt element type (unfused scan)")
     st = sub.add_parser("step")
     st.add_argument("--batch", type=int, default=32)
     st.add_argument("--channels", type=int, default=4096)

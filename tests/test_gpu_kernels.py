@@ -93,15 +93,21 @@ def _ssm_inputs(b, l, es, nst, seed, dtype):
 
 @pytest.mark.parametrize("dtype", [torch.float32, BF])
 @pytest.mark.parametrize("b,l,es,nst,init", [(2, 37, 64, 16, True), (1, 70, 200, 16, False), (3, 5, 96, 8, True),
-                                               (4, 129, 1024, 16, True), (2, 2, 32, 16, False)])
-def test_scan_prefill_matches_oracle(dtype, b, l, es, nst, init):
+                                               (4, 129, 1024, 16, True), (2, 2, 32, 16, False), (1, 9, 98, 16, True)])
+@pytest.mark.parametrize("dt_in_model_dtype", [False, True])
+def test_scan_prefill_matches_oracle(dtype, b, l, es, nst, init, dt_in_model_dtype):
+    if dt_in_model_dtype and dtype == torch.float32:
+        pytest.skip("fp32 model: dt is fp32 either way")
     x, z, dt, Bm, Cm, A_log, Dp, cw, cb, ci, si = _ssm_inputs(b, l, es, nst, 5, dtype)
     if not init:
         ci = si = None
+    dt_dtype = dtype if dt_in_model_dtype else torch.float32
+    if dt_in_model_dtype:  # the kernel widens bf16 dt exactly: give the oracle the same values
+        dt = O.bf16_round(dt)
     y_ref, cf_ref, sf_ref = O.scan_ref(x, z, dt, Bm, Cm, A_log, Dp, cw, cb, ci, si)
     T = b * l
     xz = t(np.concatenate([x, z], -1).reshape(T, 2 * es), dtype)
-    dtt = t(dt.reshape(T, es))
+    dtt = t(dt.reshape(T, es), dt_dtype)
     bc = t(np.concatenate([Bm, Cm], -1).reshape(T, 2 * nst))
     y = torch.empty(T, es, device=dev(), dtype=dtype)
     cf = torch.empty(b, es, 3, device=dev(), dtype=dtype)
@@ -109,7 +115,8 @@ def test_scan_prefill_matches_oracle(dtype, b, l, es, nst, init):
     # keep every argument tensor alive until the kernel has run
     args = [t(A_log, dtype), t(Dp, dtype), t(cw, dtype), t(cb, dtype), None if ci is None else t(ci, dtype),
             None if si is None else t(si)]
-    L.call("mtp_scan_prefill", L.ptr(xz), 2 * es, L.ptr(dtt), es, L.ptr(bc), 2 * nst, *[L.ptr(a) for a in args],
+    L.call("mtp_scan_prefill", L.ptr(xz), 2 * es, L.ptr(dtt), es, L.dtype_code(dt_dtype), L.ptr(bc), 2 * nst,
+           *[L.ptr(a) for a in args],
            L.ptr(y), es, L.ptr(cf), L.ptr(sf), b, l, es, nst, 4, L.dtype_code(dtype), L.stream_ptr())
     torch.cuda.synchronize()
     tol = 2e-4 if dtype == torch.float32 else 2e-2
