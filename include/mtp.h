@@ -168,6 +168,12 @@ int mtp_comm_destroy(mtp_comm *c);
  * after a synchronize; a timed-out reduction leaves its outputs undefined). */
 int mtp_comm_status(mtp_comm *c, int *status);
 int mtp_comm_reset_status(mtp_comm *c);
+/* Launch shape of the context's reductions: max_ctas > 0 caps a reduction's grid at
+ * max_ctas CTAs and selects the low-register kernel variant, so a reduction can run
+ * on the SMs beside a GEMM or scan of another stream (compute/communication overlap
+ * across micro-batches); 0 restores the default (one CTA per SM, register rows).
+ * Results are bit-identical either way. */
+int mtp_comm_set_max_ctas(mtp_comm *c, int max_ctas);
 
 /* AllReduce #1 epilogue (tp_model.py:106-108, :159-161): sum the fp32
  * partial [rows, R+2N] over ranks in `mode`, round the sums to dt_dtype (the

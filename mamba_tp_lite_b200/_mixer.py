@@ -33,6 +33,26 @@ from .tp_utils import KERNEL_MODES, comm_for, count_collective, torch_allreduce
 # (start_event, end_event, work) with work = algorithmic FLOPs (GEMMs) or bytes (scan).
 PROFILE = None
 
+# Set by the LM driver while it runs micro-batches on separate streams
+# (_LMKernels._prefill_overlapped): every reduction is then issued on this one
+# communication stream, in the host's order, between event waits on the calling
+# stream; the driver accounts the collectives itself (full-batch shapes).
+OVERLAP_STREAM = None
+
+
+def _on_comm_stream(fn, tensors) -> None:
+    """Runs ``fn`` (which launches on the current stream) on OVERLAP_STREAM after
+    the calling stream's work, and makes the calling stream wait for it."""
+    cur = torch.cuda.current_stream()
+    cs = OVERLAP_STREAM
+    cs.wait_stream(cur)
+    with torch.cuda.stream(cs):
+        fn()
+    for t in tensors:
+        if t is not None:
+            t.record_stream(cs)
+    cur.wait_stream(cs)
+
 
 def _prof_begin():
     if PROFILE is None:
@@ -83,14 +103,22 @@ class MixerKernels:
         ctx = None
         mode = L.RED_FP32
         if name is not None:
-            count_collective(self.comm, name, partial.shape, self._dt())
+            if OVERLAP_STREAM is None:
+                count_collective(self.comm, name, partial.shape, self._dt())
             if name in KERNEL_MODES:
                 mode = KERNEL_MODES[name]
                 ctx = comm_for(self)
             else:  # out-of-scope variants keep the reference's torch.distributed algorithm
                 partial = torch_allreduce(name, partial.to(self._dt()), self.group).float().contiguous()
-        L.call("mtp_reduce_xproj", ctx, mode, L.ptr(partial), rows, cfg.dt_rank, 2 * cfg.d_state, L.ptr(dt_low),
-               L.dtype_code(dt_low.dtype), L.ptr(bc), L.stream_ptr())
+
+        def launch():
+            L.call("mtp_reduce_xproj", ctx, mode, L.ptr(partial), rows, cfg.dt_rank, 2 * cfg.d_state, L.ptr(dt_low),
+                   L.dtype_code(dt_low.dtype), L.ptr(bc), L.stream_ptr())
+
+        if OVERLAP_STREAM is not None:
+            _on_comm_stream(launch, (partial, dt_low, bc))
+        else:
+            launch()
 
     def _reduce_out(self, partial, resid, norm_w, eps, normed):
         """AllReduce #2 (tp_model.py:132-134) fused with the bias, the block
@@ -100,7 +128,8 @@ class MixerKernels:
         ctx = None
         mode = L.RED_FP32
         if name is not None:
-            count_collective(self.comm, name, partial.shape, self._dt())
+            if OVERLAP_STREAM is None:
+                count_collective(self.comm, name, partial.shape, self._dt())
             if name in KERNEL_MODES:
                 mode = KERNEL_MODES[name]
                 ctx = comm_for(self)
@@ -108,8 +137,15 @@ class MixerKernels:
                 partial = torch_allreduce(name, partial.to(self._dt()), self.group).float().contiguous()
         bias = self._out_bias()
         odt = normed.dtype if normed is not None else self._dt()
-        L.call("mtp_reduce_outproj", ctx, mode, L.ptr(partial), rows, d, L.ptr(bias), L.ptr(resid), L.ptr(norm_w),
-               float(eps), L.ptr(normed), L.dtype_code(odt), L.stream_ptr())
+
+        def launch():
+            L.call("mtp_reduce_outproj", ctx, mode, L.ptr(partial), rows, d, L.ptr(bias), L.ptr(resid), L.ptr(norm_w),
+                   float(eps), L.ptr(normed), L.dtype_code(odt), L.stream_ptr())
+
+        if OVERLAP_STREAM is not None:
+            _on_comm_stream(launch, (partial, resid, normed))
+        else:
+            launch()
 
     def _fused_dt_ok(self) -> bool:
         """The fused dt_proj + scan kernel (opt-in, MTP_FUSED_DT=1): bf16 models
@@ -121,10 +157,24 @@ class MixerKernels:
                 and cfg.dt_rank % 8 == 0 and cfg.dt_rank <= 256 and os.environ.get("MTP_FUSED_DT", "0") == "1")
 
     # ------------------------------------------------------------ prefill core
-    def _prefill_core(self, xn, B, Lq, conv_init, ssm_init, resid, norm_w=None, eps=0.0, normed=None):
+    def _prefill_core(self, xn, B, Lq, conv_init, ssm_init, resid, norm_w=None, eps=0.0, normed=None,
+                      conv_out=None, ssm_out=None):
         """xn [T, D] (model dtype, RMS-normed block input).  Adds the mixer
         output into ``resid`` [T, D] fp32 and, when ``normed`` is given, writes
-        RMSNorm(resid) * norm_w into it.  Returns (conv_final, ssm_final)."""
+        RMSNorm(resid) * norm_w into it.  Returns (conv_final, ssm_final),
+        written into ``conv_out`` / ``ssm_out`` when given."""
+        g = self._prefill_stages(xn, B, Lq, conv_init, ssm_init, resid, norm_w, eps, normed, conv_out, ssm_out)
+        next(g)
+        try:
+            next(g)
+        except StopIteration as done:
+            return done.value
+        raise RuntimeError("prefill stages did not finish")
+
+    def _prefill_stages(self, xn, B, Lq, conv_init, ssm_init, resid, norm_w=None, eps=0.0, normed=None,
+                        conv_out=None, ssm_out=None):
+        """_prefill_core as a generator: it yields once, after AllReduce #1 has been
+        issued, so a driver can interleave the launches of several micro-batches."""
         cfg = self.cfg
         es, n, r, k = self.es, cfg.d_state, cfg.dt_rank, cfg.d_conv
         T = xn.shape[0]
@@ -143,9 +193,10 @@ class MixerKernels:
         dt_low = torch.empty(T, r, device=dev, dtype=dt_)
         bc = torch.empty(T, 2 * n, device=dev, dtype=torch.float32)
         self._reduce_x(partial_x, dt_low, bc)
+        yield
         y = torch.empty(T, es, device=dev, dtype=dt_)
-        conv_final = torch.empty(B, es, k - 1, device=dev, dtype=dt_)
-        ssm_final = torch.empty(B, es, n, device=dev, dtype=torch.float32)
+        conv_final = conv_out if conv_out is not None else torch.empty(B, es, k - 1, device=dev, dtype=dt_)
+        ssm_final = ssm_out if ssm_out is not None else torch.empty(B, es, n, device=dev, dtype=torch.float32)
         esz = xz.element_size()
         if self._fused_dt_ok():
             # dt_proj + softplus inside the scan kernel (tensor cores); no dt round trip

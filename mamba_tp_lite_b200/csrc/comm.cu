@@ -187,9 +187,45 @@ __device__ __forceinline__ void st_any(void *p, int dtype, size_t i, float v) {
   else ((__nv_bfloat16 *)p)[i] = __float2bfloat16_rn(v);
 }
 
+// Sum of squares of 4 consecutive residual values, rounded explicitly so that every
+// kernel variant that gives a lane the same columns computes the same RMS bits.
+__device__ __forceinline__ float sq4(float4 h) {
+  float t = __fmul_rn(h.x, h.x);
+  t = __fmaf_rn(h.y, h.y, t);
+  t = __fmaf_rn(h.z, h.z, t);
+  return __fmaf_rn(h.w, h.w, t);
+}
+
 // `val` is the reduced row (fp32, in global scratch or the gather buffer); read with __ldcg.
+// With cols % 4 == 0 lane l owns columns 4l + 128i .. +3, as the register-row kernel.
 template <int EPI>
 __device__ __forceinline__ void epilogue_row(const EpiOut &e, const float *val, int r, int cols, int lane) {
+  if (EPI == EPI_OUTPROJ && (cols & 3) == 0) {
+    float ss = 0.f;
+    float *res = e.resid + (size_t)r * cols;
+    for (int c = lane * 4; c < cols; c += 128) {
+      float4 v = __ldcg(reinterpret_cast<const float4 *>(val + c));
+      if (e.bias) {
+        v.x += ld_any(e.bias, e.out_dtype, c); v.y += ld_any(e.bias, e.out_dtype, c + 1);
+        v.z += ld_any(e.bias, e.out_dtype, c + 2); v.w += ld_any(e.bias, e.out_dtype, c + 3);
+      }
+      const float4 h0 = *reinterpret_cast<const float4 *>(res + c);
+      const float4 h = make_float4(h0.x + v.x, h0.y + v.y, h0.z + v.z, h0.w + v.w);
+      *reinterpret_cast<float4 *>(res + c) = h;
+      ss = __fadd_rn(ss, sq4(h));
+    }
+    if (e.normed) {
+      const float rs = rsqrtf(warp_sum(ss) / (float)cols + e.eps);
+      for (int c = lane * 4; c < cols; c += 128) {
+        const float4 h = *reinterpret_cast<const float4 *>(res + c);
+        const float hv[4] = {h.x, h.y, h.z, h.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          st_any(e.normed, e.out_dtype, (size_t)r * cols + c + q, ld_any(e.norm_w, e.out_dtype, c + q) * (hv[q] * rs));
+      }
+    }
+    return;
+  }
   if (EPI == EPI_PLAIN) {
     for (int c = lane; c < cols; c += 32) e.out[(size_t)r * cols + c] = __ldcg(val + c);
   } else if (EPI == EPI_XPROJ) {
@@ -534,7 +570,7 @@ __device__ __forceinline__ void epilogue_v(const EpiOut &e, RowV<VPL> &R, int r,
       const float4 h0 = *reinterpret_cast<const float4 *>(res + c);
       const float4 h = make_float4(h0.x + v.x, h0.y + v.y, h0.z + v.z, h0.w + v.w);
       *reinterpret_cast<float4 *>(res + c) = h;
-      ss += h.x * h.x + h.y * h.y + h.z * h.z + h.w * h.w;
+      ss = __fadd_rn(ss, sq4(h));
       R.v[i] = h;
     }
     if (e.normed) {
@@ -734,8 +770,10 @@ static int run_reduce(mtp_comm *c, int site, int mode, const float *partial, int
     int G = ceil_div(nr, WPB);
     if (G > sms) G = sms;
     if (G > G_MAX) G = G_MAX;
+    const bool capped = has_comm && c->max_ctas > 0;
+    if (capped && G > c->max_ctas) G = c->max_ctas;
     float *scr = nullptr;
-    if (cols % 4 != 0 || cols > 3072) {
+    if (cols % 4 != 0 || cols > 3072 || capped) {
       scr = row_scratch((size_t)G * WPB * cols * sizeof(float));
       if (!scr) return fail(MTP_ERR_CUDA, "could not allocate reduction scratch");
     }
@@ -771,7 +809,7 @@ static int run_reduce(mtp_comm *c, int site, int mode, const float *partial, int
     }
     const float *pp = partial + (size_t)r0 * cols;
     // register-row kernel when the width allows it
-    const int vpl = (cols % 4 != 0) ? 0 : cols <= 256 ? 2 : cols <= 512 ? 4 : cols <= 1024 ? 8 : cols <= 2048 ? 16 : cols <= 3072 ? 24 : 0;
+    const int vpl = (cols % 4 != 0 || capped) ? 0 : cols <= 256 ? 2 : cols <= 512 ? 4 : cols <= 1024 ? 8 : cols <= 2048 ? 16 : cols <= 3072 ? 24 : 0;
     if (vpl) {
       int Gv = ceil_div(nr, WPB);
       const int cap = has_comm ? (sms < G_MAX ? sms : G_MAX) : sms * 8;
@@ -895,6 +933,12 @@ int mtp_comm_status(mtp_comm *c, int *status) {
   MTP_REQUIRE(c && status, "null argument");
   if (cudaMemcpy(status, c->base + c->d.off_status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
     return fail(MTP_ERR_CUDA, "reading the comm status failed");
+  return MTP_OK;
+}
+
+int mtp_comm_set_max_ctas(mtp_comm *c, int max_ctas) {
+  MTP_REQUIRE(c && max_ctas >= 0, "bad arguments");
+  c->max_ctas = max_ctas;
   return MTP_OK;
 }
 

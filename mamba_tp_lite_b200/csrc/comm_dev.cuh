@@ -33,6 +33,7 @@ struct mtp_comm {
   char *base = nullptr;
   size_t total = 0;
   int max_rows = 0, cols[2] = {0, 0};
+  int max_ctas = 0;  // > 0: cap on a reduction's grid, low-register kernel (runs beside compute kernels)
   bool opened = false;
   cudaIpcMemHandle_t handle;
 };

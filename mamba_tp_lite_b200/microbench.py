@@ -156,6 +156,8 @@ def bench_allreduce(a):
     x[:, torch.randperm(cols, device="cuda", generator=g)[: max(1, cols // 100)]] *= 20
     out = torch.empty_like(x)
     comm = Comm(None, rank, ws, cols, cols, max_rows=max(rows, 1)) if ws > 1 else None
+    if comm is not None and a.max_ctas:
+        comm.set_max_ctas(a.max_ctas)
     mode = {"fp32": L.RED_FP32, "fp16": L.RED_FP16, "int8": L.RED_INT8TOK}[a.mode]
 
     def run():
@@ -179,7 +181,8 @@ def bench_allreduce(a):
         sent = rows * per_row * (ws - 1) / ws + rows * cols * 4 * (ws - 1) / ws
     else:
         sent = rows * per_row * (ws - 1)
-    res = {"kernel": f"allreduce_{a.mode}", "ws": ws, "rows": rows, "cols": cols, "avg_us": ms * 1e3,
+    res = {"kernel": f"allreduce_{a.mode}", "ws": ws, "rows": rows, "cols": cols, "max_ctas": a.max_ctas,
+           "avg_us": ms * 1e3,
            "protocol": "two-shot" if two_shot else "one-shot", "nvlink_bytes_sent_per_rank": sent,
            "nvlink_GBps_per_direction": sent / (ms / 1e3) / 1e9 if sent else 0.0,
            "frac_of_770": (sent / (ms / 1e3) / 1e9) / 770.0 if sent else 0.0}
@@ -284,6 +287,7 @@ def main():
     r.add_argument("--cols", type=int, default=2048)
     r.add_argument("--mode", choices=["fp32", "fp16", "int8"], default="int8")
     r.add_argument("--nccl", action="store_true", help="also time the NCCL collective of the reference path")
+    r.add_argument("--max-ctas", type=int, default=0, help="cap the reduction grid (low-register kernel)")
     dcd = sub.add_parser("decode")
     dcd.add_argument("--shape", default="1.4b")
     dcd.add_argument("--layers", type=int, default=0, help="override n_layer (0: the shape's)")

@@ -131,6 +131,17 @@ class MambaBlock(nn.Module):
         return x_t + self.mixer.step(self.norm(x_t), cache)
 
 
+_STREAMS: dict = {}
+
+
+def _side_streams(dev, count: int):
+    """Streams of this device kept for the process (a prefill forks onto them)."""
+    key = (torch.device(dev).index, count)
+    if key not in _STREAMS:
+        _STREAMS[key] = [torch.cuda.Stream(device=dev) for _ in range(count)]
+    return _STREAMS[key]
+
+
 class _LMKernels:
     """Fused LM forward shared by MambaLM and TPMambaLM: embedding gather, one
     normed activation buffer and an fp32 residual stream that each layer's
@@ -167,11 +178,99 @@ class _LMKernels:
         _mixer._prof_end(ev, "lm_head", 2.0 * normed.shape[0] * w.shape[0] * w.shape[1])
         return logits
 
+    def _overlap_split(self, b: int, l: int):
+        """Micro-batch split of a prefill for compute/communication overlap, or None.
+        Opt-in (MTP_PREFILL_OVERLAP=1): for models that run collectives over a comm
+        context (world size > 1, every site in a kernel wire format) and batches of
+        at least 2 sequences.  Off by default: the reduction kernel needs most SMs to
+        reach its bandwidth (1.4b TP=2 on B200: 160 ms per prefill step overlapped
+        vs 139 ms serial), so the overlap does not pay yet; results are bit-identical."""
+        from .tp_utils import KERNEL_MODES
+
+        if os.environ.get("MTP_PREFILL_OVERLAP", "0") != "1" or b < 2 or b * l < 2048:
+            return None
+        for blk in self.layers:
+            m = blk.mixer
+            if m._site_modes is None or m.world_size < 2:
+                return None
+            if any(m._site_modes[s] not in KERNEL_MODES for s in ("x_proj", "out_proj")):
+                return None
+        return [(0, b // 2), (b // 2, b)]
+
+    def _prefill_overlapped(self, normed, resid, b, l, cache, split):
+        """Runs the layers for micro-batches (contiguous groups of sequences) on
+        separate streams.  Each micro-batch's collectives go to one communication
+        stream in the order: for every layer, micro-batch k's AllReduce #2 and then
+        its next layer's AllReduce #1, alternating k; so the reductions of one
+        micro-batch run while the other computes (one spin-waiting kernel at a
+        time on the comm stream, the same order on every rank)."""
+        from . import _mixer
+        from .tp_utils import comm_for, count_collective, get_comm
+
+        cfg = self.cfg
+        eps = cfg.layer_norm_epsilon
+        dev = resid.device
+        m0 = self.layers[0].mixer
+        es, k, n = m0.es, cfg.d_conv, cfg.d_state
+        dt_ = self._param_dtype()
+        T = b * l
+        for blk in self.layers:  # the reference's accounting: one call per site per layer, full batch
+            m = blk.mixer
+            count_collective(m.comm, m._site_modes["x_proj"], (T, cfg.dt_rank + 2 * n), m._dt())
+            count_collective(m.comm, m._site_modes["out_proj"], (T, cfg.d_model), m._dt())
+        conv_all = [torch.empty(b, es, k - 1, device=dev, dtype=dt_) for _ in self.layers]
+        ssm_all = [torch.empty(b, es, n, device=dev, dtype=torch.float32) for _ in self.layers]
+        cur = torch.cuda.current_stream()
+        streams = _side_streams(dev, len(split) + 1)
+        comm_stream, mb_streams = streams[0], streams[1:]
+        comm_for(m0)  # creates the context outside the fork if needed (collective on first use)
+        ctx = get_comm(m0.group, m0.rank, m0.world_size, cfg.dt_rank + 2 * n, cfg.d_model)
+
+        def run(b0, b1):
+            r0, r1 = b0 * l, b1 * l
+            xn, rs = normed[r0:r1], resid[r0:r1]
+            for i, blk in enumerate(self.layers):
+                lc = cache.layers[i] if cache is not None else None
+                ci = lc.conv_state[b0:b1] if lc is not None else None
+                si = lc.ssm_state[b0:b1].float().contiguous() if lc is not None else None
+                g = blk.mixer._prefill_stages(xn, b1 - b0, l, ci, si, rs, self._next_norm_w(i), eps, xn,
+                                              conv_all[i][b0:b1], ssm_all[i][b0:b1])
+                next(g)
+                yield
+                for _ in g:
+                    pass
+
+        for st in streams:
+            st.wait_stream(cur)
+        gens = [run(b0, b1) for b0, b1 in split]
+        _mixer.OVERLAP_STREAM = comm_stream
+        ctx.set_max_ctas(int(os.environ.get("MTP_OVERLAP_COMM_CTAS", "32")))
+        try:
+            live = list(range(len(gens)))
+            while live:
+                for j in list(live):
+                    with torch.cuda.stream(mb_streams[j]):
+                        try:
+                            next(gens[j])
+                        except StopIteration:
+                            live.remove(j)
+        finally:
+            _mixer.OVERLAP_STREAM = None
+            ctx.set_max_ctas(0)
+        for st in streams:
+            cur.wait_stream(st)
+        return [LayerCache(conv_state=c, ssm_state=sm) for c, sm in zip(conv_all, ssm_all)]
+
     def _forward_prefill(self, input_ids: torch.Tensor, cache=None):
         b, l = input_ids.shape
         resid = self._embed(input_ids)
         normed = torch.empty(resid.shape, device=resid.device, dtype=self._param_dtype())
         self._norm_into(resid, self.layers[0].norm.weight, normed)
+        split = self._overlap_split(b, l)
+        if split is not None:
+            new_layers = self._prefill_overlapped(normed, resid, b, l, cache, split)
+            logits = self._lm_head(normed)
+            return logits.view(b, l, -1), MambaCache(new_layers)
         eps = self.cfg.layer_norm_epsilon
         new_layers = []
         for i, layer in enumerate(self.layers):

@@ -143,6 +143,10 @@ class Comm:
     def reset_status(self) -> None:
         L.call("mtp_comm_reset_status", self.handle)
 
+    def set_max_ctas(self, max_ctas: int) -> None:
+        """Caps the grid of this context's reductions (0: default); see mtp_comm_set_max_ctas."""
+        L.call("mtp_comm_set_max_ctas", self.handle, int(max_ctas))
+
     def check(self) -> None:
         """Raises if a bounded wait of a reduction timed out (after a synchronize)."""
         torch.cuda.synchronize()

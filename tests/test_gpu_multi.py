@@ -282,8 +282,9 @@ def _protocol_worker(rank, init_file, q):
         part = torch.randn(rows, d, generator=torch.Generator().manual_seed(7 + rank)).cuda() * 2
         w = torch.randn(d, generator=torch.Generator().manual_seed(9)).cuda().to(torch.bfloat16)
         res = {}
-        for proto in ("oneshot", "twoshot"):
-            os.environ["MTP_COMM_PROTOCOL"] = proto
+        for proto in ("oneshot", "twoshot", "capped"):
+            os.environ["MTP_COMM_PROTOCOL"] = "oneshot" if proto == "capped" else proto
+            comm.set_max_ctas(16 if proto == "capped" else 0)
             for mode in (L.RED_FP32, L.RED_FP16, L.RED_INT8TOK):
                 resid = torch.ones(rows, d, device="cuda")
                 normed = torch.empty(rows, d, device="cuda", dtype=torch.bfloat16)
@@ -305,3 +306,50 @@ def test_two_shot_bf16_gather_equals_one_shot():
         a, b = res[0][("oneshot", mode)], res[0][("twoshot", mode)]
         assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1]), mode
         assert np.array_equal(res[1][("twoshot", mode)][0], b[0])
+        c = res[0][("capped", mode)]  # 16 CTAs, low-register kernel: same bits
+        assert np.array_equal(a[0], c[0]) and np.array_equal(a[1], c[1]), mode
+
+
+# ------------------------------------------------------------------ overlapped micro-batch prefill == serial prefill
+def _overlap_worker(rank, init_file, q):
+    try:
+        _init(rank, init_file)
+        from mamba_tp_lite_b200.checkpoint import random_init_state_dict
+        from mamba_tp_lite_b200.config import MambaConfig
+        from mamba_tp_lite_b200.tp_model import TPMambaLM
+        from mamba_tp_lite_b200.tp_utils import build_spec
+
+        cfg = MambaConfig(d_model=256, n_layer=3, vocab_size=1000, dt_rank=16)
+        sd = random_init_state_dict(cfg, seed=8, dtype=torch.bfloat16)
+        spec = build_spec({"default": "int8", "overrides": {"0:out_proj": "fp16", "1:x_proj": "fp32"}}, cfg.n_layer)
+        m = TPMambaLM.from_state_dict_shard(cfg, sd, rank, WS, dtype=torch.bfloat16, allreduce_dtype=spec,
+                                            device="cuda")
+        ids = torch.randint(0, cfg.vocab_size, (5, 520), generator=torch.Generator().manual_seed(9)).cuda()
+        os.environ["MTP_PREFILL_OVERLAP"] = "1"
+        assert m._overlap_split(5, 520) is not None
+        out = {}
+        for mode in ("1", "0"):
+            os.environ["MTP_PREFILL_OVERLAP"] = mode
+            c0 = m.layers[0].mixer.comm.count
+            lg, cache = m.prefill(ids)
+            lg2, _ = m.prefill(ids[:, :7], cache)  # chunked continuation from the overlapped cache
+            out[mode] = (lg.float().cpu().numpy(), lg2.float().cpu().numpy(),
+                         [(lc.conv_state.float().cpu().numpy(), lc.ssm_state.cpu().numpy()) for lc in cache.layers],
+                         m.layers[0].mixer.comm.count - c0)
+        os.environ.pop("MTP_PREFILL_OVERLAP")
+        q.put((rank, out))
+        _finish()
+    except Exception as e:
+        q.put((rank, f"{type(e).__name__}: {e}"))
+
+
+@needs2
+def test_overlapped_prefill_bit_exact_vs_serial():
+    res = _spawn(_overlap_worker)
+    for r in range(WS):
+        a, b = res[r]["1"], res[r]["0"]
+        assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+        for (c1, s1), (c2, s2) in zip(a[2], b[2]):
+            assert np.array_equal(c1, c2) and np.array_equal(s1, s2)
+        assert a[3] == b[3] == 2 * 2  # the reference's accounting: 2 sites, 2 prefills
+    assert np.array_equal(res[0]["1"][0], res[1]["1"][0])
