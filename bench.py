@@ -276,7 +276,9 @@ def run_ours(a):
     if top == "scan":
         ach = k["work"] / (k["avg_ms"] / 1000.0) / 1e9
         roofline = {"kernel": "scan_prefill", "bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"],
-                    "unit": "GB/s", "frac": ach / peaks["hbm_gbs"], "peak_source": f"{peak_src} HBM copy"}
+                    "unit": "GB/s", "frac": ach / peaks["hbm_gbs"], "peak_source": f"{peak_src} HBM copy",
+                    "limiter": "MUFU exp rate (20 SFU ops per token-channel; ncu: XU pipe 63% of peak, "
+                               "DRAM traffic = algorithmic bytes), see profiles/scan_prefill_1p4b.md"}
     else:
         ach = k["work"] / (k["avg_ms"] / 1000.0) / 1e12
         roofline = {"kernel": f"gemm_tc ({top})", "bound": "tensor", "achieved": ach, "peak": pk, "unit": "TFLOP/s",

@@ -598,7 +598,7 @@ __device__ __forceinline__ void epilogue_v(const EpiOut &e, RowV<VPL> &R, int r,
 }
 
 template <int MODE, int EPI, int VPL>
-__global__ void __launch_bounds__(WPB * 32) reduce_rows_kernel(CommDev d, bool has_comm, int site,
+__global__ void __launch_bounds__(WPB * 32, (VPL >= 16 ? 2 : 3)) reduce_rows_kernel(CommDev d, bool has_comm, int site,
                                                                const float *__restrict__ partial, int rows, int cols,
                                                                bool two_shot, EpiOut e) {
   MTP_PDL_WAIT();
@@ -750,6 +750,23 @@ static float *row_scratch(size_t bytes) {
   return g_scratch;
 }
 
+// Resident CTAs per SM of a register-row kernel instance (queried once).  With a comm
+// context the grid is sized to fill every SM at that occupancy: CTA j only waits for CTA
+// j of the other ranks, and CTAs are dispatched in index order, so every launched CTA
+// becomes resident once the preceding kernel has drained.
+template <int M, int E, int V>
+static int rows_kernel_occupancy() {
+  static int occ = 0;
+  if (occ == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, reduce_rows_kernel<M, E, V>, WPB * 32, 0) != cudaSuccess ||
+        n < 1)
+      n = 1;
+    occ = n;
+  }
+  return occ;
+}
+
 template <int EPI>
 static int run_reduce(mtp_comm *c, int site, int mode, const float *partial, int rows, int cols, EpiOut e,
                       cudaStream_t s) {
@@ -811,10 +828,15 @@ static int run_reduce(mtp_comm *c, int site, int mode, const float *partial, int
     // register-row kernel when the width allows it
     const int vpl = (cols % 4 != 0 || capped) ? 0 : cols <= 256 ? 2 : cols <= 512 ? 4 : cols <= 1024 ? 8 : cols <= 2048 ? 16 : cols <= 3072 ? 24 : 0;
     if (vpl) {
-      int Gv = ceil_div(nr, WPB);
-      const int cap = has_comm ? (sms < G_MAX ? sms : G_MAX) : sms * 8;
-      if (Gv > cap) Gv = cap;
-#define MTP_RV(M, V) launch_pdl(reduce_rows_kernel<M, EPI, V>, dim3(Gv), dim3(WPB * 32), 0, s, d, has_comm, site, pp, nr, cols, two_shot, ee)
+      const int Gwant = ceil_div(nr, WPB);
+#define MTP_RV(M, V)                                                                                             \
+  do {                                                                                                           \
+    int cap_ = has_comm ? sms * rows_kernel_occupancy<M, EPI, V>() : sms * 8;                                    \
+    if (cap_ > G_MAX && has_comm) cap_ = G_MAX;                                                                  \
+    const int Gv = Gwant < cap_ ? Gwant : cap_;                                                                  \
+    launch_pdl(reduce_rows_kernel<M, EPI, V>, dim3(Gv), dim3(WPB * 32), 0, s, d, has_comm, site, pp, nr, cols,   \
+               two_shot, ee);                                                                                    \
+  } while (0)
 #define MTP_RV_MODE(V)                                      \
   do {                                                      \
     if (mode == MTP_RED_FP32) MTP_RV(MTP_RED_FP32, V);      \

@@ -13,7 +13,7 @@
 namespace mtp {
 
 constexpr int MAX_WS = 8;
-constexpr int G_MAX = 256;
+constexpr int G_MAX = 512;  // CTAs of one reduction launch (flag slots per source rank)
 
 struct CommDev {
   char *peer[MAX_WS];  // base of each rank's allocation (peer[rank] = own)
