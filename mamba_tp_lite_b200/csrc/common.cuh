@@ -64,6 +64,9 @@ __device__ __forceinline__ float softplus_fast(float x) {
 }
 
 
+// SiLU with the hardware exponential and a fast divide, x / (1 + e^-x).
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
 // ----------------------------------------------------------------- timing / waits
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;

@@ -109,20 +109,34 @@ template <> struct Pack16<float> {
 template <typename T, int K, int TT>
 __global__ void conv1d_silu_vec_kernel(const T *__restrict__ xz, int ld_xz, const T *__restrict__ w,
                                        const T *__restrict__ bias, const T *__restrict__ hist, T *__restrict__ xc,
-                                       int ld_xc, int L, int Es) {
+                                       int ld_xc, int L, int Es, bool wvec) {
   MTP_PDL_WAIT();
   MTP_PDL_TRIGGER();
   constexpr int V = Pack16<T>::V;
+  static_assert(V * K * sizeof(T) == 64, "a group's taps are four 16-byte words");
   const int c = (blockIdx.x * blockDim.x + threadIdx.x) * V;
   const int t0 = blockIdx.y * TT;
   const int b = blockIdx.z;
   if (c >= Es) return;
   float wk[V][K], bc[V], win[V][K - 1];
+  if (wvec) {  // the group's V x K taps and V biases as 16-byte loads
+    T tw[V * K], tb[V];
 #pragma unroll
-  for (int u = 0; u < V; ++u) {
+    for (int q = 0; q < 4; ++q) reinterpret_cast<uint4 *>(tw)[q] = __ldg(reinterpret_cast<const uint4 *>(w + (size_t)c * K) + q);
+    if (bias) *reinterpret_cast<uint4 *>(tb) = __ldg(reinterpret_cast<const uint4 *>(bias + c));
 #pragma unroll
-    for (int j = 0; j < K; ++j) wk[u][j] = ldf(w + (size_t)(c + u) * K + j);
-    bc[u] = bias ? ldf(bias + c + u) : 0.f;
+    for (int u = 0; u < V; ++u) {
+#pragma unroll
+      for (int j = 0; j < K; ++j) wk[u][j] = ldf(&tw[u * K + j]);
+      bc[u] = bias ? ldf(&tb[u]) : 0.f;
+    }
+  } else {
+#pragma unroll
+    for (int u = 0; u < V; ++u) {
+#pragma unroll
+      for (int j = 0; j < K; ++j) wk[u][j] = ldf(w + (size_t)(c + u) * K + j);
+      bc[u] = bias ? ldf(bias + c + u) : 0.f;
+    }
   }
 #pragma unroll
   for (int j = 0; j < K - 1; ++j) {
@@ -152,7 +166,7 @@ __global__ void conv1d_silu_vec_kernel(const T *__restrict__ xz, int ld_xz, cons
 #pragma unroll
       for (int j = 0; j < K - 2; ++j) win[u][j] = win[u][j + 1];
       win[u][K - 2] = xv[u];
-      o[u] = silu_f(acc);
+      o[u] = silu_fast(acc);  // as the scan's conv phase
     }
     Pack16<T>::store(xc + (size_t)(b * (size_t)L + t) * ld_xc + c, o);
   }
@@ -180,8 +194,6 @@ __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
 }
 
-// silu with the hardware exponential and a fast divide (x / (1 + e^-x))
-__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 
 template <typename T, typename TD, int N, int TPC, int TL, int K>
@@ -729,12 +741,13 @@ int mtp_conv1d_silu(const void *xz, int ld_xz, const void *conv_w, const void *c
   const int V = (int)(16 / es_b);
   const bool vec = Es % V == 0 && aligned16(xz) && aligned16(xc) && (ld_xz * es_b) % 16 == 0 && (ld_xc * es_b) % 16 == 0;
   if (vec) {
-    constexpr int TT = 16;
+    constexpr int TT = 64;  // positions per thread: the 3-position halo is re-read once per 64
     const int groups = Es / V;
+    const bool wvec = aligned16(conv_w) && (conv_b == nullptr || aligned16(conv_b));
     dim3 grid((groups + 63) / 64, (L + TT - 1) / TT, B);
     MTP_DISPATCH_FB(dtype, T,
         launch_pdl(conv1d_silu_vec_kernel<T, 4, TT>, dim3(grid), dim3(64), 0, s, (const T *)xz, ld_xz, (const T *)conv_w,
-                                                              (const T *)conv_b, (const T *)hist, (T *)xc, ld_xc, L, Es));
+                                                              (const T *)conv_b, (const T *)hist, (T *)xc, ld_xc, L, Es, wvec));
     return check_launch("conv1d_silu");
   }
   constexpr int TT = 8;
