@@ -148,19 +148,14 @@ class MixerKernels:
             launch()
 
     def _fused_dt_ok(self) -> bool:
-        """The fused dt_proj + scan kernel for bf16 models with d_state 16, d_inner
-        per rank divisible by 128 and dt_rank divisible by 8, used when the rank's
-        shard has at most 1024 channels (MTP_FUSED_DT=1 / 0 forces it on / off).
-        Measured on B200 (32 x 1024 tokens, dt_proj GEMM + scan vs fused):
-        4096 channels 1.12 vs 1.47 ms, 2048: 0.80 vs 0.92, 1024: 0.63 vs 0.57,
-        512: 0.44 vs 0.37."""
+        """The fused dt_proj + scan kernel (opt-in, MTP_FUSED_DT=1) for bf16 models
+        with d_state 16, d_inner per rank divisible by 128 and dt_rank divisible
+        by 8.  Off by default: on B200 (32 x 1024 tokens) the dt_proj GEMM plus
+        the scan is faster at every shard width: 4096 channels 1.12 vs 1.47 ms,
+        2048: 0.64 vs 0.92, 1024: 0.40 vs 0.57, 512: 0.32 vs 0.37."""
         cfg = self.cfg
-        ok = (self._dt() == torch.bfloat16 and cfg.d_state == 16 and cfg.d_conv == 4 and self.es % 128 == 0
-              and cfg.dt_rank % 8 == 0 and cfg.dt_rank <= 256)
-        force = os.environ.get("MTP_FUSED_DT")
-        if force is not None:
-            return ok and force == "1"
-        return ok and self.es <= 1024
+        return (self._dt() == torch.bfloat16 and cfg.d_state == 16 and cfg.d_conv == 4 and self.es % 128 == 0
+                and cfg.dt_rank % 8 == 0 and cfg.dt_rank <= 256 and os.environ.get("MTP_FUSED_DT", "0") == "1")
 
     # ------------------------------------------------------------ prefill core
     def _prefill_core(self, xn, B, Lq, conv_init, ssm_init, resid, norm_w=None, eps=0.0, normed=None,

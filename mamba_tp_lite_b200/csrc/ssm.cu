@@ -775,10 +775,13 @@ int mtp_scan_prefill(const void *xz, int ld_xz, const void *dt, int ld_dt, int d
   MTP_REQUIRE(dt_dtype == MTP_F32 || (ld_dt % 2 == 0 && Es % 2 == 0), "bf16 dt rows need even Es and ld_dt");
   if (B == 0 || L == 0) return MTP_OK;
   cudaStream_t s = (cudaStream_t)stream;
-  // threads per channel: enough resident warps at small channel counts
+  // threads per channel: one (all 16 states in registers) unless there are too few
+  // (sequence, channel) pairs to occupy the SMs.  B200, 32 x 1024 tokens: 2048
+  // channels 0.54 / 0.70 / 0.97 ms for 1 / 2 / 4 threads, 1024: 0.35 / 0.53 / 0.58,
+  // 512: 0.31 / 0.29 / 0.41.
   const long pairs = (long)B * Es;
   const int sms = num_sms();
-  int tpc = pairs >= (long)sms * 512 ? 1 : (pairs >= (long)sms * 256 ? 2 : 4);
+  int tpc = pairs >= (long)sms * 128 ? 1 : (pairs >= (long)sms * 32 ? 2 : 4);
   // tuning override: MTP_SCAN_TPC = 1, 2 or 4 threads per channel
   if (const char *env = getenv("MTP_SCAN_TPC")) {
     const int v = atoi(env);
