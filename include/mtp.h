@@ -252,9 +252,9 @@ int mtp_decode_status(mtp_decode_plan *plan, int *status);
 /* Clears the barrier, abort and status words after a timeout. */
 int mtp_decode_reset(mtp_decode_plan *plan);
 /* Phase timing of later steps (off by default): with tracing on, each step stores
- * %globaltimer stamps, nb = 2 + 5 n_layer barriers: out[0] = start, out[k] = when
- * CTA 0 left barrier k, out[nb + k] = when the last CTA arrived at barrier k
- * (k = 1..nb-1; barrier 1 ends the embedding phase, then five per layer). */
+ * nb = 2 + 5 n_layer %globaltimer stamps of CTA 0: out[0] = start, out[1] = end of
+ * the embedding phase, then the end of each of the five phases of every layer
+ * (in_proj+conv, x_proj, AllReduce #1 + step, out_proj, AllReduce #2 + norm). */
 int mtp_decode_set_trace(mtp_decode_plan *plan, int on);
 int mtp_decode_read_trace(mtp_decode_plan *plan, uint64_t *out, int capacity, int *n_out);
 void mtp_decode_cache_destroy(mtp_decode_cache *cache);

@@ -120,20 +120,19 @@ class DecodePlan:
         L.call("mtp_decode_set_trace", self.handle, 1 if on else 0)
 
     def phase_times_us(self) -> dict:
-        """Per-phase durations of the last traced step, summed over layers (us):
-        'work' from the previous barrier to the last CTA's arrival, 'barrier' from
-        that arrival to CTA 0 leaving."""
+        """Per-phase durations of the last traced step as seen by CTA 0, summed over
+        layers (us): the time from the end of its previous phase to the end of this
+        one, waits for other CTAs' data included."""
         nb = 2 + 5 * self.n_layer
-        buf = (C.c_uint64 * (2 * nb))()
+        buf = (C.c_uint64 * nb)()
         cnt = C.c_int(0)
-        L.call("mtp_decode_read_trace", self.handle, buf, 2 * nb, C.byref(cnt))
+        L.call("mtp_decode_read_trace", self.handle, buf, nb, C.byref(cnt))
         t = [int(v) for v in buf]
         names = ["in_proj+conv", "x_proj", "allreduce1+step", "out_proj", "allreduce2+norm"]
-        out = {"embed": (t[nb + 1] - t[0]) / 1e3, "barrier": (t[1] - t[nb + 1]) / 1e3}
+        out = {"embed": (t[1] - t[0]) / 1e3}
         for k in range(2, nb):
             ph = names[(k - 2) % 5]
-            out[ph] = out.get(ph, 0.0) + (t[nb + k] - t[k - 1]) / 1e3
-            out["barrier"] += (t[k] - t[nb + k]) / 1e3
+            out[ph] = out.get(ph, 0.0) + (t[k] - t[k - 1]) / 1e3
         out["total"] = (t[nb - 1] - t[0]) / 1e3
         return out
 

@@ -27,11 +27,12 @@
 //   P5  out_proj row tiles -> fp32 partials
 //   P6  owner CTA b: sum, AllReduce #2, + bias, residual (kept in the owner's registers
 //       for the whole step), next RMSNorm
-// A bounded grid barrier separates P1|P2|P3-4|P5|P6.  Before doing its part of a phase,
+// No grid barrier: each phase waits (bounded) only for the counters / per-row flags of
+// the data it reads (see "dependency counters").  Before doing its part of a phase,
 // each CTA asks L2 to prefetch (cp.async.bulk.prefetch.L2) the weight rows of the units
 // it will process one or two phases later, so HBM streams across the barriers.
 // Every wait is bounded: on expiry the kernel records MTP_ERR_TIMEOUT, raises the abort
-// word, and every CTA returns at its next barrier.
+// word, and every CTA returns at its next wait.
 #include <cstdlib>
 #include <cstring>
 #include <vector>
@@ -72,9 +73,11 @@ struct DecParams {
   unsigned *lflags;  // [B] per-row publication flags (value = local epoch)
   unsigned *lepoch;  // local epoch: one per layer, advanced at the end of each launch
   float *pop;        // [KCo][B][D]
-  unsigned *bar;     // [0] arrivals, [1] exits, [2] abort
+  unsigned *bar;     // [0] unused, [1] exits, [2] abort
+  unsigned *cnt;     // dependency counters (layout: see cnt_* below), zero between launches
+  int ncnt;
   int *err;
-  unsigned long long *trace;  // NULL, or [2][n_barriers + 1] globaltimer stamps (see grid_sync)
+  unsigned long long *trace;  // NULL, or [2 + 5 n_layer] globaltimer stamps of CTA 0 (phase ends)
   int B, D, Es, R, NX, KCx, KCo, chunk_x, chunk_o, xstride;
   float eps;
   int has_comm;
@@ -147,40 +150,69 @@ __device__ __forceinline__ int q_one(float x, float s) {
   return (int)fminf(fmaxf(rintf(__fdiv_rn(x, s)), -127.0f), 127.0f);
 }
 
-// ----------------------------------------------------------------- grid barrier
-// Arrivals count up monotonically within a launch: barrier k completes when the
-// counter reaches (k + 1) * gridDim.x.  The last CTA to leave the kernel resets it.
-__device__ __forceinline__ bool grid_sync(const DecParams &p, unsigned &nbar, int *s_flag) {
+// ----------------------------------------------------------------- dependency counters
+// The phases of a layer hand data to each other through counters and per-row flags
+// instead of grid barriers: a producer CTA finishes a tile (all threads, __syncthreads),
+// then thread 0 fences and adds to the tile's counter; a consumer's thread 0 spins
+// (acquire, bounded by timeout_ns, abandoning on the abort word) until the counter
+// reaches the layer's target, then the CTA reads the data with L2 (.cg) loads.  Every
+// CTA runs the phases in the same order and only waits for work of earlier phases of
+// co-resident CTAs (cooperative launch), so no wait can be part of a cycle.  Counters
+// count cumulatively over the layers of a launch and are reset by the last CTA to exit.
+//   cnt[0, KCx)           in_proj x tiles done per x_proj K chunk   (target (l+1) x tiles in chunk)
+//   cnt[KCx]              in_proj z tiles done                     (target (l+1) x Es/16)
+//   cnt[KCx+1]            x_proj units done                        (target (l+1) x units)
+//   cnt[KCx+2, +KCo)      step tiles done per out_proj K chunk      (target (l+1) x tiles in chunk)
+//   cnt[KCx+2+KCo]        out_proj units done                      (target (l+1) x units)
+//   cnt[KCx+3+KCo, +B)    normed row b ready for layer l           (value l+1)
+__device__ __forceinline__ void raise_abort(const DecParams &p);
+
+__device__ __forceinline__ bool wait_ge(const DecParams &p, const unsigned *ctr, unsigned target, int *s_flag) {
   __syncthreads();
-  ++nbar;
   if (threadIdx.x == 0) {
-    const unsigned target = nbar * gridDim.x;
-    __threadfence();
-    const unsigned prev = atomicAdd(p.bar, 1u);
-    const unsigned long long t0 = globaltimer_ns();
-    // trace: [1][k] = when the last CTA arrived at barrier k, [0][k] = when CTA 0 left it
-    const int nb = 2 + 5 * p.n_layer;
-    if (p.trace && prev == target - 1u) p.trace[nb + nbar] = t0;
-    uint32_t it = 0;
     int ok = 1;
-    while (ld_acquire_gpu(p.bar) < target) {
+    const unsigned long long t0 = globaltimer_ns();
+    uint32_t it = 0;
+    while ((int)(ld_acquire_gpu(ctr) - target) < 0) {
       if ((++it & 31u) == 0) {
         if (ld_acquire_gpu(p.bar + 2)) { ok = 0; break; }
-        if (globaltimer_ns() - t0 > p.timeout_ns) {
-          atomicExch(p.err, MTP_ERR_TIMEOUT);
-          atomicExch(p.bar + 2, 1u);
-          ok = 0;
-          break;
-        }
+        if (globaltimer_ns() - t0 > p.timeout_ns) { raise_abort(p); ok = 0; break; }
       }
     }
     __threadfence();
-    if (ok && ld_acquire_gpu(p.bar + 2)) ok = 0;
-    if (p.trace && blockIdx.x == 0) p.trace[nbar] = globaltimer_ns();
     *s_flag = ok;
   }
   __syncthreads();
   return *s_flag != 0;
+}
+
+// Threads b < n wait for flags[b] >= target.
+__device__ __forceinline__ bool wait_rows(const DecParams &p, const unsigned *flags, int n, unsigned target,
+                                          int *s_flag) {
+  if (threadIdx.x == 0) *s_flag = 1;
+  __syncthreads();
+  if ((int)threadIdx.x < n) {
+    const unsigned long long t0 = globaltimer_ns();
+    uint32_t it = 0;
+    while ((int)(ld_acquire_gpu(flags + threadIdx.x) - target) < 0) {
+      if ((++it & 31u) == 0 && (ld_acquire_gpu(p.bar + 2) || globaltimer_ns() - t0 > p.timeout_ns)) {
+        raise_abort(p);
+        *s_flag = 0;
+        break;
+      }
+    }
+    __threadfence();
+  }
+  __syncthreads();
+  return *s_flag != 0;
+}
+
+// After the CTA's writes (callers end the tile with __syncthreads): publish.
+__device__ __forceinline__ void signal_add(unsigned *ctr, unsigned n) {
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(ctr, n);
+  }
 }
 
 __device__ __forceinline__ void raise_abort(const DecParams &p) {
@@ -424,6 +456,15 @@ __device__ __forceinline__ void prefetch_p2_to_p6(const DecParams &p, const DecL
   }
 }
 
+// True (for the whole CTA) once some wait of the launch has given up.
+__device__ __forceinline__ bool bar_aborted(const DecParams &p) {
+  __shared__ int s_ab;
+  __syncthreads();
+  if (threadIdx.x == 0) s_ab = ld_acquire_gpu(p.bar + 2) != 0u;
+  __syncthreads();
+  return s_ab != 0;
+}
+
 __device__ __forceinline__ void st_release_gpu(unsigned *p, unsigned v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -444,8 +485,11 @@ __global__ void __launch_bounds__(DT, 1) decode_kernel(DecParams p) {
   float *bcs = red + DW * 16 * NTP;  // [B][2N]
   float *dts = bcs + NTP * 2 * DN;   // [16][NTP]
   float *a2s = dts + 16 * NTP;       // [16][N]
-  unsigned nbar = 0;
   if (p.trace && tid == 0 && blockIdx.x == 0) p.trace[0] = globaltimer_ns();
+  auto stamp = [&](int k) {
+    if (p.trace && tid == 0 && blockIdx.x == 0) p.trace[k] = globaltimer_ns();
+  };
+  unsigned *c1 = p.cnt, *cz = p.cnt + p.KCx, *c2 = cz + 1, *c4 = c2 + 1, *c5 = c4 + p.KCo, *nflag = c5 + 1;
   if (tid == 0) {
     s_epoch[0] = p.has_comm ? *reinterpret_cast<volatile uint32_t *>(p.cv.peer[p.cv.rank] + p.cv.off_epoch) : 0u;
     s_epoch[1] = p.has_comm ? *reinterpret_cast<volatile uint32_t *>(p.cv.peer[p.cv.rank] + p.cv.off_epoch + 4) : 0u;
@@ -481,8 +525,13 @@ __global__ void __launch_bounds__(DT, 1) decode_kernel(DecParams p) {
       const int c = tid + q * DT;
       if (c < D) p.normed[(size_t)b * D + c] = __float2bfloat16_rn(ldbf(nw + c) * (resid[q] * rs));
     }
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence();
+      st_release_gpu(nflag + b, 1u);
+    }
   }
-  if (!grid_sync(p, nbar, &s_flag)) return;
+  stamp(1);
 
   for (int l = 0; l < p.n_layer; ++l) {
     const DecLayer Ly = p.layers[l];
@@ -490,7 +539,10 @@ __global__ void __launch_bounds__(DT, 1) decode_kernel(DecParams p) {
     const bf16 *next_norm = l + 1 < p.n_layer ? p.layers[l + 1].norm_w : p.norm_f;
     // ---------------- P1: in_proj + conv
     if (p.prefetch && warp == 0) prefetch_p2_to_p6(p, Ly, Cc, next_norm, lane);
-    if (blockIdx.x < U1) stage_tokens(xs, p.xstride, p.normed, D, B, NTP, 0, D);
+    if (blockIdx.x < U1) {
+      if (!wait_rows(p, nflag, B, (unsigned)l + 1u, &s_flag)) return;  // every token's normed row
+      stage_tokens(xs, p.xstride, p.normed, D, B, NTP, 0, D);
+    }
     __syncthreads();
     for (int u = blockIdx.x; u < U1; u += G) {
       float acc[NT][4];
@@ -521,16 +573,17 @@ __global__ void __launch_bounds__(DT, 1) decode_kernel(DecParams p) {
           p.zT[(size_t)tok * Es + (n - Es)] = __float2bfloat16_rn(xz);
         }
       });
+      signal_add(16 * u < Es ? c1 + (16 * u) / p.chunk_x : cz, 1u);
     }
-    if (!grid_sync(p, nbar, &s_flag)) return;
+    stamp(2 + 5 * l);
     // ---------------- P2: x_proj partials
     if (p.prefetch && warp == 0 && l + 1 < p.n_layer) prefetch_p1(p, p.layers[l + 1], p.cache[l + 1], lane);
     {
       int staged = -1;
       for (int u = blockIdx.x; u < RTx * p.KCx; u += G) {
         const int rt = u % RTx, kc = u / RTx, k0 = kc * p.chunk_x, k1 = min(Es, k0 + p.chunk_x);
-        if (kc != staged) {
-          __syncthreads();
+        if (kc != staged) {  // this K chunk's in_proj x tiles
+          if (!wait_ge(p, c1 + kc, (unsigned)(l + 1) * (unsigned)((k1 - k0) / 16), &s_flag)) return;
           stage_tokens(xs, p.xstride, p.xcT, Es, B, NTP, k0, k1 - k0);
           __syncthreads();
           staged = kc;
@@ -541,14 +594,16 @@ __global__ void __launch_bounds__(DT, 1) decode_kernel(DecParams p) {
           const int n = 16 * rt + row;
           if (tok < B && n < NX) p.pxp[((size_t)kc * B + tok) * NX + n] = v;
         });
+        signal_add(c2, 1u);
       }
     }
-    if (!grid_sync(p, nbar, &s_flag)) return;
+    stamp(3 + 5 * l);
     // ---------------- P3: owner CTA b reduces row b of x_proj (AllReduce #1) and publishes it
     const uint32_t lep = lep0 + (uint32_t)l + 1u;
     if (p.has_comm) ++ep_x;
     if (blockIdx.x < B) {
       const int b = blockIdx.x;
+      if (!wait_ge(p, c2, (unsigned)(l + 1) * (unsigned)(RTx * p.KCx), &s_flag)) return;  // all x_proj units
       float v[2];
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
@@ -603,6 +658,7 @@ __global__ void __launch_bounds__(DT, 1) decode_kernel(DecParams p) {
         }
       }
       __syncthreads();
+      if (s_flag && !wait_ge(p, cz, (unsigned)(l + 1) * (unsigned)(Es / 16), &s_flag)) return;  // z tiles
       if (s_flag) {
         // dt_low (bf16 values) as MMA tokens, B|C rows as fp32
         for (int i = tid; i < NTP * Rp; i += DT) {
@@ -651,17 +707,19 @@ __global__ void __launch_bounds__(DT, 1) decode_kernel(DecParams p) {
             }
           }
           __syncthreads();
+          signal_add(c4 + c0 / p.chunk_o, 1u);
         }
       }
     }
-    if (!grid_sync(p, nbar, &s_flag)) return;
+    if (bar_aborted(p)) return;
+    stamp(4 + 5 * l);
     // ---------------- P5: out_proj partials
     {
       int staged = -1;
       for (int u = blockIdx.x; u < RTo * p.KCo; u += G) {
         const int rt = u % RTo, kc = u / RTo, k0 = kc * p.chunk_o, k1 = min(Es, k0 + p.chunk_o);
-        if (kc != staged) {
-          __syncthreads();
+        if (kc != staged) {  // this K chunk's step tiles
+          if (!wait_ge(p, c4 + kc, (unsigned)(l + 1) * (unsigned)((k1 - k0) / 16), &s_flag)) return;
           stage_tokens(xs, p.xstride, p.yT, Es, B, NTP, k0, k1 - k0);
           __syncthreads();
           staged = kc;
@@ -672,13 +730,15 @@ __global__ void __launch_bounds__(DT, 1) decode_kernel(DecParams p) {
           const int n = 16 * rt + row;
           if (tok < B && n < D) p.pop[((size_t)kc * B + tok) * D + n] = v;
         });
+        signal_add(c5, 1u);
       }
     }
-    if (!grid_sync(p, nbar, &s_flag)) return;
+    stamp(5 + 5 * l);
     // ---------------- P6: AllReduce #2 + bias + residual + next RMSNorm (owner CTA per token)
     if (p.has_comm) ++ep_o;
     if (blockIdx.x < B) {
       const int b = blockIdx.x;
+      if (!wait_ge(p, c5, (unsigned)(l + 1) * (unsigned)(RTo * p.KCo), &s_flag)) return;  // all out_proj units
       float v[VPT_D];
 #pragma unroll
       for (int q = 0; q < VPT_D; ++q) {
@@ -721,9 +781,15 @@ __global__ void __launch_bounds__(DT, 1) decode_kernel(DecParams p) {
           const int c = tid + q * DT;
           if (c < D) p.normed[(size_t)b * D + c] = __float2bfloat16_rn(ldbf(next_norm + c) * (resid[q] * rs));
         }
+        __syncthreads();
+        if (tid == 0) {
+          __threadfence();
+          st_release_gpu(nflag + b, (unsigned)l + 2u);
+        }
       }
     }
-    if (!grid_sync(p, nbar, &s_flag)) return;
+    if (bar_aborted(p)) return;
+    stamp(6 + 5 * l);
   }
   // exit: publish the epochs; the last CTA out resets the barrier counters
   if (tid == 0) {
@@ -735,8 +801,8 @@ __global__ void __launch_bounds__(DT, 1) decode_kernel(DecParams p) {
       *reinterpret_cast<volatile uint32_t *>(p.lepoch) = lep0 + (uint32_t)p.n_layer;
     }
     __threadfence();
-    if (atomicAdd(p.bar + 1, 1u) == (unsigned)G - 1u) {
-      p.bar[0] = 0u;
+    if (atomicAdd(p.bar + 1, 1u) == (unsigned)G - 1u) {  // every CTA is done: reset for the next launch
+      for (int i = 0; i < p.ncnt; ++i) p.cnt[i] = 0u;
       p.bar[1] = 0u;
       __threadfence();
     }
@@ -786,6 +852,7 @@ struct mtp_decode_plan {
   int comm_max_rows = 0;
   unsigned long long *trace_buf = nullptr;
   int n_trace = 0;
+  size_t cnt_bytes = 0;
 };
 
 struct mtp_decode_cache {
@@ -904,7 +971,9 @@ int mtp_decode_plan_create(const mtp_decode_layer *layers, int n_layer, const vo
   const size_t o_xd = off; off = al(off + MB * NX * 4);
   const size_t o_lflags = off; off = al(off + MB * 4 + 4);
   const size_t o_bar = off; off = al(off + 64);
-  const size_t n_trace = 2 * (size_t)(2 + 5 * n_layer);
+  const int ncnt = p.KCx + p.KCo + 3 + max_batch;
+  const size_t o_cnt = off; off = al(off + sizeof(unsigned) * ncnt);
+  const size_t n_trace = (size_t)(2 + 5 * n_layer);
   const size_t o_trace = off; off = al(off + n_trace * 8);
   char *base = nullptr;
   if (cudaMalloc(&base, off) != cudaSuccess) {
@@ -928,6 +997,9 @@ int mtp_decode_plan_create(const mtp_decode_layer *layers, int n_layer, const vo
   P->bar = reinterpret_cast<unsigned *>(base + o_bar);
   p.bar = P->bar;
   p.err = reinterpret_cast<int *>(base + o_bar + 16);
+  p.cnt = reinterpret_cast<unsigned *>(base + o_cnt);
+  p.ncnt = ncnt;
+  P->cnt_bytes = sizeof(unsigned) * ncnt;
   P->trace_buf = reinterpret_cast<unsigned long long *>(base + o_trace);
   P->n_trace = (int)n_trace;
   p.trace = nullptr;
@@ -999,7 +1071,8 @@ int mtp_decode_status(mtp_decode_plan *P, int *status) {
 
 int mtp_decode_reset(mtp_decode_plan *P) {
   MTP_REQUIRE(P, "bad arguments");
-  if (cudaMemset(P->bar, 0, 64) != cudaSuccess) return fail(MTP_ERR_CUDA, "reset of the decode barrier failed");
+  if (cudaMemset(P->bar, 0, 64) != cudaSuccess || cudaMemset(P->p.cnt, 0, P->cnt_bytes) != cudaSuccess)
+    return fail(MTP_ERR_CUDA, "reset of the decode counters failed");
   return MTP_OK;
 }
 
