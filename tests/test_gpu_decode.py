@@ -144,3 +144,21 @@ def test_decode_falls_back_beyond_max_batch():
     out = m.step(nxt, cache)
     assert L.launch_count() - before > 2
     assert torch.isfinite(out.float()).all()
+
+
+def test_decode_trace_phases_add_up():
+    """mtp_decode_set_trace / read_trace: CTA 0's phase stamps of one step."""
+    cfg, _, m = _model("mid")
+    ids = torch.zeros(2, 4, dtype=torch.long, device=dev())
+    _, cache = m.prefill(ids)
+    nxt = torch.zeros(2, 1, dtype=torch.long, device=dev())
+    m.step(nxt, cache)
+    plan = m._mtp_decode
+    plan.set_trace(True)
+    m.step(nxt, cache)
+    torch.cuda.synchronize()
+    ph = plan.phase_times_us()
+    plan.set_trace(False)
+    parts = sum(v for k, v in ph.items() if k != "total")
+    assert ph["total"] > 0 and all(v >= 0 for v in ph.values())
+    assert abs(parts - ph["total"]) < 1e-3 * ph["total"] + 1e-3  # consecutive stamps of one CTA
