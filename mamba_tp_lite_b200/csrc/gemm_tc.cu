@@ -22,7 +22,8 @@ constexpr int BM = 128, BK = 64, BN_MAX = 256, STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;
 constexpr int B_BYTES = BN_MAX * BK * 2;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int NUM_EPI_WARPS = 8;
+constexpr int NUM_EPI_WARPS = 12;  // 3 per TMEM lane quarter
+constexpr int EPI_PARTS = NUM_EPI_WARPS / 4;  // warps sharing a lane quarter split its 16-column chunks
 constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
@@ -227,7 +228,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else {
     // ------------------------------------------------------------ epilogue (warps 2..9)
     const int q = warp & 3;              // TMEM lane quarter this warp may access
-    const int half = (warp - 2) >> 2;    // which alternate 16-column chunks it takes
+    const int part = (warp - 2) >> 2;    // chunks part, part + EPI_PARTS, ... of the lane quarter
     int local = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
       const int a = local & 1;
@@ -238,23 +239,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tile_coords(p, t, mt, nt);
       const int row = mt * BM + q * 32 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN_MAX);
-      // this warp's 16-column chunks are j, j + 32, j + 64, ...: two per TMEM wait
-      for (int j = half * 16; j < p.bn; j += 64) {
+      // this warp's 16-column chunks are j, j + 16 EPI_PARTS, ...: two per TMEM wait
+      constexpr int CS = 16 * EPI_PARTS;
+      for (int j = part * 16; j < p.bn; j += 2 * CS) {
         const int n0 = nt * p.bn + j;
-        const bool two = j + 32 < p.bn;  // warp-uniform
+        const bool two = j + CS < p.bn;  // warp-uniform
         float b[16], b2[16];
         if (p.epi != MTP_EPI_STORE) {  // issued before the TMEM read
           if (n0 < p.N) load_bias16(p, n0, b);
-          if (two && n0 + 32 < p.N) load_bias16(p, n0 + 32, b2);
+          if (two && n0 + CS < p.N) load_bias16(p, n0 + CS, b2);
         }
         float v[16], v2[16];
         if (two) {
-          tmem_ld16x2(tbase + (uint32_t)j, tbase + (uint32_t)(j + 32), v, v2);
+          tmem_ld16x2(tbase + (uint32_t)j, tbase + (uint32_t)(j + CS), v, v2);
         } else {
           tmem_ld16(tbase + (uint32_t)j, v);
         }
         if (n0 < p.N) epilogue_store(p, row, n0, v, b);
-        if (two && n0 + 32 < p.N) epilogue_store(p, row, n0 + 32, v2, b2);
+        if (two && n0 + CS < p.N) epilogue_store(p, row, n0 + CS, v2, b2);
       }
       tc_fence_before();
       __syncwarp();
