@@ -3,11 +3,17 @@
  * channel-sharded tensor-parallel Mamba-1 forward pass.
  *
  * Every entry point takes plain device pointers, sizes and a cudaStream_t
- * (passed as void*), returns an int status (0 = ok, see MTP_ERR_*), allocates
- * no device memory outside the create / bind calls (mtp_comm_create,
- * mtp_decode_plan_create, mtp_decode_bind_cache), and launches only on the given stream, so all of them can be recorded in a CUDA
- * graph.  No torch types appear here; the Python package binds this header
- * with ctypes.
+ * (passed as void*), returns an int status (0 = ok, see MTP_ERR_*) and launches
+ * only on the given stream.  Device memory is allocated by the create / bind
+ * calls (mtp_comm_create, mtp_decode_plan_create, mtp_decode_bind_cache) and,
+ * on first use, for three internal buffers kept until exit: a status word of
+ * the tensor-core GEMM, one of the fused dt_proj scan, and the row scratch of
+ * the reductions that do not hold a row in registers (rows wider than 3072
+ * values or not a multiple of 4, or a grid capped by mtp_comm_set_max_ctas),
+ * which grows to the largest size used.  A call that is to be recorded in a
+ * CUDA graph therefore needs one call of the same kind before the capture (the
+ * package's GraphedStepper runs warm-up steps first).  No torch types appear
+ * here; the Python package binds this header with ctypes.
  *
  * Layout conventions: matrices are row-major; a "token row" is one position
  * of one sequence, tokens ordered (batch, position).  Element type codes are
