@@ -11,7 +11,10 @@ every other site int8-per-token).
   e2e     the same through the public API with the ids in pinned host memory:
           host->device copy of the ids, prefill, greedy next token read back
   decode  CUDA-graph decode ms/token (256 replayed steps) at batch 1 and 32
-          after a 64-token prompt
+          after prompts of 64, 256 and 1024 tokens, with its HBM roofline
+  accuracy  KL(fp32 || bench) and top-1 agreement of the bench's logits (bf16,
+          its precision map) against the fp32 TP model on the same bf16-rounded
+          weights (fp32 map), on 2 of the prompts
 
     python bench.py [--gpus N --steps K --warmup W]
     torchrun --nproc-per-node N bench.py --gpus N ...
@@ -54,18 +57,31 @@ def load_peaks():
     return FALLBACK_PEAKS, "fallback"
 
 
-def read_traffic(name: str):
-    """DRAM bytes per launch of a kernel from the committed ncu summary
-    (a line ``dram_bytes_per_launch[<name>]: <int>``), else None."""
+def read_traffic(name: str, channels: int):
+    """DRAM bytes per launch of a kernel from the committed ncu summary (lines
+    ``dram_bytes_per_launch[<name>]: <int>`` and ``capture_channels[<name>]: <int>``,
+    the d_inner shard of the capture), scaled to a shard of ``channels``: the scan's
+    traffic is proportional to its channels.  Other kernels only at the captured
+    width, else None."""
     p = os.path.join(REPO, "profiles", "traffic.txt")
     if not os.path.exists(p):
         return None
-    key = f"dram_bytes_per_launch[{name}]:"
+    vals = {}
     with open(p) as f:
         for line in f:
-            if line.startswith(key):
-                return float(line.split(":", 1)[1].strip())
-    return None
+            if ":" in line:
+                k, v = line.split(":", 1)
+                try:
+                    vals[k.strip()] = float(v.strip())
+                except ValueError:
+                    pass
+    b = vals.get(f"dram_bytes_per_launch[{name}]")
+    cap = vals.get(f"capture_channels[{name}]")
+    if b is None or cap is None:
+        return None
+    if cap == channels:
+        return b
+    return b * channels / cap if name == "scan" else None
 
 
 class ClockSampler:
@@ -121,7 +137,82 @@ class ClockSampler:
                 "samples": len(rows)}
 
 
-# ------------------------------------------------------------------ CPU arm (oracle port)
+# ------------------------------------------------------------------ CPU arm
+REF_DIR = os.path.join(REPO, "baseline", "_ref")
+
+
+def _all_host_threads():
+    """Lifts torchrun's OMP_NUM_THREADS=1 for the CPU arm: every host core for torch
+    and for numpy's BLAS.  Returns (threads, limiter or None)."""
+    import torch
+
+    n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    try:
+        from threadpoolctl import threadpool_limits
+
+        return n, threadpool_limits(limits=n)
+    except Exception:
+        return n, None
+
+
+class ReferenceCPU:
+    """The unmodified reference (``mamba_lite`` installed into baseline/_ref) on the host
+    cores: its ``TPMambaLM`` at world size 1 over a one-process gloo group, fp32, the
+    bench's precision map, default parameter init (the values do not change the work).
+    One sample = prefill of 1 x ``tokens`` ids through all n_layer layers + lm_head."""
+
+    def __init__(self, shape: str, spec, tokens: int):
+        import torch
+        import torch.distributed as dist
+
+        sys.path.insert(0, REF_DIR)
+        from mamba_lite.model import MambaConfig as RefConfig
+        from mamba_lite.tp_model import TPMambaLM as RefTP
+
+        from mamba_tp_lite_b200.config import shape_config
+
+        cfg = shape_config(shape)
+        self.threads, self._lim = _all_host_threads()
+        fd, self._rdv = tempfile.mkstemp(prefix="ref_gloo_")
+        os.close(fd)
+        os.unlink(self._rdv)
+        if dist.is_initialized():
+            raise RuntimeError("the reference CPU arm runs in a process without a process group")
+        dist.init_process_group("gloo", init_method=f"file://{self._rdv}", rank=0, world_size=1)
+        self.group = dist.group.WORLD
+        rc = RefConfig(d_model=cfg.d_model, n_layer=cfg.n_layer, vocab_size=cfg.vocab_size, d_state=cfg.d_state,
+                       d_conv=cfg.d_conv, expand=cfg.expand, dt_rank=cfg.dt_rank)
+        torch.manual_seed(0)
+        with torch.no_grad():
+            self.model = RefTP(rc, 0, 1, self.group, spec).eval()
+        self.n_layer = cfg.n_layer
+        self.tokens = tokens
+        self.ids = torch.randint(0, cfg.vocab_size, (1, tokens), generator=torch.Generator().manual_seed(0))
+        self.desc = (f"unmodified reference mamba_lite.tp_model.TPMambaLM (world size 1, gloo, fp32, "
+                     f"{'mixed int8/fp16' if isinstance(spec, dict) else spec} map): prefill of 1 x {tokens} "
+                     f"tokens through all {cfg.n_layer} {shape}-shaped layers + lm_head")
+
+    def sample(self):
+        import torch
+
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            self.model.prefill(self.ids)
+        dt = time.perf_counter() - t0
+        return self.tokens / dt, dt
+
+
+def reference_available() -> bool:
+    return os.path.isdir(os.path.join(REF_DIR, "mamba_lite"))
+
+
+def ref_spec(a, n_layer: int):
+    from mamba_tp_lite_b200.tp_utils import build_spec
+
+    return build_spec(mixed_spec(n_layer), n_layer) if a.spec == "mixed" else a.spec
+
+
 def cpu_sample(shape: str, tokens: int, layers: int, seed: int = 0):
     """Times the numpy restatement of the reference forward (oracle/) on a
     bounded sample: ``layers`` mixer layers of the shape plus the lm_head, for
@@ -133,6 +224,7 @@ def cpu_sample(shape: str, tokens: int, layers: int, seed: int = 0):
     from oracle import mamba_oracle as O
 
     cfg = shape_config(shape)
+    threads, _lim = _all_host_threads()
     rng = np.random.default_rng(seed)
     e, d, n, r = cfg.d_inner, cfg.d_model, cfg.d_state, cfg.dt_rank
     f32 = np.float32
@@ -160,12 +252,6 @@ def cpu_sample(shape: str, tokens: int, layers: int, seed: int = 0):
     O._linear(O.rmsnorm(x, np.ones(d, f32), 1e-5), emb)
     t2 = time.perf_counter()
     per_seq = (t1 - t0) * cfg.n_layer / layers + (t2 - t1)
-    try:
-        from threadpoolctl import threadpool_info
-
-        threads = max([i.get("num_threads", 1) for i in threadpool_info()] + [1])
-    except Exception:
-        threads = os.cpu_count() or 1
     desc = (f"numpy oracle port, fp32: prefill of 1 x {tokens} tokens through {layers} of {cfg.n_layer} "
             f"{shape}-shaped layers + lm_head, scaled to {cfg.n_layer} layers")
     return tokens / per_seq, t2 - t0, desc, threads
@@ -175,29 +261,90 @@ def run_reference(a):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    tokens, layers = a.ref_tokens, a.ref_layers
+    from mamba_tp_lite_b200.config import shape_config
+
+    if reference_available() and not a.ref_port:
+        ref = ReferenceCPU(a.shape, ref_spec(a, shape_config(a.shape).n_layer), a.ref_sample_tokens)
+        kind, desc, threads = "reference", ref.desc, ref.threads
+        run = ref.sample
+    else:
+        tokens, layers = a.ref_tokens, a.ref_layers
+        kind = "port"
+        desc, threads = None, None
+
+        def run():
+            nonlocal desc, threads
+            v, sec, desc, threads = cpu_sample(a.shape, tokens, layers)
+            return v, sec
     for _ in range(a.warmup):
-        cpu_sample(a.shape, tokens, layers)
+        run()
     vals, secs = [], []
     for _ in range(a.steps):
-        v, s, desc, threads = cpu_sample(a.shape, tokens, layers)
+        v, sec = run()
         vals.append(v)
-        secs.append(s)
+        secs.append(sec)
     value = statistics.median(vals)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": a.gpus,
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1000 * statistics.median(secs),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded random weights, uniform random token ids)",
-        "config": {"workload": f"mamba-{a.shape}-shaped prefill, reference algorithm on the host cores",
-                   "shape": a.shape, "sample_tokens": tokens, "sample_layers": layers},
-        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": desc},
+        "config": {"workload": f"mamba-{a.shape}-shaped TP prefill {a.batch}x{a.seqlen}, reference on the host "
+                               f"cores (bounded sample)", "shape": a.shape, "global_batch": a.batch,
+                   "seq_len": a.seqlen, "tp": a.gpus},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": kind, "sample": desc},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
 # ------------------------------------------------------------------ GPU arm
+def accuracy_vs_fp32(model, ids):
+    """Accuracy of the bench's logits: quant_eval.quant_metrics
+    (quant_eval.py:48-60) of the model's prefill logits against the same TP model
+    converted to fp32 (same bf16-rounded weights, every site fp32: the reference's fp32
+    path, which the fp32 kernels restate to 1e-4).  Two more rows split the error:
+    the fp32 model under the bench's precision map (the map alone, as the reference
+    computes it) and the bf16 model with every site fp32 (bf16 arithmetic alone)."""
+    import torch
+
+    from mamba_tp_lite_b200.quant_eval import quant_metrics
+    from mamba_tp_lite_b200.tp_model import TPMambaLM
+
+    def metrics(ref, q):
+        q, ref = q.float(), ref.float()
+        m = quant_metrics(ref, q)
+        return {"kl": float(m["kl"].mean()), "top1": float(m["top1"].mean()),
+                "top5_unordered": float(m["top5_unordered"].mean()),
+                "max_abs_err_over_max_logit": float((q - ref).abs().max() / ref.abs().max())}
+
+    spec = model.allreduce_dtype
+    with torch.device("meta"):
+        ref_model = TPMambaLM(model.cfg, model.rank, model.world_size, model.group, "fp32")
+    ref_model = ref_model.to_empty(device=ids.device).float()
+    ref_model.load_state_dict({k: v.float() for k, v in model.state_dict().items()})
+    ref_model.eval()
+    with torch.no_grad():
+        r, _ = ref_model.prefill(ids)
+        q, _ = model.prefill(ids)
+        out = {"reference": "fp32 TP model, same weights, fp32 sites", "prompts": list(ids.shape)}
+        out.update(metrics(r, q))
+        del q
+        ref_model.set_allreduce_dtype(spec)
+        qm, _ = ref_model.prefill(ids)
+        out["fp32_model_bench_map"] = metrics(r, qm)
+        del qm
+        model.set_allreduce_dtype("fp32")
+        try:
+            qb, _ = model.prefill(ids)
+        finally:
+            model.set_allreduce_dtype(spec)
+        out["bf16_model_fp32_sites"] = metrics(r, qb)
+    del ref_model, r, qb
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(a):
     import torch
     import torch.distributed as dist
@@ -271,30 +418,41 @@ def run_ours(a):
         kern[name] = {"launches": len(recs), "avg_ms": sum(durs) / len(durs), "total_ms": sum(durs), "work": work}
     peaks, peak_src = load_peaks()
     pk = peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
+    hbm = peaks["hbm_gbs"]
+    gemms = {"in_proj", "x_proj", "dt_proj", "out_proj", "lm_head"}
     top = max(kern, key=lambda k: kern[k]["total_ms"])  # the kernel with the largest share of the step
     k = kern[top]
-    if top == "scan":
-        ach = k["work"] / (k["avg_ms"] / 1000.0) / 1e9
-        roofline = {"kernel": "scan_prefill", "bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"],
-                    "unit": "GB/s", "frac": ach / peaks["hbm_gbs"], "peak_source": f"{peak_src} HBM copy",
-                    "limiter": "MUFU exp rate (20 SFU ops per token-channel; ncu: XU pipe 63% of peak, "
-                               "DRAM traffic = algorithmic bytes), see profiles/scan_prefill_1p4b.md"}
-    else:
+    es_rank = cfg.d_inner // ws
+    if top in gemms:
         ach = k["work"] / (k["avg_ms"] / 1000.0) / 1e12
         roofline = {"kernel": f"gemm_tc ({top})", "bound": "tensor", "achieved": ach, "peak": pk, "unit": "TFLOP/s",
                     "frac": ach / pk, "peak_source": f"{peak_src} sustained bf16"}
-    roofline.update({"traffic": read_traffic(top), "launches": k["launches"], "avg_launch_ms": k["avg_ms"],
+    else:
+        ach = k["work"] / (k["avg_ms"] / 1000.0) / 1e9
+        roofline = {"kernel": top, "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+                    "peak_source": f"{peak_src} HBM copy"}
+        if top == "scan":
+            roofline["limiter"] = ("SFU/issue rate of the recurrence (16 state exponentials per token-channel), "
+                                   "not DRAM: see profiles/scan_prefill_1p4b.md")
+    roofline.update({"traffic": read_traffic(top, es_rank), "launches": k["launches"], "avg_launch_ms": k["avg_ms"],
                      "share_of_step": k["total_ms"] / ms})
     per_kernel = {}
     for name, v in kern.items():
-        if name == "scan":
-            gbs = v["work"] / (v["avg_ms"] / 1000.0) / 1e9
-            per_kernel[name] = {"bound": "hbm", "achieved_GBps": gbs, "frac_of_hbm": gbs / peaks["hbm_gbs"],
-                                "avg_ms": v["avg_ms"], "share_of_step": v["total_ms"] / ms}
-        else:
+        row = {"launches": v["launches"], "avg_ms": v["avg_ms"], "share_of_step": v["total_ms"] / ms}
+        if name in gemms:
             tf = v["work"] / (v["avg_ms"] / 1000.0) / 1e12
-            per_kernel[name] = {"bound": "tensor", "achieved_TFLOPs": tf, "frac": tf / pk, "avg_ms": v["avg_ms"],
-                                "share_of_step": v["total_ms"] / ms}
+            row.update({"bound": "tensor", "achieved_TFLOPs": tf, "frac": tf / pk})
+        elif name in ("reduce_x", "reduce_out"):
+            # work = bytes this rank sends to its peers (0 at TP=1: the wire format's round trip only)
+            gbs = v["work"] / (v["avg_ms"] / 1000.0) / 1e9
+            row.update({"bound": "nvlink" if ws > 1 else "hbm", "sent_GBps": gbs,
+                        "frac_of_nvlink_900": gbs / 900.0 if ws > 1 else None})
+        else:
+            gbs = v["work"] / (v["avg_ms"] / 1000.0) / 1e9
+            row.update({"bound": "hbm", "achieved_GBps": gbs, "frac_of_hbm": gbs / hbm})
+        per_kernel[name] = row
+    other_ms = ms / a.steps - sum(v["total_ms"] for v in kern.values()) / a.steps
+    per_kernel["untimed_rest"] = {"ms_per_step": other_ms, "share_of_step": other_ms * a.steps / ms}
 
     # ------------------------------------------------ end to end through the API, host ids
     host_ids = ids.cpu().pin_memory()
@@ -318,34 +476,62 @@ def run_ours(a):
     # ------------------------------------------------ graphed decode
     decode = {}
     if not a.no_decode:
-        for db in a.decode_batches:
-            prompt = ids[:db, :64].contiguous()
-            _, cache = model.prefill(prompt)
-            st = GraphedStepper(model, cache, db, "cuda")
-            st.capture()
-            nid = torch.zeros(db, 1, dtype=torch.long, device="cuda")
-            for _ in range(5):
-                st.replay(nid)
-            torch.cuda.synchronize()
-            barrier()
-            d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            d0.record()
-            for _ in range(a.decode_steps):
-                st.replay(nid)
-            d1.record()
-            torch.cuda.synchronize()
-            barrier()
-            dms = max_over_ranks(d0.elapsed_time(d1)) / a.decode_steps
-            decode[f"b{db}_ms_per_token"] = dms
-            st.release()
-            del cache
-        decode["steps"] = a.decode_steps
-        decode["prompt"] = 64
+        # HBM bytes of one decode step on this rank: every weight once (the tied embedding
+        # as the lm_head) + per sequence the SSM state (fp32) and conv history read and written
+        w_bytes = sum(p.numel() * p.element_size() for p in model.parameters())
+        st_bytes = cfg.n_layer * 2 * (es_rank * cfg.d_state * 4 + es_rank * (cfg.d_conv - 1) * 2)
+        by_prompt = {}
+        for plen in a.decode_prompts:
+            row = {}
+            for db in a.decode_batches:
+                prompt = ids[:db, :plen].contiguous()
+                _, cache = model.prefill(prompt)
+                st = GraphedStepper(model, cache, db, "cuda")
+                st.capture()
+                nid = torch.zeros(db, 1, dtype=torch.long, device="cuda")
+                for _ in range(5):
+                    st.replay(nid)
+                torch.cuda.synchronize()
+                barrier()
+                d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                d0.record()
+                for _ in range(a.decode_steps):
+                    st.replay(nid)
+                d1.record()
+                torch.cuda.synchronize()
+                barrier()
+                dms = max_over_ranks(d0.elapsed_time(d1)) / a.decode_steps
+                gbs = (w_bytes + db * st_bytes) / (dms / 1000.0) / 1e9
+                row[f"b{db}_ms_per_token"] = dms
+                row[f"b{db}_hbm_frac"] = gbs / hbm
+                st.release()
+                del cache
+            by_prompt[str(plen)] = row
+        first = by_prompt[str(a.decode_prompts[0])]
+        decode = {k: v for k, v in first.items() if k.endswith("ms_per_token")}
+        decode.update({"steps": a.decode_steps, "prompt": a.decode_prompts[0], "by_prompt": by_prompt})
+        b0 = a.decode_batches[0]
+        dms0 = first[f"b{b0}_ms_per_token"]
+        ach = (w_bytes + b0 * st_bytes) / (dms0 / 1000.0) / 1e9
+        decode["roofline"] = {"bound": "hbm", "batch": b0, "bytes_per_step": w_bytes + b0 * st_bytes,
+                              "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+                              "floor_ms": (w_bytes + b0 * st_bytes) / hbm / 1e6}
+
+    # ------------------------------------------------ accuracy against the fp32 TP model
+    accuracy = None
+    if not a.no_accuracy:
+        accuracy = accuracy_vs_fp32(model, ids[:a.acc_batch].contiguous())
 
     cpu = None
     if rank == 0 and ws == 1 and not a.no_cpu_baseline:
-        v, _, desc, threads = cpu_sample(a.shape, a.ref_tokens, a.ref_layers)
-        cpu = {"value": v, "unit": "tok/s", "cores": threads, "kind": "port", "sample": desc}
+        if reference_available() and not a.ref_port:
+            ref = ReferenceCPU(a.shape, ref_spec(a, cfg.n_layer), a.ref_sample_tokens)
+            ref.sample()  # warm-up
+            v = statistics.median([ref.sample()[0] for _ in range(2)])
+            cpu = {"value": v, "unit": "tok/s", "cores": ref.threads, "kind": "reference", "sample": ref.desc}
+        else:
+            v, _, desc, threads = cpu_sample(a.shape, a.ref_tokens, a.ref_layers)
+            cpu = {"value": v, "unit": "tok/s", "cores": threads, "kind": "port", "sample": desc}
 
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": a.steps, "warmup": a.warmup,
@@ -356,7 +542,8 @@ def run_ours(a):
                    "precision_map": a.spec if a.spec != "mixed" else
                    "int8-per-token, out_proj of layers 0 and last 4 in fp16",
                    "l2": "inputs larger than L2 (2.8 GB of weights, >126 MB of activations per layer)"},
-        "decode": decode, "roofline": roofline, "kernels": per_kernel, "cpu_baseline": cpu, "e2e": e2e,
+        "decode": decode, "accuracy": accuracy, "roofline": roofline, "kernels": per_kernel, "cpu_baseline": cpu,
+        "e2e": e2e,
         "clocks": clocks.summary(), "gpu_launches": launches,
     }
     if rank == 0:
@@ -379,6 +566,12 @@ def main():
     ap.add_argument("--spec", default="mixed", help="'mixed' (configuration 4 map) or one reduction name")
     ap.add_argument("--decode-steps", type=int, default=256)
     ap.add_argument("--decode-batches", type=int, nargs="*", default=[1, 32])
+    ap.add_argument("--decode-prompts", type=int, nargs="*", default=[64, 256, 1024])
+    ap.add_argument("--no-accuracy", action="store_true")
+    ap.add_argument("--acc-batch", type=int, default=2, help="prompts of the accuracy check")
+    ap.add_argument("--ref-port", action="store_true", help="CPU arm: the numpy port even if baseline/_ref exists")
+    ap.add_argument("--ref-sample-tokens", type=int, default=128,
+                    help="tokens of one reference CPU sample (1 sequence, all layers)")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-tokens", type=int, default=1024)

@@ -105,6 +105,23 @@ int mtp_scan_prefill(const void *xz, int ld_xz, const void *dt, int ld_dt, int d
                      const void *conv_init, const float *ssm_init, void *y, int ld_y, void *conv_final,
                      float *ssm_final, int B, int L, int Es, int N, int K, int dtype, void *stream);
 
+/* The selective scan of mtp_scan_prefill fed with the conv output instead of raw x:
+ * xc [B*L, ld_xc] = SiLU(conv1d(x)) as written by mtp_conv1d_silu (the x_proj input,
+ * computed once per layer); z is read from columns [Es, 2Es) of xz and the raw x
+ * columns [0, Es) of xz only for the final conv history.  Other arguments as
+ * mtp_scan_prefill (conv weights are not needed).  State pairs are updated with
+ * packed fp32 arithmetic and part of the state exponentials is evaluated on the FP32
+ * pipe (the polynomial of mtp_exp2_fma).  Replaces tp_model.py:101-103 and :113-129
+ * (model.py:210-241), the Python loop over t at tp_model.py:124-126. */
+int mtp_scan_prefill_xc(const void *xc, int ld_xc, const void *xz, int ld_xz, const void *dt, int ld_dt,
+                        int dt_dtype, const float *bc, int ld_bc, const void *A_log, const void *Dp,
+                        const void *conv_init, const float *ssm_init, void *y, int ld_y, void *conv_final,
+                        float *ssm_final, int B, int L, int Es, int N, int K, int dtype, void *stream);
+/* out[i] = 2^x[i] for x[i] <= 0 by the FP32-pipe polynomial that mtp_scan_prefill_xc
+ * uses for part of exp(dt * A) (x < -125 gives 2^-125).  Test entry: the reference
+ * computes these factors with torch.exp (tp_model.py:114). */
+int mtp_exp2_fma(const float *x, float *out, int n, void *stream);
+
 /* The fused prefill above with dt_proj folded in (bf16 models): dt = softplus(
  * dt_low . W_dt^T + b_dt) is computed inside the kernel on the tensor cores
  * (tcgen05.mma, TMEM accumulators) instead of being read from memory.
@@ -180,6 +197,12 @@ int mtp_comm_reset_status(mtp_comm *c);
  * across micro-batches); 0 restores the default (one CTA per SM, register rows).
  * Results are bit-identical either way. */
 int mtp_comm_set_max_ctas(mtp_comm *c, int max_ctas);
+
+/* Bytes this rank sends to its peers over NVLink for one reduction of [rows, cols] in
+ * `mode` whose results are rounded to rdt (MTP_F32 / MTP_BF16), with the protocol the
+ * reduce calls choose (0 without a context or at world size 1).  For bandwidth reports;
+ * the reference counts payload bytes per call at tp_utils.py:24-26, :38-40, :114-116. */
+int mtp_comm_sent_bytes(mtp_comm *c, int mode, int rows, int cols, int rdt, double *bytes);
 
 /* AllReduce #1 epilogue (tp_model.py:106-108, :159-161): sum the fp32
  * partial [rows, R+2N] over ranks in `mode`, round the sums to dt_dtype (the

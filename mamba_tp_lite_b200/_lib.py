@@ -33,6 +33,9 @@ _SIGS = {
                          _i, _i, _i, _i, _i, _i, _vp],
     "mtp_scan_prefill_fused": [_vp, _i, _vp, _i, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp,
                                _vp, _i, _i, _i, _i, _i, _i, _vp],
+    "mtp_scan_prefill_xc": [_vp, _i, _vp, _i, _vp, _i, _i, _vp, _i, _vp, _vp, _vp, _vp, _vp, _i, _vp, _vp,
+                            _i, _i, _i, _i, _i, _i, _vp],
+    "mtp_exp2_fma": [_vp, _vp, _i, _vp],
     "mtp_scan_status": [C.POINTER(_i)],
     "mtp_step": [_vp, _i, _vp, _i, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,
                  _i, _i, _i, _i, _i, _i, _vp],
@@ -48,6 +51,7 @@ _SIGS = {
     "mtp_comm_status": [_vp, C.POINTER(_i)],
     "mtp_comm_reset_status": [_vp],
     "mtp_comm_set_max_ctas": [_vp, _i],
+    "mtp_comm_sent_bytes": [_vp, _i, _i, _i, _i, C.POINTER(_d)],
     "mtp_reduce_xproj": [_vp, _i, _vp, _i, _i, _i, _vp, _i, _vp, _vp],
     "mtp_reduce_outproj": [_vp, _i, _vp, _i, _i, _vp, _vp, _vp, _f, _vp, _i, _vp],
     "mtp_allreduce": [_vp, _i, _i, _vp, _vp, _i, _i, _vp],
@@ -114,6 +118,13 @@ def call(name: str, *args) -> None:
 
 def launch_count() -> int:
     return int(load().mtp_launch_count())
+
+
+def comm_sent_bytes(comm, mode: int, rows: int, cols: int, rdt: int) -> float:
+    """Bytes one rank sends to its peers for a reduction call (0 at world size 1)."""
+    out = C.c_double(0.0)
+    call("mtp_comm_sent_bytes", comm, mode, rows, cols, rdt, C.byref(out))
+    return out.value
 
 
 def stream_ptr(stream=None) -> int:

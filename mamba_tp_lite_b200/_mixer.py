@@ -7,8 +7,8 @@ One mixer forward is this chain of libmtp calls (T = batch x positions):
     conv1d    conv1d+SiLU     xz -> xc [T,Es] (input of x_proj)      (tp_model.py:95-100)
     x_proj    GEMM            xc -> partial [T,R+2N] fp32            (tp_model.py:106)
     AR #1     reduce_xproj    partial -> dt_low [T,R], B|C [T,2N]    (tp_model.py:107-108)
-    dt_proj   GEMM+softplus   dt_low -> dt [T,Es] fp32               (tp_model.py:110-111)
-    scan      fused conv+SiLU+scan+D+gate -> y [T,Es], final conv/ssm state (tp_model.py:93-129)
+    dt_proj   GEMM+softplus   dt_low -> dt [T,Es] model dtype        (tp_model.py:110-111)
+    scan      scan over xc + D skip + SiLU(z) gate -> y [T,Es], final conv/ssm state (tp_model.py:101-129)
     out_proj  GEMM            y -> partial [T,D] fp32                (tp_model.py:131)
     AR #2     reduce_outproj  partial -> resid += out; normed = RMSNorm_next(resid)
                                                                       (tp_model.py:132-134, :254-257)
@@ -118,7 +118,11 @@ class MixerKernels:
         if OVERLAP_STREAM is not None:
             _on_comm_stream(launch, (partial, dt_low, bc))
         else:
+            ev = _prof_begin()
             launch()
+            if ev is not None:
+                _prof_end(ev, "reduce_x", L.comm_sent_bytes(ctx, mode, rows, partial.shape[1],
+                                                            L.dtype_code(dt_low.dtype)))
 
     def _reduce_out(self, partial, resid, norm_w, eps, normed):
         """AllReduce #2 (tp_model.py:132-134) fused with the bias, the block
@@ -145,7 +149,10 @@ class MixerKernels:
         if OVERLAP_STREAM is not None:
             _on_comm_stream(launch, (partial, resid, normed))
         else:
+            ev = _prof_begin()
             launch()
+            if ev is not None:
+                _prof_end(ev, "reduce_out", L.comm_sent_bytes(ctx, mode, rows, d, L.dtype_code(odt)))
 
     def _fused_dt_ok(self) -> bool:
         """The fused dt_proj + scan kernel (opt-in, MTP_FUSED_DT=1) for bf16 models
@@ -187,8 +194,10 @@ class MixerKernels:
         conv_w = self.conv1d.weight
         conv_b = self.conv1d.bias
         xc = torch.empty(T, es, device=dev, dtype=dt_)
+        ev = _prof_begin()
         L.call("mtp_conv1d_silu", L.ptr(xz), 2 * es, L.ptr(conv_w), L.ptr(conv_b), L.ptr(conv_init), L.ptr(xc), es,
                B, Lq, es, k, L.dtype_code(dt_), L.stream_ptr())
+        _prof_end(ev, "conv1d", 2 * T * es * xz.element_size())  # x read, xc written
         partial_x = torch.empty(T, r + 2 * n, device=dev, dtype=torch.float32)
         self._gemm(xc, self.x_proj.weight, partial_x, tag="x_proj")
         dt_low = torch.empty(T, r, device=dev, dtype=dt_)
@@ -216,9 +225,10 @@ class MixerKernels:
         dt = torch.empty(T, es, device=dev, dtype=dt_)
         self._gemm(dt_low, self.dt_proj.weight, dt, L.EPI_BIAS_SOFTPLUS, self.dt_proj.bias, tag="dt_proj")
         ev = _prof_begin()
-        L.call("mtp_scan_prefill", L.ptr(xz), 2 * es, L.ptr(dt), es, L.dtype_code(dt_), L.ptr(bc), 2 * n,
-               L.ptr(self.A_log), L.ptr(self.D), L.ptr(conv_w), L.ptr(conv_b), L.ptr(conv_init), L.ptr(ssm_init),
-               L.ptr(y), es, L.ptr(conv_final), L.ptr(ssm_final), B, Lq, es, n, k, L.dtype_code(dt_), L.stream_ptr())
+        # the scan reads the conv output xc that x_proj already consumed (no conv recompute)
+        L.call("mtp_scan_prefill_xc", L.ptr(xc), es, L.ptr(xz), 2 * es, L.ptr(dt), es, L.dtype_code(dt_), L.ptr(bc),
+               2 * n, L.ptr(self.A_log), L.ptr(self.D), L.ptr(conv_init), L.ptr(ssm_init), L.ptr(y), es,
+               L.ptr(conv_final), L.ptr(ssm_final), B, Lq, es, n, k, L.dtype_code(dt_), L.stream_ptr())
         # algorithmic bytes: x, z, dt, y in the model dtype, B|C fp32 (+ per-sequence state I/O)
         _prof_end(ev, "scan", T * (es * 4 * esz + 2 * n * 4) + B * es * (2 * n * 4 + 2 * (k - 1) * esz))
         partial_o = torch.empty(T, cfg.d_model, device=dev, dtype=torch.float32)

@@ -171,6 +171,7 @@ struct EpiOut {
   float eps;
   int out_dtype;        // OUTPROJ: dtype of bias / norm_w / normed
   int rdt;              // dtype the reduced values are rounded to (the collective's return dtype)
+  int wide;             // rows take the 16-column granule layout (RMSNorm sum order of reduce_wide_kernel)
 };
 
 // Round to the collective's return dtype: the reference's reductions return the
@@ -200,6 +201,36 @@ __device__ __forceinline__ float sq4(float4 h) {
 // With cols % 4 == 0 lane l owns columns 4l + 128i .. +3, as the register-row kernel.
 template <int EPI>
 __device__ __forceinline__ void epilogue_row(const EpiOut &e, const float *val, int r, int cols, int lane) {
+  if (EPI == EPI_OUTPROJ && e.wide) {
+    // lane l owns the 16-column granules 16 (32 i + l), summed four values at a time in column
+    // order: the order of reduce_wide_kernel, so both variants give the same bits
+    float ss = 0.f;
+    float *res = e.resid + (size_t)r * cols;
+    for (int c0 = 16 * lane; c0 < cols; c0 += 512) {
+      for (int q = 0; q < 16; q += 4) {
+        const int c = c0 + q;
+        float4 v = __ldcg(reinterpret_cast<const float4 *>(val + c));
+        if (e.bias) {
+          v.x += ld_any(e.bias, e.out_dtype, c); v.y += ld_any(e.bias, e.out_dtype, c + 1);
+          v.z += ld_any(e.bias, e.out_dtype, c + 2); v.w += ld_any(e.bias, e.out_dtype, c + 3);
+        }
+        const float4 h0 = *reinterpret_cast<const float4 *>(res + c);
+        const float4 h = make_float4(h0.x + v.x, h0.y + v.y, h0.z + v.z, h0.w + v.w);
+        *reinterpret_cast<float4 *>(res + c) = h;
+        ss = __fadd_rn(ss, sq4(h));
+      }
+    }
+    if (e.normed) {
+      const float rs = rsqrtf(warp_sum(ss) / (float)cols + e.eps);
+      for (int c0 = 16 * lane; c0 < cols; c0 += 512) {
+        for (int q = 0; q < 16; ++q) {
+          const int c = c0 + q;
+          st_any(e.normed, e.out_dtype, (size_t)r * cols + c, ld_any(e.norm_w, e.out_dtype, c) * (res[c] * rs));
+        }
+      }
+    }
+    return;
+  }
   if (EPI == EPI_OUTPROJ && (cols & 3) == 0) {
     float ss = 0.f;
     float *res = e.resid + (size_t)r * cols;
@@ -678,6 +709,387 @@ __global__ void __launch_bounds__(WPB * 32, (VPL >= 16 ? 2 : 3)) reduce_rows_ker
   finish();
 }
 
+// ----------------------------------------------------------------- wide-row reduction (16-column granules)
+// For rows of at least 512 values with cols % 16 == 0 (the out_proj site: d_model 768 ..
+// 2560): lane l of a warp owns the 16 consecutive columns 16 (32 i + l) .. +15 of chunk
+// i, so every global access is 16 bytes or more per lane: the fp32 partial and the
+// residual as four float4, the int8 wire as one 16-byte word, the fp16 wire and the bf16
+// gather / normed rows as two.  The int8 slot keeps the reference's payload order
+// (scales, then rows x cols int8) with the int8 block starting at the next 16-byte
+// boundary.  NC chunks per lane: cols <= 512 NC.
+template <int NC> struct RowW { float v[NC][16]; };
+
+__device__ __forceinline__ size_t q_offset(int rows) { return ((size_t)4 * rows + 15) & ~(size_t)15; }
+
+template <bool CG, int NC>
+__device__ __forceinline__ void load_roww(const float *row, int cols, int lane, RowW<NC> &R) {
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    const int c = 16 * (i * 32 + lane);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (c < cols) f = CG ? __ldcg(reinterpret_cast<const float4 *>(row + c) + j) : *(reinterpret_cast<const float4 *>(row + c) + j);
+      R.v[i][4 * j] = f.x; R.v[i][4 * j + 1] = f.y; R.v[i][4 * j + 2] = f.z; R.v[i][4 * j + 3] = f.w;
+    }
+  }
+}
+
+template <int NC>
+__device__ __forceinline__ float roww_amax(const RowW<NC> &R) {
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < NC; ++i)
+#pragma unroll
+    for (int k = 0; k < 16; ++k) m = fmaxf(m, fabsf(R.v[i][k]));
+  return warp_max(m);
+}
+
+template <int MODE, int NC>
+__device__ __forceinline__ void roundtrip_w(RowW<NC> &R) {
+  if (MODE == MTP_RED_FP16) {
+#pragma unroll
+    for (int i = 0; i < NC; ++i)
+#pragma unroll
+      for (int k = 0; k < 16; ++k) R.v[i][k] = h1(R.v[i][k]);
+  } else if (MODE == MTP_RED_INT8TOK) {
+    const float s = row_scale(roww_amax(R));
+#pragma unroll
+    for (int i = 0; i < NC; ++i)
+#pragma unroll
+      for (int k = 0; k < 16; ++k) R.v[i][k] = dq1(R.v[i][k], s);
+  }
+}
+
+template <int NC>
+__device__ __forceinline__ void round_w(RowW<NC> &R, int rdt) {
+  if (rdt != MTP_BF16) return;
+#pragma unroll
+  for (int i = 0; i < NC; ++i)
+#pragma unroll
+    for (int k = 0; k < 16; ++k) R.v[i][k] = rnd_rdt(R.v[i][k], rdt);
+}
+
+__device__ __forceinline__ uint4 pack_bf16x8(const float *v) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    w[i] = *reinterpret_cast<uint32_t *>(&h2);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+__device__ __forceinline__ void unpack_bf16x8(uint4 u, float *v) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[i]));
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ uint4 pack_half8(const float *v) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 h2 = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+    w[i] = *reinterpret_cast<uint32_t *>(&h2);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+__device__ __forceinline__ void unpack_half8(uint4 u, float *v) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[i]));
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+template <int MODE, int NC>
+__device__ __forceinline__ void write_wire_w(char *dst, const RowW<NC> &R, int r, int rows, int cols, int lane,
+                                             float scale) {
+  if (MODE == MTP_RED_INT8TOK && lane == 0) reinterpret_cast<float *>(dst)[r] = scale;
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    const int c = 16 * (i * 32 + lane);
+    if (c >= cols) break;
+    const float *v = R.v[i];
+    if (MODE == MTP_RED_FP32) {
+      float4 *o = reinterpret_cast<float4 *>(reinterpret_cast<float *>(dst) + (size_t)r * cols + c);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    } else if (MODE == MTP_RED_FP16) {
+      uint4 *o = reinterpret_cast<uint4 *>(reinterpret_cast<__half *>(dst) + (size_t)r * cols + c);
+      o[0] = pack_half8(v);
+      o[1] = pack_half8(v + 8);
+    } else {
+      uint32_t w[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        w[j] = pack4(quant1(v[4 * j], scale), quant1(v[4 * j + 1], scale), quant1(v[4 * j + 2], scale),
+                     quant1(v[4 * j + 3], scale));
+      *reinterpret_cast<uint4 *>(dst + q_offset(rows) + (size_t)r * cols + c) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
+// Rank-ordered reduction of row r over the slots into registers (16-byte loads per source
+// and granule; sums in rank order, product rounded before the add for int8).
+template <int MODE, int NC>
+__device__ __forceinline__ void reduce_w(char *const *slots, int nsrc, int r, int rows, int cols, int lane,
+                                         RowW<NC> &R) {
+#pragma unroll
+  for (int i = 0; i < NC; ++i)
+#pragma unroll
+    for (int k = 0; k < 16; ++k) R.v[i][k] = 0.f;
+  for (int k = 0; k < nsrc; ++k) {
+    const float sk = MODE == MTP_RED_INT8TOK ? __ldcg(reinterpret_cast<const float *>(slots[k]) + r) : 0.f;
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const int c = 16 * (i * 32 + lane);
+      if (c >= cols) break;
+      float *a = R.v[i];
+      if (MODE == MTP_RED_INT8TOK) {
+        const uint4 w = __ldcg(reinterpret_cast<const uint4 *>(slots[k] + q_offset(rows) + (size_t)r * cols + c));
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 16; ++j) a[j] = __fadd_rn(a[j], __fmul_rn(unpack_i8(ww[j >> 2], j & 3), sk));
+      } else if (MODE == MTP_RED_FP16) {
+        const uint4 *p = reinterpret_cast<const uint4 *>(reinterpret_cast<const __half *>(slots[k]) + (size_t)r * cols + c);
+        float f[16];
+        unpack_half8(__ldcg(p), f);
+        unpack_half8(__ldcg(p + 1), f + 8);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) a[j] = __fadd_rn(a[j], f[j]);
+      } else {
+        const float4 *p = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(slots[k]) + (size_t)r * cols + c);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float4 f = __ldcg(p + j);
+          a[4 * j] = __fadd_rn(a[4 * j], f.x); a[4 * j + 1] = __fadd_rn(a[4 * j + 1], f.y);
+          a[4 * j + 2] = __fadd_rn(a[4 * j + 2], f.z); a[4 * j + 3] = __fadd_rn(a[4 * j + 3], f.w);
+        }
+      }
+    }
+  }
+  if (MODE == MTP_RED_FP16) {
+#pragma unroll
+    for (int i = 0; i < NC; ++i)
+#pragma unroll
+      for (int k = 0; k < 16; ++k) R.v[i][k] = h1(R.v[i][k]);
+  }
+}
+
+// gather rows travel in the result dtype (bf16: 32 bytes per granule, fp32: 64)
+template <int NC>
+__device__ __forceinline__ void store_gather_w(char *g, const RowW<NC> &R, int r, int cols, int lane, int rdt) {
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    const int c = 16 * (i * 32 + lane);
+    if (c >= cols) break;
+    if (rdt == MTP_BF16) {
+      uint4 *o = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(g) + (size_t)r * cols + c);
+      o[0] = pack_bf16x8(R.v[i]);
+      o[1] = pack_bf16x8(R.v[i] + 8);
+    } else {
+      float4 *o = reinterpret_cast<float4 *>(reinterpret_cast<float *>(g) + (size_t)r * cols + c);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o[j] = make_float4(R.v[i][4 * j], R.v[i][4 * j + 1], R.v[i][4 * j + 2], R.v[i][4 * j + 3]);
+    }
+  }
+}
+template <int NC>
+__device__ __forceinline__ void load_gather_w(const char *g, RowW<NC> &R, int r, int cols, int lane, int rdt) {
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    const int c = 16 * (i * 32 + lane);
+    if (c >= cols) {
+#pragma unroll
+      for (int k = 0; k < 16; ++k) R.v[i][k] = 0.f;
+      continue;
+    }
+    if (rdt == MTP_BF16) {
+      const uint4 *p = reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(g) + (size_t)r * cols + c);
+      const uint4 a = __ldcg(p), b = __ldcg(p + 1);
+      unpack_bf16x8(a, R.v[i]);
+      unpack_bf16x8(b, R.v[i] + 8);
+    } else {
+      const float4 *p = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(g) + (size_t)r * cols + c);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float4 f = __ldcg(p + j);
+        R.v[i][4 * j] = f.x; R.v[i][4 * j + 1] = f.y; R.v[i][4 * j + 2] = f.z; R.v[i][4 * j + 3] = f.w;
+      }
+    }
+  }
+}
+
+// 16 consecutive values of a model-dtype (bf16) or fp32 vector starting at column c
+__device__ __forceinline__ void load_vec16(const void *p, int dtype, int c, float *v) {
+  if (dtype == MTP_F32) {
+    const float4 *q = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(p) + c);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 f = __ldg(q + j);
+      v[4 * j] = f.x; v[4 * j + 1] = f.y; v[4 * j + 2] = f.z; v[4 * j + 3] = f.w;
+    }
+  } else {
+    const uint4 *q = reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(p) + c);
+    unpack_bf16x8(__ldg(q), v);
+    unpack_bf16x8(__ldg(q + 1), v + 8);
+  }
+}
+
+// Epilogue of a reduced row in the 16-column layout.  The RMSNorm sum of squares runs over
+// the lane's granules in column order, four values at a time (sq4), then across the warp:
+// the same order as epilogue_row gives the wide layout, so every kernel variant computes the
+// same bits.  Bias, norm_w and normed need 16-byte aligned rows (checked on the host).
+template <int EPI, int NC>
+__device__ __forceinline__ void epilogue_w(const EpiOut &e, RowW<NC> &R, int r, int cols, int lane) {
+  if (EPI == EPI_PLAIN) {
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const int c = 16 * (i * 32 + lane);
+      if (c >= cols) break;
+      float4 *o = reinterpret_cast<float4 *>(e.out + (size_t)r * cols + c);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o[j] = make_float4(R.v[i][4 * j], R.v[i][4 * j + 1], R.v[i][4 * j + 2], R.v[i][4 * j + 3]);
+    }
+    return;
+  }
+  // EPI_OUTPROJ
+  float ss = 0.f;
+  float *res = e.resid + (size_t)r * cols;
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    const int c = 16 * (i * 32 + lane);
+    if (c >= cols) break;
+    if (e.bias) {
+      float b[16];
+      load_vec16(e.bias, e.out_dtype, c, b);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) R.v[i][k] += b[k];
+    }
+    float4 *rp = reinterpret_cast<float4 *>(res + c);
+    float4 h0[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) h0[j] = rp[j];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 h = make_float4(h0[j].x + R.v[i][4 * j], h0[j].y + R.v[i][4 * j + 1], h0[j].z + R.v[i][4 * j + 2],
+                                   h0[j].w + R.v[i][4 * j + 3]);
+      rp[j] = h;
+      ss = __fadd_rn(ss, sq4(h));
+      R.v[i][4 * j] = h.x; R.v[i][4 * j + 1] = h.y; R.v[i][4 * j + 2] = h.z; R.v[i][4 * j + 3] = h.w;
+    }
+  }
+  if (e.normed) {
+    const float rs = rsqrtf(warp_sum(ss) / (float)cols + e.eps);
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const int c = 16 * (i * 32 + lane);
+      if (c >= cols) break;
+      float w[16], o[16];
+      load_vec16(e.norm_w, e.out_dtype, c, w);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) o[k] = w[k] * (R.v[i][k] * rs);
+      if (e.out_dtype == MTP_F32) {
+        float4 *p = reinterpret_cast<float4 *>(reinterpret_cast<float *>(e.normed) + (size_t)r * cols + c);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) p[j] = make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+      } else {
+        uint4 *p = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(e.normed) + (size_t)r * cols + c);
+        p[0] = pack_bf16x8(o);
+        p[1] = pack_bf16x8(o + 8);
+      }
+    }
+  }
+}
+
+template <int MODE, int EPI, int NC>
+__global__ void __launch_bounds__(WPB * 32, 2) reduce_wide_kernel(CommDev d, bool has_comm, int site,
+                                                                  const float *__restrict__ partial, int rows,
+                                                                  int cols, bool two_shot, EpiOut e) {
+  MTP_PDL_WAIT();
+  MTP_PDL_TRIGGER();
+  __shared__ int abort_sm;
+  __shared__ uint32_t epoch_sm;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int j = blockIdx.x, G = gridDim.x;
+  RowW<NC> R;
+  if (!has_comm) {
+    for (int r = j * WPB + warp; r < rows; r += G * WPB) {
+      load_roww<false>(partial + (size_t)r * cols, cols, lane, R);
+      roundtrip_w<MODE>(R);
+      round_w(R, e.rdt);
+      epilogue_w<EPI>(e, R, r, cols, lane);
+    }
+    return;
+  }
+  uint32_t *ep = reinterpret_cast<uint32_t *>(d.peer[d.rank] + d.off_epoch) + site;
+  if (threadIdx.x == 0) {
+    abort_sm = 0;
+    epoch_sm = *reinterpret_cast<volatile uint32_t *>(ep) + 1u;
+  }
+  __syncthreads();
+  const uint32_t epoch = epoch_sm;
+  auto finish = [&]() {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      unsigned int *done = reinterpret_cast<unsigned int *>(d.peer[d.rank] + d.off_done) + site;
+      if (atomicAdd(done, 1u) == (unsigned)G - 1u) {
+        *done = 0u;
+        *reinterpret_cast<volatile uint32_t *>(ep) = epoch;
+        __threadfence();
+      }
+    }
+  };
+  const size_t half = (size_t)(epoch & 1u) * d.ws * d.slot_bytes[site];
+  const uint32_t all = (1u << d.ws) - 1u;
+  const int chunk = (rows + d.ws - 1) / d.ws;
+  const size_t my_slot = d.off_recv[site] + half + (size_t)d.rank * d.slot_bytes[site];
+  for (int r = j * WPB + warp; r < rows; r += G * WPB) {
+    load_roww<false>(partial + (size_t)r * cols, cols, lane, R);
+    const float sc = MODE == MTP_RED_INT8TOK ? row_scale(roww_amax(R)) : 0.f;
+    if (two_shot) {
+      write_wire_w<MODE>(d.peer[r / chunk] + my_slot, R, r, rows, cols, lane, sc);
+    } else {
+      for (int k = 0; k < d.ws; ++k) write_wire_w<MODE>(d.peer[(d.rank + k) % d.ws] + my_slot, R, r, rows, cols, lane, sc);
+    }
+  }
+  signal(d, site, 0, epoch, all);
+  if (!wait_all(d, site, 0, epoch, all, &abort_sm)) { finish(); return; }
+  char *slots[MAX_WS];
+  for (int k = 0; k < d.ws; ++k) slots[k] = d.peer[d.rank] + d.off_recv[site] + half + (size_t)k * d.slot_bytes[site];
+  if (!two_shot) {
+    for (int r = j * WPB + warp; r < rows; r += G * WPB) {
+      reduce_w<MODE>(slots, d.ws, r, rows, cols, lane, R);
+      round_w(R, e.rdt);
+      epilogue_w<EPI>(e, R, r, cols, lane);
+    }
+    finish();
+    return;
+  }
+  // owner rows: the rows of rank d.rank's chunk that this warp covers
+  for (int r = j * WPB + warp; r < rows; r += G * WPB) {
+    if (r / chunk != d.rank) continue;
+    reduce_w<MODE>(slots, d.ws, r, rows, cols, lane, R);
+    round_w(R, e.rdt);
+    for (int k = 0; k < d.ws; ++k) store_gather_w(d.peer[(d.rank + k) % d.ws] + d.off_gath[site], R, r, cols, lane, e.rdt);
+  }
+  signal(d, site, 1, epoch, all);
+  if (!wait_all(d, site, 1, epoch, all, &abort_sm)) { finish(); return; }
+  const char *gath_local = d.peer[d.rank] + d.off_gath[site];
+  for (int r = j * WPB + warp; r < rows; r += G * WPB) {
+    load_gather_w(gath_local, R, r, cols, lane, e.rdt);
+    epilogue_w<EPI>(e, R, r, cols, lane);
+  }
+  finish();
+}
+
 // ----------------------------------------------------------------- standalone quantiser / dequant
 __global__ void quantize_rows_kernel(const float *__restrict__ in, int rows, int cols, int ld, float *scales, int8_t *q) {
   MTP_PDL_WAIT();
@@ -754,6 +1166,28 @@ static float *row_scratch(size_t bytes) {
 // context the grid is sized to fill every SM at that occupancy: CTA j only waits for CTA
 // j of the other ranks, and CTAs are dispatched in index order, so every launched CTA
 // becomes resident once the preceding kernel has drained.
+// Rows wide enough (and outputs aligned) for reduce_wide_kernel.  The EPI_XPROJ split
+// (dt_low | B|C) keeps the narrow kernels: its rows are at most a few hundred values.
+static bool wide_ok(int epi, int cols, const EpiOut &e) {
+  if (epi == EPI_XPROJ || cols % 16 != 0 || cols < 512 || cols > 3072) return false;
+  if (epi == EPI_PLAIN) return aligned16(e.out);
+  return aligned16(e.resid) && (!e.bias || aligned16(e.bias)) && (!e.normed || (aligned16(e.normed) && aligned16(e.norm_w)));
+}
+
+// Resident CTAs per SM of a wide-row kernel instance (queried once per instance).
+template <int M, int E, int NC>
+static int wide_occupancy() {
+  static int occ = 0;
+  if (occ == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, reduce_wide_kernel<M, E, NC>, WPB * 32, 0) != cudaSuccess ||
+        n < 1)
+      n = 1;
+    occ = n;
+  }
+  return occ;
+}
+
 template <int M, int E, int V>
 static int rows_kernel_occupancy() {
   static int occ = 0;
@@ -765,6 +1199,42 @@ static int rows_kernel_occupancy() {
     occ = n;
   }
   return occ;
+}
+
+// Wire bytes of one row in `mode`, and of one reduced row in the result dtype.
+static size_t wire_row_bytes(int mode, int cols) {
+  return mode == MTP_RED_FP32 ? 4 * (size_t)cols : mode == MTP_RED_FP16 ? 2 * (size_t)cols : (size_t)cols + 4;
+}
+static size_t rdt_row_bytes(int rdt, int cols) { return (rdt == MTP_BF16 ? 2 : 4) * (size_t)cols; }
+
+// Protocol of one reduction launch of nr rows: fewer bytes sent per rank wins; small
+// messages stay one-shot (one flag round).  MTP_COMM_PROTOCOL=oneshot|twoshot overrides.
+static bool use_two_shot(int ws, int mode, int nr, int cols, int rdt) {
+  if (ws < 2) return false;
+  const size_t wire_row = wire_row_bytes(mode, cols), rdt_row = rdt_row_bytes(rdt, cols);
+  const double one = (double)(ws - 1) * nr * wire_row;
+  const double two = (double)(ws - 1) / ws * nr * (wire_row + rdt_row);
+  bool two_shot = two < one && (size_t)nr * wire_row >= ((size_t)1 << 20);
+  if (const char *env = getenv("MTP_COMM_PROTOCOL")) {
+    if (!strcmp(env, "twoshot")) two_shot = true;
+    if (!strcmp(env, "oneshot")) two_shot = false;
+  }
+  return two_shot;
+}
+
+// Bytes one rank sends to its peers for a reduction of [rows, cols] (launches of at most
+// max_rows rows): one-shot (ws-1) wire rows per row; two-shot (ws-1)/ws of the wire rows
+// to their owners plus (ws-1)/ws of the reduced rows back to every rank.
+static double sent_bytes(int ws, int max_rows, int mode, int rows, int cols, int rdt) {
+  if (ws < 2) return 0.0;
+  double total = 0.0;
+  for (int r0 = 0; r0 < rows; r0 += max_rows) {
+    const int nr = rows - r0 < max_rows ? rows - r0 : max_rows;
+    const double w = (double)nr * wire_row_bytes(mode, cols);
+    total += use_two_shot(ws, mode, nr, cols, rdt) ? (double)(ws - 1) / ws * (w + (double)nr * rdt_row_bytes(rdt, cols))
+                                                   : (double)(ws - 1) * w;
+  }
+  return total;
 }
 
 template <int EPI>
@@ -807,24 +1277,41 @@ static int run_reduce(mtp_comm *c, int site, int mode, const float *partial, int
     }
     CommDev d{};
     if (has_comm) d = c->d;
-    // protocol: fewer bytes sent per rank wins; small messages stay one-shot (one flag round)
-    const size_t wire_row = mode == MTP_RED_FP32 ? 4 * (size_t)cols : mode == MTP_RED_FP16 ? 2 * (size_t)cols : cols + 4;
-    const size_t rdt_row = (e.rdt == MTP_BF16 ? 2 : 4) * (size_t)cols;
-    bool two_shot = false;
-    if (has_comm) {
-      const int ws = c->d.ws;
-      const double one = (double)(ws - 1) * nr * wire_row;
-      const double two = (double)(ws - 1) / ws * nr * (wire_row + rdt_row);
-      two_shot = two < one && (size_t)nr * wire_row >= ((size_t)1 << 20);
-    }
-    // protocol override (tests, tuning): MTP_COMM_PROTOCOL=oneshot|twoshot
-    if (has_comm) {
-      if (const char *env = getenv("MTP_COMM_PROTOCOL")) {
-        if (!strcmp(env, "twoshot")) two_shot = true;
-        if (!strcmp(env, "oneshot")) two_shot = false;
-      }
-    }
+    const bool two_shot = has_comm && use_two_shot(c->d.ws, mode, nr, cols, e.rdt);
     const float *pp = partial + (size_t)r0 * cols;
+    // wide rows in 16-column granules (16-byte accesses) when the width and the output
+    // pointers allow it, else the register-row kernel, else the scratch kernel
+    ee.wide = wide_ok(EPI, cols, ee) ? 1 : 0;
+    if (!capped && ee.wide) {
+      const int nc = (cols + 511) / 512;
+      const int Gwant = ceil_div(nr, WPB);
+#define MTP_RW(M, NCC)                                                                                           \
+  do {                                                                                                           \
+    int cap_ = has_comm ? sms * wide_occupancy<M, EPI, NCC>() : sms * 8;                                         \
+    if (cap_ > G_MAX && has_comm) cap_ = G_MAX;                                                                  \
+    const int Gv = Gwant < cap_ ? Gwant : cap_;                                                                  \
+    launch_pdl(reduce_wide_kernel<M, EPI, NCC>, dim3(Gv), dim3(WPB * 32), 0, s, d, has_comm, site, pp, nr, cols, \
+               two_shot, ee);                                                                                    \
+  } while (0)
+#define MTP_RW_MODE(NCC)                                    \
+  do {                                                      \
+    if (mode == MTP_RED_FP32) MTP_RW(MTP_RED_FP32, NCC);      \
+    else if (mode == MTP_RED_FP16) MTP_RW(MTP_RED_FP16, NCC); \
+    else MTP_RW(MTP_RED_INT8TOK, NCC);                        \
+  } while (0)
+      switch (nc) {
+        case 2: MTP_RW_MODE(2); break;
+        case 3: MTP_RW_MODE(3); break;
+        case 4: MTP_RW_MODE(4); break;
+        case 5: MTP_RW_MODE(5); break;
+        default: MTP_RW_MODE(6); break;
+      }
+#undef MTP_RW_MODE
+#undef MTP_RW
+      int rc = check_launch("reduce");
+      if (rc) return rc;
+      continue;
+    }
     // register-row kernel when the width allows it
     const int vpl = (cols % 4 != 0 || capped) ? 0 : cols <= 256 ? 2 : cols <= 512 ? 4 : cols <= 1024 ? 8 : cols <= 2048 ? 16 : cols <= 3072 ? 24 : 0;
     if (vpl) {
@@ -967,6 +1454,12 @@ int mtp_comm_set_max_ctas(mtp_comm *c, int max_ctas) {
 int mtp_comm_reset_status(mtp_comm *c) {
   MTP_REQUIRE(c, "null argument");
   if (cudaMemset(c->base + c->d.off_status, 0, sizeof(int)) != cudaSuccess) return fail(MTP_ERR_CUDA, "reset status");
+  return MTP_OK;
+}
+
+int mtp_comm_sent_bytes(mtp_comm *c, int mode, int rows, int cols, int rdt, double *bytes) {
+  MTP_REQUIRE(bytes && rows >= 0 && cols > 0, "bad arguments");
+  *bytes = (c && c->d.ws > 1) ? sent_bytes(c->d.ws, c->max_rows, mode, rows, cols, rdt) : 0.0;
   return MTP_OK;
 }
 

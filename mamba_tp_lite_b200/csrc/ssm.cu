@@ -6,6 +6,7 @@
 //   y_t   = (sum_n C_t[n] * h_t[n] + D * xc_t) * silu(z_t)
 // restating mamba_lite/tp_model.py:93-129 (prefill) and :145-173 (step).
 #include <cstdlib>
+#include <type_traits>
 #include "common.cuh"
 #include "tc_common.cuh"
 
@@ -350,6 +351,251 @@ __global__ void __launch_bounds__(128, (TPC == 1 ? 4 : 6)) scan_prefill_kernel(
     if (sub == 0) {
 #pragma unroll
       for (int j = 0; j < K - 1; ++j) stf(conv_final + ((size_t)b * Es + c) * (K - 1) + j, win[j]);
+    }
+  }
+}
+
+// ----------------------------------------------------------------- scan over the conv output
+// The recurrence of the fused prefill above, fed with xc = SiLU(conv1d(x)) as written by
+// conv1d_silu_vec_kernel for x_proj (so the scan spends no SFU work on the conv), with
+// the SFU load cut further:
+//   * the state update runs on packed fp32 pairs (fma.rn.f32x2 / mul.rn.f32x2, sm_100a);
+//   * NPP of the thread's N/(2 TPC) state pairs take exp2 on the FP32 pipe
+//     (exp2_poly2 below) instead of the MUFU unit, which stays the limit otherwise;
+//   * bf16 models gate with silu(z) = h + h tanh(h), h = z/2 (one tanh.approx,
+//     |error| <= 2.5e-4 of |z|, below a bf16 step); fp32 models keep z / (1 + e^-z).
+// TPC threads share a channel; for TPC > 1 the gate of position tt is computed and
+// y stored by lane tt % TPC of the channel, spreading that work over the lanes.
+
+// 2^x, x <= 0, on the FP32 pipe, for a pair of values.  Range reduction in the style of
+// Cody and Waite: j = rint(x) through the 1.5 * 2^23 rounding constant (the sum's low
+// mantissa bits hold j), f = x - j in [-1/2, 1/2]; 2^f by a degree-5 polynomial fitted for
+// minimum relative error on [-1/2, 1/2] with the Remez exchange algorithm
+// (csrc/fit_exp2_poly.py prints these coefficients); 2^j is added into the exponent field.
+// Relative error <= 2.4e-7 (fp32 Horner included) for x in [-125, 0]; x < -125 gives
+// 2^-125 (the ex2.approx.ftz result there is 0; both are negligible as a state decay).
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float RND = 12582912.0f;  // 1.5 * 2^23
+  constexpr float P0 = 1.0000001192092896f, P1 = 0.6931469440460205f, P2 = 0.24022120237350464f,
+                  P3 = 0.05550713092088699f, P4 = 0.009675540961325169f, P5 = 0.0013276472454890609f;
+  x.x = fmaxf(x.x, -125.0f);
+  x.y = fmaxf(x.y, -125.0f);
+  const float2 t = __fadd2_rn(x, make_float2(RND, RND));
+  const float2 nj = __ffma2_rn(t, make_float2(-1.0f, -1.0f), make_float2(RND, RND));  // -rint(x), exact
+  const float2 f = __fadd2_rn(x, nj);
+  float2 p = __ffma2_rn(make_float2(P5, P5), f, make_float2(P4, P4));
+  p = __ffma2_rn(p, f, make_float2(P3, P3));
+  p = __ffma2_rn(p, f, make_float2(P2, P2));
+  p = __ffma2_rn(p, f, make_float2(P1, P1));
+  p = __ffma2_rn(p, f, make_float2(P0, P0));
+  // the rounded sum's bits are 0x4B400000 + j; shifted by 23 only j << 23 survives (mod 2^32)
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+
+__device__ __forceinline__ float tanh_hw(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <typename T> __device__ __forceinline__ float gate_silu(float z);
+template <> __device__ __forceinline__ float gate_silu<__nv_bfloat16>(float z) {
+  const float h = 0.5f * z;
+  return fmaf(h, tanh_hw(h), h);
+}
+template <> __device__ __forceinline__ float gate_silu<float>(float z) { return silu_fast(z); }
+
+__global__ void exp2_fma_kernel(const float *__restrict__ x, float *__restrict__ out, int n) {
+  MTP_PDL_WAIT();
+  MTP_PDL_TRIGGER();
+  const int i = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (i >= n) return;
+  const float2 v = exp2_poly2(make_float2(x[i], i + 1 < n ? x[i + 1] : 0.f));
+  out[i] = v.x;
+  if (i + 1 < n) out[i + 1] = v.y;
+}
+
+template <typename T, typename TD, int N, int TPC, int TL>
+struct ScanXcSmem {
+  static constexpr int CB = 128 / TPC;
+  T xc[2][TL][CB];
+  T z[2][TL][CB];
+  TD dt[2][TL][CB];
+  float bc[2][TL][2 * N];
+};
+
+template <typename T, typename TD, int N, int TPC, int TL, int K, int NPP, int MINB>
+__global__ void __launch_bounds__(128, MINB) scan_xc_kernel(
+    const T *__restrict__ xc, int ld_xc, const T *__restrict__ xz, int ld_xz, const TD *__restrict__ dtp, int ld_dt,
+    const float *__restrict__ bcp, int ld_bc, const T *__restrict__ A_log, const T *__restrict__ Dp,
+    const T *conv_init, const float *ssm_init, T *__restrict__ y, int ld_y, T *conv_final, float *ssm_final, int L,
+    int Es, bool vec16) {
+  MTP_PDL_WAIT();
+  MTP_PDL_TRIGGER();
+  using S = ScanXcSmem<T, TD, N, TPC, TL>;
+  constexpr int CB = S::CB;
+  constexpr int NS = N / TPC;  // states per thread
+  constexpr int NP = NS / 2;   // state pairs per thread
+  static_assert(NS % 4 == 0 && NPP <= NP, "states per thread: a multiple of 4");
+  constexpr int NT = 128;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  S &sm = *reinterpret_cast<S *>(smem_raw);
+
+  const int b = blockIdx.y;
+  const int c0 = blockIdx.x * CB;
+  const int cl = threadIdx.x / TPC;
+  const int sub = threadIdx.x % TPC;
+  const int c = c0 + cl;
+  const bool live = c < Es;
+  const int ncb = min(CB, Es - c0);
+  const size_t row0 = (size_t)b * L;
+
+  float2 A2[NP], h[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const int n = sub * NS + 2 * i;
+    A2[i].x = live ? -expf(ldf(A_log + (size_t)c * N + n)) * kLog2e : 0.f;
+    A2[i].y = live ? -expf(ldf(A_log + (size_t)c * N + n + 1)) * kLog2e : 0.f;
+    h[i].x = (live && ssm_init) ? ssm_init[((size_t)b * Es + c) * N + n] : 0.f;
+    h[i].y = (live && ssm_init) ? ssm_init[((size_t)b * Es + c) * N + n + 1] : 0.f;
+  }
+  const float Dv = live ? ldf(Dp + c) : 0.f;
+
+  auto load_chunk = [&](int k, int buf) {
+    const int t0 = k * TL;
+    const int tl = min(TL, L - t0);
+    if (vec16) {  // full channel blocks, 16-byte aligned rows
+      constexpr int XW = CB * (int)sizeof(T) / 16, DW = CB * (int)sizeof(TD) / 16, BW = 2 * N * 4 / 16;
+      constexpr int DE = 16 / (int)sizeof(TD);
+      for (int i = threadIdx.x; i < tl * XW; i += NT) {
+        const int tt = i / XW, w = i % XW;
+        cp_async16(reinterpret_cast<char *>(&sm.xc[buf][tt][0]) + 16 * w,
+                   reinterpret_cast<const char *>(xc + (row0 + t0 + tt) * ld_xc + c0) + 16 * w);
+        cp_async16(reinterpret_cast<char *>(&sm.z[buf][tt][0]) + 16 * w,
+                   reinterpret_cast<const char *>(xz + (row0 + t0 + tt) * ld_xz + Es + c0) + 16 * w);
+      }
+      for (int i = threadIdx.x; i < tl * DW; i += NT) {
+        const int tt = i / DW, w = i % DW;
+        cp_async16(&sm.dt[buf][tt][DE * w], dtp + (row0 + t0 + tt) * ld_dt + c0 + DE * w);
+      }
+      for (int i = threadIdx.x; i < tl * BW; i += NT) {
+        const int tt = i / BW, w = i % BW;
+        cp_async16(&sm.bc[buf][tt][4 * w], bcp + (row0 + t0 + tt) * ld_bc + 4 * w);
+      }
+    } else {  // 4-byte granules, partial channel blocks
+      constexpr int EPW = 4 / sizeof(T);
+      const int wpr = (ncb + EPW - 1) / EPW;
+      for (int i = threadIdx.x; i < tl * wpr; i += NT) {
+        const int tt = i / wpr, wi = i % wpr;
+        cp_async4(&sm.xc[buf][tt][wi * EPW], xc + (row0 + t0 + tt) * ld_xc + c0 + wi * EPW);
+        cp_async4(&sm.z[buf][tt][wi * EPW], xz + (row0 + t0 + tt) * ld_xz + Es + c0 + wi * EPW);
+      }
+      constexpr int DPW = 4 / sizeof(TD);
+      const int dpr = (ncb + DPW - 1) / DPW;
+      for (int i = threadIdx.x; i < tl * dpr; i += NT) {
+        const int tt = i / dpr, wi = i % dpr;
+        cp_async4(&sm.dt[buf][tt][wi * DPW], dtp + (row0 + t0 + tt) * ld_dt + c0 + wi * DPW);
+      }
+      for (int i = threadIdx.x; i < tl * 2 * N; i += NT) {
+        const int tt = i / (2 * N), j = i % (2 * N);
+        cp_async4(&sm.bc[buf][tt][j], bcp + (row0 + t0 + tt) * ld_bc + j);
+      }
+    }
+    cp_async_commit();
+  };
+
+  const int nchunks = (L + TL - 1) / TL;
+  load_chunk(0, 0);
+  for (int k = 0; k < nchunks; ++k) {
+    const int buf = k & 1;
+    if (k + 1 < nchunks) {
+      load_chunk(k + 1, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const int t0 = k * TL;
+    const int tl = min(TL, L - t0);
+    // TPC > 1: gates of the positions this lane stores, tt = sub + TPC * i, computed up
+    // front (one lane per position); TPC == 1 gates each position where it is stored
+    constexpr int NG = TPC == 1 ? 1 : TL / TPC;
+    float gt[NG];
+    if constexpr (TPC > 1) {
+#pragma unroll
+      for (int i = 0; i < NG; ++i) {
+        const int tt = sub + TPC * i;
+        gt[i] = tt < tl ? gate_silu<T>(ldf(&sm.z[buf][tt][cl])) : 0.f;
+      }
+    }
+    T *ychunk = y + (row0 + t0) * ld_y + c;
+    auto token = [&](const int tt) {
+      const float xv = ldf(&sm.xc[buf][tt][cl]);
+      const float dt = ldf(&sm.dt[buf][tt][cl]);
+      const float2 dt2 = make_float2(dt, dt);
+      const float dtx = dt * xv;
+      const float2 dtx2 = make_float2(dtx, dtx);
+      const float4 *bv = reinterpret_cast<const float4 *>(&sm.bc[buf][tt][sub * NS]);
+      const float4 *cv = reinterpret_cast<const float4 *>(&sm.bc[buf][tt][N + sub * NS]);
+      float2 ya = make_float2(0.f, 0.f), yb = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int q = 0; q < NS / 4; ++q) {
+        const float4 B4 = bv[q], C4 = cv[q];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int i = 2 * q + u;
+          const float2 Bp = u ? make_float2(B4.z, B4.w) : make_float2(B4.x, B4.y);
+          const float2 Cp = u ? make_float2(C4.z, C4.w) : make_float2(C4.x, C4.y);
+          const float2 arg = __fmul2_rn(dt2, A2[i]);
+          float2 dA;
+          if (i < NPP) {
+            dA = exp2_poly2(arg);
+          } else {
+            dA.x = ex2_hw(arg.x);
+            dA.y = ex2_hw(arg.y);
+          }
+          h[i] = __ffma2_rn(dA, h[i], __fmul2_rn(Bp, dtx2));
+          if (u) yb = __ffma2_rn(Cp, h[i], yb);
+          else ya = __ffma2_rn(Cp, h[i], ya);
+        }
+      }
+      const float2 ys = __fadd2_rn(ya, yb);
+      float yv = ys.x + ys.y;
+#pragma unroll
+      for (int o = 1; o < TPC; o <<= 1) yv += __shfl_xor_sync(0xffffffffu, yv, o);
+      if constexpr (TPC == 1) {
+        if (live) stf(ychunk + (size_t)tt * ld_y, fmaf(Dv, xv, yv) * gate_silu<T>(ldf(&sm.z[buf][tt][cl])));
+      } else {
+        if (sub == tt % TPC && live) stf(ychunk + (size_t)tt * ld_y, fmaf(Dv, xv, yv) * gt[tt / TPC]);
+      }
+    };
+    // (a guard-free copy of this loop for full chunks measured slower: the interleaving it
+    // allows spills registers)
+#pragma unroll
+    for (int tt = 0; tt < TL; ++tt)
+      if (tt < tl) token(tt);
+    // buffer `buf` is refilled by the next iteration's prefetch only after this barrier
+    __syncthreads();
+  }
+  if (live) {
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+      ssm_final[((size_t)b * Es + c) * N + sub * NS + 2 * i] = h[i].x;
+      ssm_final[((size_t)b * Es + c) * N + sub * NS + 2 * i + 1] = h[i].y;
+    }
+    if (sub == 0) {
+      // conv history for the next chunk: the last K-1 inputs of [conv_init | x]
+      // (all read before any write: conv_final may alias conv_init)
+      float hv[K - 1];
+#pragma unroll
+      for (int j = 0; j < K - 1; ++j) {
+        const int t = L - (K - 1) + j;
+        hv[j] = t >= 0 ? ldf(xz + (row0 + t) * ld_xz + c)
+                       : (conv_init ? ldf(conv_init + ((size_t)b * Es + c) * (K - 1) + (K - 1 + t)) : 0.f);
+      }
+#pragma unroll
+      for (int j = 0; j < K - 1; ++j) stf(conv_final + ((size_t)b * Es + c) * (K - 1) + j, hv[j]);
     }
   }
 }
@@ -724,6 +970,67 @@ static int launch_scan(const void *xz, int ld_xz, const void *dt_v, int ld_dt, c
   return check_launch("scan_prefill");
 }
 
+
+// Default number of state pairs per thread whose exponential runs on the FP32 pipe
+// (exp2_poly2), by threads per channel; MTP_SCAN_POLY overrides it (0 .. N / (2 TPC)).
+constexpr int kPolyPairsTpc1 = 0, kPolyPairsTpc2 = 0, kPolyPairsTpc4 = 0;
+
+template <typename T, typename TD, int N, int TPC, int NPP, int MINB>
+static int launch_scan_xc(const void *xc, int ld_xc, const void *xz, int ld_xz, const void *dt_v, int ld_dt,
+                          const float *bc, int ld_bc, const void *A_log, const void *Dp, const void *conv_init,
+                          const float *ssm_init, void *y, int ld_y, void *conv_final, float *ssm_final, int B, int L,
+                          int Es, cudaStream_t s) {
+  constexpr int TL = 16, K = 4;
+  using S = ScanXcSmem<T, TD, N, TPC, TL>;
+  constexpr int CB = S::CB;
+  auto kern = scan_xc_kernel<T, TD, N, TPC, TL, K, NPP, MINB>;
+  const TD *dt = (const TD *)dt_v;
+  static bool attr_set = false;  // per template instance
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(S)) != cudaSuccess)
+      return check_launch("scan_prefill_xc attr");
+    attr_set = true;
+  }
+  const bool vec16 = Es % CB == 0 && aligned16(xc) && aligned16(xz) && aligned16(dt) && aligned16(bc) &&
+                     ((size_t)ld_xc * sizeof(T)) % 16 == 0 && ((size_t)ld_xz * sizeof(T)) % 16 == 0 &&
+                     ((size_t)Es * sizeof(T)) % 16 == 0 && ((size_t)ld_dt * sizeof(TD)) % 16 == 0 && ld_bc % 4 == 0;
+  dim3 grid((Es + CB - 1) / CB, B);
+  launch_pdl(kern, dim3(grid), dim3(128), sizeof(S), s, (const T *)xc, ld_xc, (const T *)xz, ld_xz, dt, ld_dt, bc,
+             ld_bc, (const T *)A_log, (const T *)Dp, (const T *)conv_init, ssm_init, (T *)y, ld_y, (T *)conv_final,
+             ssm_final, L, Es, vec16);
+  return check_launch("scan_prefill_xc");
+}
+
+// Picks the instance for (threads per channel, polynomial pairs, CTAs per SM).  The
+// FP32-pipe exponential did not pay on B200 (1.4b TP=1 shard, 32 x 1024: 0.69 ms with no
+// polynomial pairs, 0.71 / 0.77 / 0.83 / 0.90 ms with 1 / 2 / 3 / 4 of 8), so every
+// default is 0; bf16 models with bf16 dt and d_state 16 also build one polynomial split
+// per width (MTP_SCAN_POLY, tests) and, for one thread per channel, 4, 5 or 6 resident
+// CTAs per SM (MTP_SCAN_OCC; 4, the default, measured best: 0.688 / 0.691 / 0.690 ms).
+template <typename T, typename TD, int N, int TPC>
+static int scan_xc_npp(int npp, int occ, const void *xc, int ld_xc, const void *xz, int ld_xz, const void *dt,
+                       int ld_dt, const float *bc, int ld_bc, const void *A_log, const void *Dp, const void *conv_init,
+                       const float *ssm_init, void *y, int ld_y, void *conv_final, float *ssm_final, int B, int L,
+                       int Es, cudaStream_t s) {
+#define MTP_SXC(P, OCC)                                                                                          \
+  return launch_scan_xc<T, TD, N, TPC, P, OCC>(xc, ld_xc, xz, ld_xz, dt, ld_dt, bc, ld_bc, A_log, Dp, conv_init, \
+                                               ssm_init, y, ld_y, conv_final, ssm_final, B, L, Es, s)
+  constexpr int NP = N / TPC / 2;
+  constexpr int DEF = TPC == 1 ? kPolyPairsTpc1 : TPC == 2 ? kPolyPairsTpc2 : kPolyPairsTpc4;
+  constexpr int D0 = DEF < NP ? DEF : NP;
+  constexpr int OCC0 = TPC == 1 ? 4 : 6;
+  constexpr int P1 = NP >= 2 ? 2 : 1;
+  constexpr bool ALL = std::is_same<T, __nv_bfloat16>::value && std::is_same<TD, __nv_bfloat16>::value && N == 16;
+  if constexpr (ALL) {
+    if (npp == P1) MTP_SXC(P1, OCC0);
+    if constexpr (TPC == 1) {
+      if (npp == D0 && occ == 5) MTP_SXC(D0, 5);
+      if (npp == D0 && occ == 6) MTP_SXC(D0, 6);
+    }
+  }
+  MTP_SXC(D0, OCC0);
+#undef MTP_SXC
+}
 }  // namespace mtp
 
 using namespace mtp;
@@ -803,6 +1110,63 @@ int mtp_scan_prefill(const void *xz, int ld_xz, const void *dt, int ld_dt, int d
   }
 #undef MTP_SCAN_CASE
   return fail(MTP_ERR_UNSUPPORTED, "scan_prefill: dtype must be F32 or BF16");
+}
+
+int mtp_scan_prefill_xc(const void *xc, int ld_xc, const void *xz, int ld_xz, const void *dt, int ld_dt, int dt_dtype,
+                        const float *bc, int ld_bc, const void *A_log, const void *Dp, const void *conv_init,
+                        const float *ssm_init, void *y, int ld_y, void *conv_final, float *ssm_final, int B, int L,
+                        int Es, int N, int K, int dtype, void *stream) {
+  MTP_REQUIRE(xc && xz && dt && bc && A_log && Dp && y && conv_final && ssm_final, "null pointer");
+  MTP_REQUIRE(B >= 0 && L >= 0 && Es > 0, "bad sizes");
+  MTP_REQUIRE(K == 4, "only d_conv == 4 is built");
+  MTP_REQUIRE(N == 16 || N == 8, "d_state must be 8 or 16");
+  MTP_REQUIRE(ld_xc >= Es && ld_xz >= 2 * Es && ld_dt >= Es && ld_bc >= 2 * N && ld_y >= Es,
+              "leading dimensions too small");
+  MTP_REQUIRE(dtype == MTP_F32 || dtype == MTP_BF16, "dtype must be F32 or BF16");
+  const size_t es = dtype == MTP_F32 ? 4 : 2;
+  // 4-byte cp.async granules: element pairs must be 4-byte aligned
+  MTP_REQUIRE(aligned(xc, 4) && aligned(xz, 4) && aligned(dt, 4) && aligned(bc, 4), "inputs must be 4-byte aligned");
+  MTP_REQUIRE(es == 4 || (ld_xz % 2 == 0 && ld_xc % 2 == 0 && Es % 2 == 0), "bf16 rows need even Es and strides");
+  MTP_REQUIRE(dt_dtype == MTP_F32 || dt_dtype == dtype, "dt must be F32 or the model dtype");
+  MTP_REQUIRE(dt_dtype == MTP_F32 || (ld_dt % 2 == 0 && Es % 2 == 0), "bf16 dt rows need even Es and ld_dt");
+  if (B == 0 || L == 0) return MTP_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const long pairs = (long)B * Es;
+  const int sms = num_sms();
+  int tpc = pairs >= (long)sms * 128 ? 1 : (pairs >= (long)sms * 32 ? 2 : 4);
+  if (const char *env = getenv("MTP_SCAN_TPC")) {
+    const int v = atoi(env);
+    if (v == 1 || v == 2 || v == 4) tpc = v;
+  }
+  if (N == 8) tpc = 2;
+  int npp = tpc == 1 ? kPolyPairsTpc1 : tpc == 2 ? kPolyPairsTpc2 : kPolyPairsTpc4;
+  if (const char *env = getenv("MTP_SCAN_POLY")) npp = atoi(env);
+  if (npp < 0) npp = 0;
+  int occ = 0;
+  if (const char *env = getenv("MTP_SCAN_OCC")) occ = atoi(env);
+#define MTP_SXC_CASE(TT, TDD, NN, TP)                                                                          \
+  return scan_xc_npp<TT, TDD, NN, TP>(npp, occ, xc, ld_xc, xz, ld_xz, dt, ld_dt, bc, ld_bc, A_log, Dp, conv_init, \
+                                      ssm_init, y, ld_y, conv_final, ssm_final, B, L, Es, s)
+  using bf16 = __nv_bfloat16;
+  if (dtype == MTP_F32) {
+    if (N == 16) { if (tpc == 1) MTP_SXC_CASE(float, float, 16, 1); if (tpc == 2) MTP_SXC_CASE(float, float, 16, 2); MTP_SXC_CASE(float, float, 16, 4); }
+    MTP_SXC_CASE(float, float, 8, 2);
+  } else if (dt_dtype == MTP_F32) {
+    if (N == 16) { if (tpc == 1) MTP_SXC_CASE(bf16, float, 16, 1); if (tpc == 2) MTP_SXC_CASE(bf16, float, 16, 2); MTP_SXC_CASE(bf16, float, 16, 4); }
+    MTP_SXC_CASE(bf16, float, 8, 2);
+  } else {
+    if (N == 16) { if (tpc == 1) MTP_SXC_CASE(bf16, bf16, 16, 1); if (tpc == 2) MTP_SXC_CASE(bf16, bf16, 16, 2); MTP_SXC_CASE(bf16, bf16, 16, 4); }
+    MTP_SXC_CASE(bf16, bf16, 8, 2);
+  }
+#undef MTP_SXC_CASE
+}
+
+int mtp_exp2_fma(const float *x, float *out, int n, void *stream) {
+  MTP_REQUIRE(x && out && n >= 0, "bad arguments");
+  if (n == 0) return MTP_OK;
+  const int pairs = (n + 1) / 2;
+  launch_pdl(exp2_fma_kernel, dim3((pairs + 255) / 256), dim3(256), 0, (cudaStream_t)stream, x, out, n);
+  return check_launch("exp2_fma");
 }
 
 int mtp_scan_prefill_fused(const void *xz, int ld_xz, const void *dt_low, int ld_dl, const void *W_dt,

@@ -90,8 +90,16 @@ def bench_scan(a):
     Wdt = torch.randn(es, R, device="cuda", dtype=dt_) * 0.05
     bdt = (torch.rand(es, device="cuda") * 4 - 7).to(dt_)
 
+    if a.fused:
+        a.variant = "raw"
+    xc = torch.randn(T, es, device="cuda", dtype=dt_) if a.variant == "xc" else None
+
     def run():
-        if a.fused:
+        if a.variant == "xc":
+            L.call("mtp_scan_prefill_xc", L.ptr(xc), es, L.ptr(xz), 2 * es, L.ptr(dt), es, L.dtype_code(dt.dtype),
+                   L.ptr(bc), 2 * n, L.ptr(A_log), L.ptr(Dp), None, None, L.ptr(y), es, L.ptr(cf), L.ptr(sf), B, Lq, es,
+                   n, 4, L.BF16, L.stream_ptr())
+        elif a.fused:
             L.call("mtp_scan_prefill_fused", L.ptr(xz), 2 * es, L.ptr(dl), R, L.ptr(Wdt), L.ptr(bdt), L.ptr(bc), 2 * n,
                    L.ptr(A_log), L.ptr(Dp), L.ptr(cw), L.ptr(cb), None, None, L.ptr(y), es, L.ptr(cf), L.ptr(sf), B,
                    Lq, es, n, R, 4, L.stream_ptr())
@@ -101,12 +109,13 @@ def bench_scan(a):
                    es, n, 4, L.BF16, L.stream_ptr())
 
     ms = _time(run, a.warmup, a.iters)
-    # algorithmic bytes: x, z, y (bf16) and dt fp32 (or dt_low bf16 when fused), B|C fp32, states
+    # algorithmic bytes: x (or xc), z, y (bf16) and dt (or dt_low bf16 when fused), B|C fp32, states
     dt_bytes = R * 2 if a.fused else es * dt.element_size()
     nbytes = T * (es * 3 * 2 + dt_bytes + 2 * n * 4) + B * es * (n * 4 + 3 * 2)
     gbs = nbytes / (ms / 1e3) / 1e9
     exps = T * es * n
-    return {"kernel": "scan_prefill_fused" if a.fused else "scan_prefill", "B": B, "L": Lq, "Es": es, "avg_ms": ms,
+    name = "scan_prefill_fused" if a.fused else "scan_prefill_xc" if a.variant == "xc" else "scan_prefill"
+    return {"kernel": name, "B": B, "L": Lq, "Es": es, "avg_ms": ms,
             "GBps": gbs,
             "frac_of_hbm": gbs / peaks()["hbm_gbs"], "algorithmic_bytes": nbytes, "Gexp_per_s": exps / (ms / 1e3) / 1e9}
 
@@ -140,6 +149,13 @@ def bench_step(a):
 
 
 def bench_allreduce(a):
+    """One isolated reduction site: activations [rows, cols],
+    N(0, 1) with a seeded 1% of the columns scaled by 20, reduced over the ranks of the
+    run in each wire mode.  --epi plain: mtp_allreduce into fp32; --epi outproj: the
+    out_proj site as the model runs it (bf16 result, residual add and the next RMSNorm).
+    --sweep runs every (rows, cols, mode) of the configuration in one process.  Sent
+    bytes per rank come from the library's protocol choice (mtp_comm_sent_bytes); the
+    NCCL time is the reference's collective on the same tensor (tp_utils.py:27, :41, :120)."""
     import torch.distributed as dist
 
     from .tp_utils import Comm
@@ -150,65 +166,76 @@ def bench_allreduce(a):
     torch.cuda.set_device(local)
     if ws > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-    rows, cols = a.rows, a.cols
-    g = torch.Generator(device="cuda").manual_seed(rank * 1000 + rows)
-    x = torch.randn(rows, cols, device="cuda", generator=g)
-    x[:, torch.randperm(cols, device="cuda", generator=g)[: max(1, cols // 100)]] *= 20
-    out = torch.empty_like(x)
-    comm = Comm(None, rank, ws, cols, cols, max_rows=max(rows, 1)) if ws > 1 else None
-    if comm is not None and a.max_ctas:
-        comm.set_max_ctas(a.max_ctas)
-    mode = {"fp32": L.RED_FP32, "fp16": L.RED_FP16, "int8": L.RED_INT8TOK}[a.mode]
-
-    def run():
-        L.call("mtp_allreduce", None if comm is None else comm.ptr, 1, mode, L.ptr(x), L.ptr(out), rows, cols,
-               L.stream_ptr())
-
-    if ws > 1:
-        dist.barrier()
-    ms = _time(run, a.warmup, a.iters)
-    if ws > 1:
-        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = t.item()
-    esz = {"fp32": 4, "fp16": 2, "int8": 1}[a.mode]
-    per_row = cols * esz + (4 if a.mode == "int8" else 0)
-    two_shot = ws > 2 and rows * cols * 4 >= (1 << 20)
-    # bytes each rank sends over NVLink per call
-    if ws == 1:
-        sent = 0
-    elif two_shot:
-        sent = rows * per_row * (ws - 1) / ws + rows * cols * 4 * (ws - 1) / ws
-    else:
-        sent = rows * per_row * (ws - 1)
-    res = {"kernel": f"allreduce_{a.mode}", "ws": ws, "rows": rows, "cols": cols, "max_ctas": a.max_ctas,
-           "avg_us": ms * 1e3,
-           "protocol": "two-shot" if two_shot else "one-shot", "nvlink_bytes_sent_per_rank": sent,
-           "nvlink_GBps_per_direction": sent / (ms / 1e3) / 1e9 if sent else 0.0,
-           "frac_of_770": (sent / (ms / 1e3) / 1e9) / 770.0 if sent else 0.0}
-    if ws > 1 and a.nccl:
-        # the reference's collective on NCCL for the same tensor (tp_utils.py:27, :41, :120)
-        xb = x.clone()
-        if a.mode == "fp32":
-            fn = lambda: dist.all_reduce(xb, op=dist.ReduceOp.SUM)
-        elif a.mode == "fp16":
-            xh = x.half()
-            fn = lambda: dist.all_reduce(xh, op=dist.ReduceOp.SUM)
-        else:
-            payload = torch.empty(rows * (4 + cols), dtype=torch.uint8, device="cuda")
-            gathered = torch.empty(ws * payload.numel(), dtype=torch.uint8, device="cuda")
-            fn = lambda: dist.all_gather_into_tensor(gathered, payload)
-        dist.barrier()
-        nms = _time(fn, a.warmup, a.iters)
-        t = torch.tensor([nms], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        res["nccl_collective_us"] = t.item() * 1e3
-    if comm is not None:
+    modes = ["fp32", "fp16", "int8"] if a.sweep else [a.mode]
+    shapes = [(r, c) for c in (768, 2048, 2560) for r in (1, 32, 1024, 32768)] if a.sweep else [(a.rows, a.cols)]
+    comms = {}
+    results = []
+    for rows, cols in shapes:
+        if ws > 1 and cols not in comms:
+            comms[cols] = Comm(None, rank, ws, cols, cols)
+            if a.max_ctas:
+                comms[cols].set_max_ctas(a.max_ctas)
+        comm = comms.get(cols)
+        g = torch.Generator(device="cuda").manual_seed(rank * 1000 + rows)
+        x = torch.randn(rows, cols, device="cuda", generator=g)
+        x[:, torch.randperm(cols, device="cuda", generator=g)[: max(1, cols // 100)]] *= 20
+        out = torch.empty_like(x)
+        resid = torch.zeros(rows, cols, device="cuda")
+        normed = torch.empty(rows, cols, device="cuda", dtype=torch.bfloat16)
+        nw = torch.ones(cols, device="cuda", dtype=torch.bfloat16)
+        for mname in modes:
+            mode = {"fp32": L.RED_FP32, "fp16": L.RED_FP16, "int8": L.RED_INT8TOK}[mname]
+            cp = None if comm is None else comm.ptr
+            if a.epi == "outproj":
+                def run():
+                    L.call("mtp_reduce_outproj", cp, mode, L.ptr(x), rows, cols, None, L.ptr(resid), L.ptr(nw), 1e-5,
+                           L.ptr(normed), L.BF16, L.stream_ptr())
+                rdt = L.BF16
+            else:
+                def run():
+                    L.call("mtp_allreduce", cp, 1, mode, L.ptr(x), L.ptr(out), rows, cols, L.stream_ptr())
+                rdt = L.F32
+            if ws > 1:
+                dist.barrier()
+            ms = _time(run, a.warmup, a.iters)
+            if ws > 1:
+                t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                ms = t.item()
+            sent = L.comm_sent_bytes(cp, mode, rows, cols, rdt)
+            gbs = sent / (ms / 1e3) / 1e9 if sent else 0.0
+            res = {"kernel": f"reduce_{a.epi}_{mname}", "ws": ws, "rows": rows, "cols": cols, "max_ctas": a.max_ctas,
+                   "avg_us": ms * 1e3, "sent_bytes_per_rank": sent, "nvlink_GBps_per_direction": gbs,
+                   "frac_of_770_measured": gbs / 770.0, "frac_of_900_nominal": gbs / 900.0}
+            if ws > 1 and a.nccl:
+                xb = x.clone()
+                if mname == "fp32":
+                    fn = lambda: dist.all_reduce(xb, op=dist.ReduceOp.SUM)
+                elif mname == "fp16":
+                    xh = x.half()
+                    fn = lambda: dist.all_reduce(xh, op=dist.ReduceOp.SUM)
+                else:
+                    payload = torch.empty(rows * (4 + cols), dtype=torch.uint8, device="cuda")
+                    gathered = torch.empty(ws * payload.numel(), dtype=torch.uint8, device="cuda")
+                    fn = lambda: dist.all_gather_into_tensor(gathered, payload)
+                dist.barrier()
+                nms = _time(fn, a.warmup, a.iters)
+                t = torch.tensor([nms], device="cuda", dtype=torch.float64)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                res["nccl_collective_us"] = t.item() * 1e3
+            results.append(res)
+            if rank == 0 and a.sweep:
+                print(json.dumps(res), flush=True)
+        del x, out, resid, normed
+    for comm in comms.values():
         comm.check()
         comm.destroy()
+    if ws > 1:
         dist.barrier()
         dist.destroy_process_group()
-    return res if rank == 0 else None
+    if rank != 0:
+        return None
+    return None if a.sweep else results[0]
 
 
 def bench_decode(a):
@@ -277,6 +304,8 @@ def main():
     s.add_argument("--channels", type=int, default=4096)
     s.add_argument("--rank", type=int, default=128, help="dt_rank (fused variant)")
     s.add_argument("--fused", action="store_true", help="dt_proj + softplus inside the scan (tcgen05)")
+    s.add_argument("--variant", choices=["xc", "raw"], default="xc",
+                   help="xc: the scan over the conv output (prefill path); raw: conv inside the scan")
     s.add_argument("--dt", choices=["bf16", "f32"], default="bf16", help="dt element type (unfused scan)")
     st = sub.add_parser("step")
     st.add_argument("--batch", type=int, default=32)
@@ -288,6 +317,9 @@ def main():
     r.add_argument("--mode", choices=["fp32", "fp16", "int8"], default="int8")
     r.add_argument("--nccl", action="store_true", help="also time the NCCL collective of the reference path")
     r.add_argument("--max-ctas", type=int, default=0, help="cap the reduction grid (low-register kernel)")
+    r.add_argument("--epi", choices=["plain", "outproj"], default="plain",
+                   help="plain: fp32 out; outproj: bf16 result + residual + next RMSNorm (the model's site)")
+    r.add_argument("--sweep", action="store_true", help="every size and mode of the configuration, one line each")
     dcd = sub.add_parser("decode")
     dcd.add_argument("--shape", default="1.4b")
     dcd.add_argument("--layers", type=int, default=0, help="override n_layer (0: the shape's)")

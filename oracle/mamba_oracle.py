@@ -570,7 +570,24 @@ def scan_ref(x, z, dt, B, C, A_log, Dp, conv_w, conv_b, conv_init, ssm_init):
     softplus, B, C [B, L, N].  Returns (y [B,L,Es], conv_final, ssm_final)
     (tp_model.py:93-103, :113-129)."""
     xc, cf = conv_silu_ref(x, conv_w, conv_b, conv_init)
+    return scan_xc_ref(xc, cf, z, dt, B, C, A_log, Dp, ssm_init)
+
+
+def final_conv_history(x, conv_init, k=4):
+    """Last K-1 inputs of [conv_init | x] per (sequence, channel): the conv_state the
+    reference keeps after a prefill (tp_model.py:101-103).  x [B, L, Es]."""
     b, l, es = x.shape
+    h = np.zeros((b, es, k - 1), F32) if conv_init is None else conv_init.astype(F32)
+    xp = np.concatenate([h, np.transpose(x.astype(F32), (0, 2, 1))], axis=-1)
+    return xp[..., l:].copy()
+
+
+def scan_xc_ref(xc, conv_final, z, dt, B, C, A_log, Dp, ssm_init):
+    """Scan kernel contract with the conv output given: xc [B, L, Es] = SiLU(conv1d(x))
+    (tp_model.py:99-100), z, dt [B, L, Es], B, C [B, L, N].  Returns (y, conv_final,
+    ssm_final) (tp_model.py:113-129); conv_final is passed through."""
+    cf = conv_final
+    b, l, es = xc.shape
     n = A_log.shape[1]
     A = (-np.exp(A_log.astype(F32))).astype(F32)
     h = np.zeros((b, es, n), F32) if ssm_init is None else ssm_init.astype(F32).copy()

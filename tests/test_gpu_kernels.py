@@ -125,6 +125,97 @@ def test_scan_prefill_matches_oracle(dtype, b, l, es, nst, init, dt_in_model_dty
     np.testing.assert_allclose(n(sf), sf_ref, atol=tol, rtol=tol)
 
 
+SCAN_XC_CASES = [(2, 37, 64, 16, True), (1, 70, 200, 16, False), (3, 5, 96, 8, True), (4, 129, 1024, 16, True),
+                 (2, 2, 32, 16, False), (1, 9, 98, 16, True), (3, 300, 256, 16, True)]
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, BF])
+@pytest.mark.parametrize("b,l,es,nst,init", SCAN_XC_CASES)
+@pytest.mark.parametrize("tpc,npp,occ", [(None, None, None), ("1", "0", "4"), ("1", "0", "6"), ("1", "2", None),
+                                         ("2", "2", None), ("4", "2", None), ("2", "0", None), ("4", "0", None)])
+def test_scan_prefill_xc_matches_oracle(monkeypatch, dtype, b, l, es, nst, init, tpc, npp, occ):
+    """The scan fed with the conv output (the prefill path): every threads-per-channel
+    width, the FP32-pipe exponential split and the occupancy variants against the
+    oracle recurrence on the same xc."""
+    for var, val in (("MTP_SCAN_TPC", tpc), ("MTP_SCAN_POLY", npp), ("MTP_SCAN_OCC", occ)):
+        if val is not None:
+            monkeypatch.setenv(var, val)
+    x, z, dt, Bm, Cm, A_log, Dp, cw, cb, ci, si = _ssm_inputs(b, l, es, nst, 5, dtype)
+    if not init:
+        ci = si = None
+    rnd = O.bf16_round if dtype == BF else (lambda v: v)
+    xc_ref, _ = O.conv_silu_ref(x, cw, cb, ci)
+    xc_in = rnd(xc_ref)
+    dt = rnd(dt)
+    cf_ref = O.final_conv_history(x, ci)
+    y_ref, _, sf_ref = O.scan_xc_ref(xc_in, cf_ref, z, dt, Bm, Cm, A_log, Dp, si)
+    T = b * l
+    xz = t(np.concatenate([x, z], -1).reshape(T, 2 * es), dtype)
+    xct = t(xc_in.reshape(T, es), dtype)
+    dtt = t(dt.reshape(T, es), dtype)
+    bc = t(np.concatenate([Bm, Cm], -1).reshape(T, 2 * nst))
+    y = torch.empty(T, es, device=dev(), dtype=dtype)
+    cf = torch.empty(b, es, 3, device=dev(), dtype=dtype)
+    sf = torch.empty(b, es, nst, device=dev(), dtype=torch.float32)
+    args = [t(A_log, dtype), t(Dp, dtype), None if ci is None else t(ci, dtype), None if si is None else t(si)]
+    L.call("mtp_scan_prefill_xc", L.ptr(xct), es, L.ptr(xz), 2 * es, L.ptr(dtt), es, L.dtype_code(dtype), L.ptr(bc),
+           2 * nst, *[L.ptr(a) for a in args], L.ptr(y), es, L.ptr(cf), L.ptr(sf), b, l, es, nst, 4,
+           L.dtype_code(dtype), L.stream_ptr())
+    torch.cuda.synchronize()
+    tol = 2e-4 if dtype == torch.float32 else 2e-2
+    np.testing.assert_allclose(n(y).reshape(b, l, es), y_ref, atol=tol, rtol=tol)
+    np.testing.assert_allclose(n(cf), rnd(cf_ref), atol=0, rtol=0)
+    np.testing.assert_allclose(n(sf), sf_ref, atol=tol, rtol=tol)
+
+
+def test_scan_prefill_xc_in_place_history():
+    """Chunked prefill passes the cache's conv history as both conv_init and
+    conv_final (and the ssm state likewise): results equal the out-of-place call."""
+    b, l, es, nst = 2, 2, 64, 16  # L < K-1: part of the new history comes from the old one
+    x, z, dt, Bm, Cm, A_log, Dp, cw, cb, ci, si = _ssm_inputs(b, l, es, nst, 8, BF)
+    xc_in = O.bf16_round(O.conv_silu_ref(x, cw, cb, ci)[0])
+    T = b * l
+    xz = t(np.concatenate([x, z], -1).reshape(T, 2 * es), BF)
+    xct, dtt = t(xc_in.reshape(T, es), BF), t(O.bf16_round(dt).reshape(T, es), BF)
+    bc = t(np.concatenate([Bm, Cm], -1).reshape(T, 2 * nst))
+    A_t, D_t = t(A_log, BF), t(Dp, BF)
+    outs = []
+    for in_place in (False, True):
+        ci_t, si_t = t(ci, BF), t(si)
+        cf = ci_t if in_place else torch.empty_like(ci_t)
+        sf = si_t if in_place else torch.empty_like(si_t)
+        y = torch.empty(T, es, device=dev(), dtype=BF)
+        L.call("mtp_scan_prefill_xc", L.ptr(xct), es, L.ptr(xz), 2 * es, L.ptr(dtt), es, L.BF16, L.ptr(bc), 2 * nst,
+               L.ptr(A_t), L.ptr(D_t), L.ptr(ci_t), L.ptr(si_t), L.ptr(y), es, L.ptr(cf), L.ptr(sf), b, l, es, nst, 4,
+               L.BF16, L.stream_ptr())
+        torch.cuda.synchronize()
+        outs.append((n(y), n(cf), n(sf)))
+    for a, c in zip(*outs):
+        np.testing.assert_array_equal(a, c)
+    np.testing.assert_array_equal(outs[0][1], O.bf16_round(O.final_conv_history(x, ci)))
+
+
+def test_exp2_fma_error_bound():
+    """The FP32-pipe 2^x used for part of the scan's state decays: relative error within
+    2.5e-7 of the exact value on [-125, 0] (the hardware ex2.approx.f32 is specified to
+    about 2 ulp, 2.4e-7), and 2^-125 below -125."""
+    xs = np.concatenate([np.linspace(-125.0, 0.0, 1 << 21, dtype=np.float32),
+                         -np.logspace(-8, 0, 4096, dtype=np.float32), np.float32([0.0, -0.5, -0.5000001, -124.5])])
+    xt = t(xs)
+    out = torch.empty_like(xt)
+    L.call("mtp_exp2_fma", L.ptr(xt), L.ptr(out), xs.size, L.stream_ptr())
+    torch.cuda.synchronize()
+    got = n(out).astype(np.float64)
+    want = np.exp2(xs.astype(np.float64))
+    rel = np.abs(got - want) / want
+    assert rel.max() <= 2.5e-7, f"max relative error {rel.max():.3e} at x={xs[rel.argmax()]}"
+    low = t(np.float32([-126.0, -300.0, -1e30]))
+    lo_out = torch.empty_like(low)
+    L.call("mtp_exp2_fma", L.ptr(low), L.ptr(lo_out), 3, L.stream_ptr())
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(n(lo_out), np.float32(2.0 ** -125), rtol=3e-7)
+
+
 @pytest.mark.parametrize("b,l,es,R,init", [(2, 37, 128, 48, True), (3, 70, 256, 128, True), (1, 16, 384, 160, False),
                                           (2, 5, 128, 64, True), (4, 129, 512, 256, True)])
 def test_fused_dt_scan_matches_oracle(b, l, es, R, init):
@@ -241,7 +332,8 @@ def test_dequant_sum_bit_exact_on_reference_payloads(golden_dir, ws):
 
 
 @pytest.mark.parametrize("mode,name", [(L.RED_FP32, "fp32"), (L.RED_FP16, "fp16"), (L.RED_INT8TOK, "int8")])
-@pytest.mark.parametrize("rows,cols", [(1, 160), (37, 80), (5000, 2048), (9, 18)])
+@pytest.mark.parametrize("rows,cols", [(1, 160), (37, 80), (5000, 2048), (9, 18), (33, 768), (300, 2560), (17, 3072),
+                                       (64, 1000)])
 def test_allreduce_world_size_one_round_trip(mode, name, rows, cols):
     """At world size 1 the reference still round-trips through the wire format."""
     x = _rand((rows, cols), 31, 3.0)
@@ -252,8 +344,10 @@ def test_allreduce_world_size_one_round_trip(mode, name, rows, cols):
     assert n(out).tobytes() == ref.astype(np.float32).tobytes()
 
 
-def test_reduce_outproj_epilogue_matches_oracle():
-    rows, d = 77, 768
+@pytest.mark.parametrize("d", [768, 1000, 2048, 2560])
+def test_reduce_outproj_epilogue_matches_oracle(d):
+    """16-column-granule rows (d % 16 == 0, d >= 512) and the register-row kernel (1000)."""
+    rows = 77
     part = _rand((rows, d), 41)
     resid = _rand((rows, d), 42)
     w = _rand((d,), 43) + 1

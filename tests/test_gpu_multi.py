@@ -1,10 +1,21 @@
-"""Multi-GPU tests (one process per GPU, NCCL process group for the
-bootstrap): the peer-memory reductions are bit-exact against the oracle in
-every wire mode and protocol, the TP model matches the oracle's TP emulation
-with identical results on every rank, graphed TP decode equals eager decode,
-and a reduction whose peer never arrives ends with a timeout status (bounded
-wait) instead of hanging.  Skipped on boxes with fewer than 2 GPUs."""
+"""Multi-GPU tests (one process per GPU, NCCL process group for the bootstrap), at
+world sizes 2, 4 and 8 (each skipped when the box has fewer GPUs):
+
+* the peer-memory reductions are bit-exact against the oracle in every wire mode and
+  both protocols, including the [32768, 2048] int8 out_proj site of the 1.4b bench
+  (two-shot at 4 and 8 ranks) with 1% outlier channels, and every rank holds the
+  same bytes (the reference's cross-rank bit identity, tests/test_per_site_allreduce.py);
+* the TP model matches the oracle's TP emulation at the same world size with identical
+  results on every rank, graphed decode equals eager decode bitwise, and the persistent
+  decode kernel agrees with the per-layer chain;
+* the out_proj epilogue gives the same bits through one-shot, two-shot and capped grids,
+  and the overlapped micro-batch prefill equals the serial prefill bitwise.
+
+One spawn per world size runs every check (``_suite``); large results travel back as
+SHA-256 digests.  Two more tests, at 2 GPUs, make a reduction and a decode step wait
+for a peer that never arrives and check the timeout status (bounded waits)."""
 import datetime
+import hashlib
 import os
 import tempfile
 
@@ -13,18 +24,24 @@ import pytest
 import torch
 
 pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
-WS = 2
-
-needs2 = pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < WS,
-                            reason="needs 2 GPUs")
+WS_LIST = (2, 4, 8)
+BIG = (32768, 2048)  # the 1.4b out_proj site of a 32 x 1024 prefill
 
 
-def _init(rank, init_file):
+def _ngpu():
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+def needs(ws):
+    return pytest.mark.skipif(_ngpu() < ws, reason=f"needs {ws} GPUs")
+
+
+def _init(rank, init_file, ws):
     import torch.distributed as dist
 
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", init_method=f"file://{init_file}", rank=rank, world_size=WS,
+    dist.init_process_group("nccl", init_method=f"file://{init_file}", rank=rank, world_size=ws,
                             timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", rank))
 
 
@@ -40,156 +57,257 @@ def _finish():
     dist.destroy_process_group()
 
 
-def _spawn(fn, *args, timeout=300):
+def _spawn(fn, ws, *args, timeout=600):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     with tempfile.TemporaryDirectory() as d:
-        procs = [ctx.Process(target=fn, args=(r, os.path.join(d, "rdv"), q) + args) for r in range(WS)]
+        procs = [ctx.Process(target=fn, args=(r, os.path.join(d, "rdv"), q, ws) + args) for r in range(ws)]
         for p in procs:
             p.start()
         try:
-            res = dict(q.get(timeout=timeout) for _ in range(WS))
+            res = dict(q.get(timeout=timeout) for _ in range(ws))
         finally:
             for p in procs:
                 p.join(timeout=60)
                 if p.is_alive():
                     p.kill()
-    for r in range(WS):
+    for r in range(ws):
         if isinstance(res[r], str):
             raise AssertionError(f"rank {r}: {res[r]}")
     return res
 
 
-# ------------------------------------------------------------------ raw reductions
-def _allreduce_worker(rank, init_file, q, protocol):
+def _digest(a: np.ndarray) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a, dtype=np.float32).tobytes()).hexdigest()
+
+
+def _partial(rank, rows, cols, outliers=False):
+    """The seeded partial of one rank: N(0, 3^2); with outliers, a fixed 1% of the
+    columns scaled by 20 (the activation model of the collective microbench)."""
+    x = torch.randn(rows, cols, generator=torch.Generator().manual_seed(1000 * rank + rows)) * 3
+    if outliers:
+        idx = torch.randperm(cols, generator=torch.Generator().manual_seed(77))[:max(1, cols // 100)]
+        x[:, idx] *= 20
+    return x
+
+
+RED_CASES = ((1, 160), (33, 2048), (4096, 768), (20000, 2048), (7, 18))
+
+
+# ------------------------------------------------------------------ one spawn per world size
+def _suite(rank, init_file, q, ws):
     try:
-        if protocol:
-            os.environ["MTP_COMM_PROTOCOL"] = protocol
-        _init(rank, init_file)
+        _init(rank, init_file, ws)
         from mamba_tp_lite_b200 import _lib as L
-        from mamba_tp_lite_b200.tp_utils import get_comm
-
-        out = {}
-        for rows, cols in ((1, 160), (33, 2048), (4096, 768), (20000, 2048), (7, 18)):
-            comm = get_comm(None, rank, WS, cols, cols)
-            xs = [torch.randn(rows, cols, generator=torch.Generator().manual_seed(1000 * r + rows)) * 3 for r in range(WS)]
-            x = xs[rank].cuda()
-            for mode in (L.RED_FP32, L.RED_FP16, L.RED_INT8TOK):
-                y = torch.empty_like(x)
-                for _ in range(2):  # back-to-back calls on one site
-                    L.call("mtp_allreduce", comm.ptr, 1, mode, L.ptr(x), L.ptr(y), rows, cols, L.stream_ptr())
-                torch.cuda.synchronize()
-                out[(rows, cols, mode)] = y.cpu().numpy()
-            comm.check()
-        q.put((rank, out))
-        _finish()
-    except Exception as e:  # report instead of hanging the parent
-        q.put((rank, f"{type(e).__name__}: {e}"))
-
-
-@needs2
-@pytest.mark.parametrize("protocol", [None, "twoshot"])
-def test_peer_reductions_bit_exact_vs_oracle(protocol):
-    from mamba_tp_lite_b200 import _lib as L
-    from oracle import mamba_oracle as O
-
-    res = _spawn(_allreduce_worker, protocol)
-    names = {L.RED_FP32: "fp32", L.RED_FP16: "fp16", L.RED_INT8TOK: "int8"}
-    for (rows, cols, mode), got in res[0].items():
-        xs = [(torch.randn(rows, cols, generator=torch.Generator().manual_seed(1000 * r + rows)) * 3).numpy()
-              for r in range(WS)]
-        want = O.REDUCE_FNS[names[mode]](xs)
-        assert got.tobytes() == want.astype(np.float32).tobytes(), (rows, cols, names[mode])
-        assert np.array_equal(res[1][(rows, cols, mode)], got)  # every rank identical
-
-
-# ------------------------------------------------------------------ TP model
-def _tp_model_worker(rank, init_file, q, dtype_name):
-    try:
-        _init(rank, init_file)
         from mamba_tp_lite_b200.checkpoint import random_init_state_dict
         from mamba_tp_lite_b200.config import MambaConfig
         from mamba_tp_lite_b200.cuda_graph import GraphedStepper
         from mamba_tp_lite_b200.tp_model import TPMambaLM
+        from mamba_tp_lite_b200.tp_utils import build_spec, get_comm
 
-        dtype = getattr(torch, dtype_name)
+        out = {"reduce": {}, "model": {}, "proto": {}, "overlap": {}}
+        # ---- raw reductions: every mode, default and forced two-shot protocol
+        for protocol in (None, "twoshot"):
+            if protocol:
+                os.environ["MTP_COMM_PROTOCOL"] = protocol
+            cases = RED_CASES + ((BIG[0], BIG[1], True),)
+            for case in cases:
+                rows, cols = case[:2]
+                big = len(case) == 3
+                comm = get_comm(None, rank, ws, cols, cols)
+                x = _partial(rank, rows, cols, outliers=big).cuda()
+                for mode in ((L.RED_INT8TOK,) if big else (L.RED_FP32, L.RED_FP16, L.RED_INT8TOK)):
+                    y = torch.empty_like(x)
+                    for _ in range(2):  # back-to-back calls on one site
+                        L.call("mtp_allreduce", comm.ptr, 1, mode, L.ptr(x), L.ptr(y), rows, cols, L.stream_ptr())
+                    torch.cuda.synchronize()
+                    out["reduce"][(protocol, rows, cols, mode)] = _digest(y.cpu().numpy())
+                comm.check()
+                del x, y
+            os.environ.pop("MTP_COMM_PROTOCOL", None)
+        torch.cuda.empty_cache()
+        # ---- TP model: fp32 and bf16, three wire maps, eager / graphed / per-layer chain decode
         cfg = MambaConfig(d_model=256, n_layer=3, vocab_size=1000, dt_rank=16)
-        sd = random_init_state_dict(cfg, seed=3, dtype=dtype)
         ids = torch.randint(0, cfg.vocab_size, (2, 72), generator=torch.Generator().manual_seed(4))
-        out = {}
-        for spec in ("fp32", "fp16", "int8"):
-            m = TPMambaLM.from_state_dict_shard(cfg, sd, rank, WS, dtype=dtype, allreduce_dtype=spec, device="cuda")
-            logits, cache = m.prefill(ids.cuda())
-            nxt = torch.zeros(2, 1, dtype=torch.long, device="cuda")
-            eager = [m.step(nxt, cache).clone() for _ in range(3)]
-            _, cg = m.prefill(ids.cuda())
-            st = GraphedStepper(m, cg, 2, "cuda")
-            st.capture()
-            graphed = [st.replay(nxt).clone() for _ in range(3)]
-            st.release()
-            count = m.layers[0].mixer.comm.count
-            # the same steps through the per-layer kernel chain (bf16: the persistent decode
-            # kernel ran above; both ranks switch paths together)
-            os.environ["MTP_DECODE_FUSED"] = "0"
-            _, cc = m.prefill(ids.cuda())
-            chain = [m.step(nxt, cc).float().cpu().numpy() for _ in range(3)]
-            os.environ.pop("MTP_DECODE_FUSED")
-            out[spec] = (logits.float().cpu().numpy(), [e.float().cpu().numpy() for e in eager],
-                         all(torch.equal(a, b) for a, b in zip(eager, graphed)), count, chain,
-                         getattr(m, "_mtp_decode", None) is not None)
+        for dtype in (torch.float32, torch.bfloat16):
+            sd = random_init_state_dict(cfg, seed=3, dtype=dtype)
+            for spec in ("fp32", "fp16", "int8"):
+                m = TPMambaLM.from_state_dict_shard(cfg, sd, rank, ws, dtype=dtype, allreduce_dtype=spec,
+                                                    device="cuda")
+                logits, cache = m.prefill(ids.cuda())
+                nxt = torch.zeros(2, 1, dtype=torch.long, device="cuda")
+                eager = [m.step(nxt, cache).clone() for _ in range(3)]
+                _, cg = m.prefill(ids.cuda())
+                st = GraphedStepper(m, cg, 2, "cuda")
+                st.capture()
+                graphed = [st.replay(nxt).clone() for _ in range(3)]
+                st.release()
+                count = m.layers[0].mixer.comm.count
+                os.environ["MTP_DECODE_FUSED"] = "0"  # the same steps through the per-layer chain
+                _, cc = m.prefill(ids.cuda())
+                chain = [m.step(nxt, cc).float().cpu().numpy() for _ in range(3)]
+                os.environ.pop("MTP_DECODE_FUSED")
+                out["model"][(str(dtype), spec)] = (
+                    logits.float().cpu().numpy(), [e.float().cpu().numpy() for e in eager],
+                    all(torch.equal(a, b) for a, b in zip(eager, graphed)), count, chain,
+                    getattr(m, "_mtp_decode", None) is not None)
+                del m
+        # ---- out_proj epilogue through one-shot, two-shot and a capped grid
+        rows, d = 3000, 1024
+        comm = get_comm(None, rank, ws, 48, d)
+        part = torch.randn(rows, d, generator=torch.Generator().manual_seed(7 + rank)).cuda() * 2
+        w = torch.randn(d, generator=torch.Generator().manual_seed(9)).cuda().to(torch.bfloat16)
+        for proto in ("oneshot", "twoshot", "capped"):
+            os.environ["MTP_COMM_PROTOCOL"] = "oneshot" if proto == "capped" else proto
+            comm.set_max_ctas(16 if proto == "capped" else 0)
+            for mode in (L.RED_FP32, L.RED_FP16, L.RED_INT8TOK):
+                resid = torch.ones(rows, d, device="cuda")
+                normed = torch.empty(rows, d, device="cuda", dtype=torch.bfloat16)
+                L.call("mtp_reduce_outproj", comm.ptr, mode, L.ptr(part), rows, d, None, L.ptr(resid), L.ptr(w),
+                       1e-5, L.ptr(normed), L.BF16, L.stream_ptr())
+                torch.cuda.synchronize()
+                out["proto"][(proto, mode)] = (_digest(resid.cpu().numpy()), _digest(normed.float().cpu().numpy()))
+        comm.set_max_ctas(0)
+        os.environ.pop("MTP_COMM_PROTOCOL")
+        comm.check()
+        # ---- overlapped micro-batch prefill == serial prefill
+        sd = random_init_state_dict(cfg, seed=8, dtype=torch.bfloat16)
+        spec = build_spec({"default": "int8", "overrides": {"0:out_proj": "fp16", "1:x_proj": "fp32"}}, cfg.n_layer)
+        m = TPMambaLM.from_state_dict_shard(cfg, sd, rank, ws, dtype=torch.bfloat16, allreduce_dtype=spec,
+                                            device="cuda")
+        ids2 = torch.randint(0, cfg.vocab_size, (5, 520), generator=torch.Generator().manual_seed(9)).cuda()
+        for mode in ("1", "0"):
+            os.environ["MTP_PREFILL_OVERLAP"] = mode
+            c0 = m.layers[0].mixer.comm.count
+            lg, cache = m.prefill(ids2)
+            lg2, _ = m.prefill(ids2[:, :7], cache)  # chunked continuation from the overlapped cache
+            out["overlap"][mode] = (lg.float().cpu().numpy(), lg2.float().cpu().numpy(),
+                                    [(lc.conv_state.float().cpu().numpy(), lc.ssm_state.cpu().numpy())
+                                     for lc in cache.layers], m.layers[0].mixer.comm.count - c0)
+        os.environ.pop("MTP_PREFILL_OVERLAP")
         q.put((rank, out))
         _finish()
-    except Exception as e:
-        q.put((rank, f"{type(e).__name__}: {e}"))
+    except Exception as e:  # report instead of hanging the parent
+        import traceback
+
+        q.put((rank, f"{type(e).__name__}: {e}\n{traceback.format_exc()}"))
 
 
-@needs2
+_RESULTS = {}
+
+
+def suite(ws):
+    if ws not in _RESULTS:
+        _RESULTS[ws] = _spawn(_suite, ws)
+    return _RESULTS[ws]
+
+
+# ------------------------------------------------------------------ raw reductions
+@pytest.mark.parametrize("ws", WS_LIST)
+def test_peer_reductions_bit_exact_vs_oracle(ws):
+    if _ngpu() < ws:
+        pytest.skip(f"needs {ws} GPUs")
+    from mamba_tp_lite_b200 import _lib as L
+    from oracle import mamba_oracle as O
+
+    res = suite(ws)
+    names = {L.RED_FP32: "fp32", L.RED_FP16: "fp16", L.RED_INT8TOK: "int8"}
+    want_cache = {}
+    for (protocol, rows, cols, mode), got in res[0]["reduce"].items():
+        key = (rows, cols, mode)
+        if key not in want_cache:
+            big = (rows, cols) == BIG
+            xs = [_partial(r, rows, cols, outliers=big).numpy() for r in range(ws)]
+            want_cache[key] = _digest(O.REDUCE_FNS[names[mode]](xs))
+            del xs
+        assert got == want_cache[key], (protocol, rows, cols, names[mode])
+        for r in range(1, ws):  # every rank holds the same bytes
+            assert res[r]["reduce"][(protocol, rows, cols, mode)] == got, (r, protocol, rows, cols)
+
+
+# ------------------------------------------------------------------ TP model
+@pytest.mark.parametrize("ws", WS_LIST)
 @pytest.mark.parametrize("dtype_name", ["float32", "bfloat16"])
-def test_tp2_model_matches_oracle_and_ranks_agree(dtype_name):
+def test_tp_model_matches_oracle_and_ranks_agree(ws, dtype_name):
+    if _ngpu() < ws:
+        pytest.skip(f"needs {ws} GPUs")
     from mamba_tp_lite_b200.checkpoint import random_init_state_dict
     from mamba_tp_lite_b200.config import MambaConfig
     from oracle import mamba_oracle as O
 
-    res = _spawn(_tp_model_worker, dtype_name)
+    res = suite(ws)
+    dtype = getattr(torch, dtype_name)
     cfg = MambaConfig(d_model=256, n_layer=3, vocab_size=1000, dt_rank=16)
-    sd = random_init_state_dict(cfg, seed=3, dtype=getattr(torch, dtype_name))
+    sd = random_init_state_dict(cfg, seed=3, dtype=dtype)
     ids = torch.randint(0, cfg.vocab_size, (2, 72), generator=torch.Generator().manual_seed(4)).numpy()
     for spec in ("fp32", "fp16", "int8"):
-        lg0, st0, graph_ok, count, chain0, fused = res[0][spec]
-        lg1, st1, _, _, chain1, _ = res[1][spec]
+        lg0, st0, graph_ok, count, chain0, fused = res[0]["model"][(str(dtype), spec)]
         assert fused == (dtype_name == "bfloat16"), spec   # bf16 steps ran the persistent decode kernel
-        assert all(np.array_equal(a, b) for a, b in zip(chain0, chain1)), spec
+        for r in range(1, ws):                              # identical on every rank
+            lgr, str_, _, _, chainr, _ = res[r]["model"][(str(dtype), spec)]
+            assert np.array_equal(lg0, lgr), (spec, r)
+            assert all(np.array_equal(a, b) for a, b in zip(st0, str_)), (spec, r)
+            assert all(np.array_equal(a, b) for a, b in zip(chain0, chainr)), (spec, r)
         for a, c in zip(st0, chain0):                      # fused == chain up to accumulation order
             assert np.abs(a - c).max() <= 2e-2 * np.abs(c).max(), spec
-        assert np.array_equal(lg0, lg1), spec          # identical on every rank
-        assert all(np.array_equal(a, b) for a, b in zip(st0, st1)), spec
-        assert graph_ok, spec                          # graph replay == eager, bitwise
+        assert graph_ok, spec                              # graph replay == eager, bitwise
         # host-side count, as the reference's CommCounter: 2 per prefill (x2), 2 per eager step (3),
         # 2 per graph warm-up step (3) and 2 for the captured step; replays are not counted
         assert count == 2 * 2 + 2 * 3 + 2 * 3 + 2, count
         lm = O.OracleLM(O.Cfg(cfg.d_model, cfg.n_layer, cfg.vocab_size, dt_rank=cfg.dt_rank),
-                        O.state_dict_numpy(sd), world_size=WS, spec=spec)
+                        O.state_dict_numpy(sd), world_size=ws, spec=spec)
         ref, _ = lm.prefill(ids)
         if dtype_name == "float32":
             tol = {"fp32": 2e-4, "fp16": 2e-3}.get(spec, 2e-2)
             np.testing.assert_allclose(lg0, ref, atol=tol, rtol=1e-3)
+            assert np.array_equal(lg0.argmax(-1), ref.argmax(-1)) or spec != "fp32"  # greedy tokens identical
         else:
             met = O.quant_metrics(ref, lg0)
             assert met["kl"].mean() <= 2e-3 and met["top1"].mean() >= 0.95, (spec, met)
 
 
+# ------------------------------------------------------------------ protocols agree (out_proj epilogue, bf16 gather)
+@pytest.mark.parametrize("ws", WS_LIST)
+def test_two_shot_bf16_gather_equals_one_shot(ws):
+    if _ngpu() < ws:
+        pytest.skip(f"needs {ws} GPUs")
+    res = suite(ws)
+    for mode in (0, 1, 2):
+        a = res[0]["proto"][("oneshot", mode)]
+        assert res[0]["proto"][("twoshot", mode)] == a, mode
+        assert res[0]["proto"][("capped", mode)] == a, mode  # 16 CTAs, low-register kernel: same bits
+        for r in range(1, ws):
+            for proto in ("oneshot", "twoshot", "capped"):
+                assert res[r]["proto"][(proto, mode)] == a, (r, proto, mode)
+
+
+# ------------------------------------------------------------------ overlapped micro-batch prefill == serial prefill
+@pytest.mark.parametrize("ws", WS_LIST)
+def test_overlapped_prefill_bit_exact_vs_serial(ws):
+    if _ngpu() < ws:
+        pytest.skip(f"needs {ws} GPUs")
+    res = suite(ws)
+    for r in range(ws):
+        a, b = res[r]["overlap"]["1"], res[r]["overlap"]["0"]
+        assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+        for (c1, s1), (c2, s2) in zip(a[2], b[2]):
+            assert np.array_equal(c1, c2) and np.array_equal(s1, s2)
+        assert a[3] == b[3] == 2 * 2  # the reference's accounting: 2 sites, 2 prefills
+        assert np.array_equal(res[0]["overlap"]["1"][0], a[0])
+
+
 # ------------------------------------------------------------------ bounded wait: a peer that never arrives
-def _timeout_worker(rank, init_file, q):
+def _timeout_worker(rank, init_file, q, ws):
     try:
         import torch.distributed as dist
 
-        _init(rank, init_file)
+        _init(rank, init_file, ws)
         from mamba_tp_lite_b200 import _lib as L
         from mamba_tp_lite_b200.tp_utils import Comm
 
-        comm = Comm(None, rank, WS, 64, 64, max_rows=64, timeout_s=1.0)
+        comm = Comm(None, rank, ws, 64, 64, max_rows=64, timeout_s=1.0)
         x = torch.ones(8, 64, device="cuda")
         y = torch.empty_like(x)
         status = 0
@@ -210,24 +328,24 @@ def _timeout_worker(rank, init_file, q):
         q.put((rank, f"{type(e).__name__}: {e}"))
 
 
-@needs2
+@needs(2)
 def test_reduction_with_absent_peer_times_out_with_status():
     from mamba_tp_lite_b200 import _lib as L
 
-    res = _spawn(_timeout_worker)
+    res = _spawn(_timeout_worker, 2)
     assert res[0] == L.MTP_ERR_TIMEOUT
     assert res[1] == 0
 
 
 # ------------------------------------------------------------------ persistent decode: a peer that never steps
-def _decode_timeout_worker(rank, init_file, q):
+def _decode_timeout_worker(rank, init_file, q, ws):
     try:
         import time
 
         import torch.distributed as dist
 
         os.environ["MTP_COMM_TIMEOUT_S"] = "1"
-        _init(rank, init_file)
+        _init(rank, init_file, ws)
         from mamba_tp_lite_b200.checkpoint import random_init_state_dict
         from mamba_tp_lite_b200.config import MambaConfig
         from mamba_tp_lite_b200.tp_model import TPMambaLM
@@ -235,7 +353,7 @@ def _decode_timeout_worker(rank, init_file, q):
 
         cfg = MambaConfig(d_model=256, n_layer=2, vocab_size=512, dt_rank=16)
         sd = random_init_state_dict(cfg, seed=5, dtype=torch.bfloat16)
-        m = TPMambaLM.from_state_dict_shard(cfg, sd, rank, WS, dtype=torch.bfloat16, allreduce_dtype="int8",
+        m = TPMambaLM.from_state_dict_shard(cfg, sd, rank, ws, dtype=torch.bfloat16, allreduce_dtype="int8",
                                             device="cuda")
         ids = torch.randint(0, cfg.vocab_size, (2, 16), generator=torch.Generator().manual_seed(6)).cuda()
         _, cache = m.prefill(ids)  # both ranks: creates the comm context
@@ -244,7 +362,7 @@ def _decode_timeout_worker(rank, init_file, q):
         dist.barrier()
         result = (0, 0, 0.0)
         if rank == 0:  # rank 1 never steps: rank 0's AllReduce #1 wait must expire
-            comm = get_comm(None, rank, WS, cfg.dt_rank + 2 * cfg.d_state, cfg.d_model)
+            comm = get_comm(None, rank, ws, cfg.dt_rank + 2 * cfg.d_state, cfg.d_model)
             t0 = time.time()
             m.step(torch.zeros(2, 1, dtype=torch.long, device="cuda"), cache)
             torch.cuda.synchronize()
@@ -259,97 +377,12 @@ def _decode_timeout_worker(rank, init_file, q):
         q.put((rank, f"{type(e).__name__}: {e}"))
 
 
-@needs2
+@needs(2)
 def test_decode_kernel_with_absent_peer_times_out_with_status():
     from mamba_tp_lite_b200 import _lib as L
 
-    res = _spawn(_decode_timeout_worker)
+    res = _spawn(_decode_timeout_worker, 2)
     plan_status, comm_status, elapsed = res[0]
     assert plan_status == L.MTP_ERR_TIMEOUT and comm_status == L.MTP_ERR_TIMEOUT
     assert 0.5 < elapsed < 30
     assert res[1] == (0, 0, 0.0)
-
-
-# ------------------------------------------------------------------ protocols agree (out_proj epilogue, bf16 gather)
-def _protocol_worker(rank, init_file, q):
-    try:
-        _init(rank, init_file)
-        from mamba_tp_lite_b200 import _lib as L
-        from mamba_tp_lite_b200.tp_utils import get_comm
-
-        rows, d = 3000, 1024
-        comm = get_comm(None, rank, WS, 48, d)
-        part = torch.randn(rows, d, generator=torch.Generator().manual_seed(7 + rank)).cuda() * 2
-        w = torch.randn(d, generator=torch.Generator().manual_seed(9)).cuda().to(torch.bfloat16)
-        res = {}
-        for proto in ("oneshot", "twoshot", "capped"):
-            os.environ["MTP_COMM_PROTOCOL"] = "oneshot" if proto == "capped" else proto
-            comm.set_max_ctas(16 if proto == "capped" else 0)
-            for mode in (L.RED_FP32, L.RED_FP16, L.RED_INT8TOK):
-                resid = torch.ones(rows, d, device="cuda")
-                normed = torch.empty(rows, d, device="cuda", dtype=torch.bfloat16)
-                L.call("mtp_reduce_outproj", comm.ptr, mode, L.ptr(part), rows, d, None, L.ptr(resid), L.ptr(w),
-                       1e-5, L.ptr(normed), L.BF16, L.stream_ptr())
-                torch.cuda.synchronize()
-                res[(proto, mode)] = (resid.cpu().numpy(), normed.float().cpu().numpy())
-        comm.check()
-        q.put((rank, res))
-        _finish()
-    except Exception as e:
-        q.put((rank, f"{type(e).__name__}: {e}"))
-
-
-@needs2
-def test_two_shot_bf16_gather_equals_one_shot():
-    res = _spawn(_protocol_worker)
-    for mode in (0, 1, 2):
-        a, b = res[0][("oneshot", mode)], res[0][("twoshot", mode)]
-        assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1]), mode
-        assert np.array_equal(res[1][("twoshot", mode)][0], b[0])
-        c = res[0][("capped", mode)]  # 16 CTAs, low-register kernel: same bits
-        assert np.array_equal(a[0], c[0]) and np.array_equal(a[1], c[1]), mode
-
-
-# ------------------------------------------------------------------ overlapped micro-batch prefill == serial prefill
-def _overlap_worker(rank, init_file, q):
-    try:
-        _init(rank, init_file)
-        from mamba_tp_lite_b200.checkpoint import random_init_state_dict
-        from mamba_tp_lite_b200.config import MambaConfig
-        from mamba_tp_lite_b200.tp_model import TPMambaLM
-        from mamba_tp_lite_b200.tp_utils import build_spec
-
-        cfg = MambaConfig(d_model=256, n_layer=3, vocab_size=1000, dt_rank=16)
-        sd = random_init_state_dict(cfg, seed=8, dtype=torch.bfloat16)
-        spec = build_spec({"default": "int8", "overrides": {"0:out_proj": "fp16", "1:x_proj": "fp32"}}, cfg.n_layer)
-        m = TPMambaLM.from_state_dict_shard(cfg, sd, rank, WS, dtype=torch.bfloat16, allreduce_dtype=spec,
-                                            device="cuda")
-        ids = torch.randint(0, cfg.vocab_size, (5, 520), generator=torch.Generator().manual_seed(9)).cuda()
-        os.environ["MTP_PREFILL_OVERLAP"] = "1"
-        assert m._overlap_split(5, 520) is not None
-        out = {}
-        for mode in ("1", "0"):
-            os.environ["MTP_PREFILL_OVERLAP"] = mode
-            c0 = m.layers[0].mixer.comm.count
-            lg, cache = m.prefill(ids)
-            lg2, _ = m.prefill(ids[:, :7], cache)  # chunked continuation from the overlapped cache
-            out[mode] = (lg.float().cpu().numpy(), lg2.float().cpu().numpy(),
-                         [(lc.conv_state.float().cpu().numpy(), lc.ssm_state.cpu().numpy()) for lc in cache.layers],
-                         m.layers[0].mixer.comm.count - c0)
-        os.environ.pop("MTP_PREFILL_OVERLAP")
-        q.put((rank, out))
-        _finish()
-    except Exception as e:
-        q.put((rank, f"{type(e).__name__}: {e}"))
-
-
-@needs2
-def test_overlapped_prefill_bit_exact_vs_serial():
-    res = _spawn(_overlap_worker)
-    for r in range(WS):
-        a, b = res[r]["1"], res[r]["0"]
-        assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
-        for (c1, s1), (c2, s2) in zip(a[2], b[2]):
-            assert np.array_equal(c1, c2) and np.array_equal(s1, s2)
-        assert a[3] == b[3] == 2 * 2  # the reference's accounting: 2 sites, 2 prefills
-    assert np.array_equal(res[0]["1"][0], res[1]["1"][0])
