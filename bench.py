@@ -378,10 +378,31 @@ def run_ours(a):
 
     cfg = shape_config(a.shape)
     spec = build_spec(mixed_spec(cfg.n_layer), cfg.n_layer) if a.spec == "mixed" else a.spec
-    sd = random_init_state_dict(cfg, seed=0, dtype=torch.bfloat16, device="cuda")
-    model = TPMambaLM.from_state_dict_shard(cfg, sd, rank, ws, dtype=torch.bfloat16, allreduce_dtype=spec,
-                                            device="cuda")
-    del sd
+    load_note = "random-init state dict built on the GPU, this rank's slices copied"
+    if a.from_checkpoint:
+        # per-rank slicing from a checkpoint on disk: rank 0 writes
+        # it one layer per shard file, every rank reads only its own slices of each tensor
+        import shutil
+
+        from mamba_tp_lite_b200.checkpoint import write_random_checkpoint_by_layer
+
+        ckdir = os.path.join(tempfile.gettempdir(), f"mtp_bench_ckpt_{a.shape}_{os.environ.get('MASTER_PORT', '0')}")
+        if rank == 0:
+            write_random_checkpoint_by_layer(ckdir, cfg, seed=0, dtype=torch.bfloat16, device="cuda")
+        barrier()
+        model = TPMambaLM.from_pretrained_shard(ckdir, rank, ws, dtype=torch.bfloat16, allreduce_dtype=spec,
+                                                device="cuda")
+        torch.cuda.synchronize()
+        barrier()
+        if rank == 0:
+            shutil.rmtree(ckdir, ignore_errors=True)
+        load_note = ("checkpoint written one layer per safetensors shard; each rank read only its slices "
+                     "(from_pretrained_shard, safetensors get_slice)")
+    else:
+        sd = random_init_state_dict(cfg, seed=0, dtype=torch.bfloat16, device="cuda")
+        model = TPMambaLM.from_state_dict_shard(cfg, sd, rank, ws, dtype=torch.bfloat16, allreduce_dtype=spec,
+                                                device="cuda")
+        del sd
     torch.cuda.empty_cache()
     B, S = a.batch, a.seqlen
     g = torch.Generator(device="cuda").manual_seed(0)
@@ -453,6 +474,8 @@ def run_ours(a):
         per_kernel[name] = row
     other_ms = ms / a.steps - sum(v["total_ms"] for v in kern.values()) / a.steps
     per_kernel["untimed_rest"] = {"ms_per_step": other_ms, "share_of_step": other_ms * a.steps / ms}
+    # the reductions run between the compute kernels on one stream: all of their time is exposed
+    coll_ms = sum(kern[k]["total_ms"] for k in ("reduce_x", "reduce_out") if k in kern) / a.steps
 
     # ------------------------------------------------ end to end through the API, host ids
     host_ids = ids.cpu().pin_memory()
@@ -484,7 +507,10 @@ def run_ours(a):
         for plen in a.decode_prompts:
             row = {}
             for db in a.decode_batches:
-                prompt = ids[:db, :plen].contiguous()
+                if db <= B and plen <= S:
+                    prompt = ids[:db, :plen].contiguous()
+                else:  # more sequences (or positions) than the prefill batch holds
+                    prompt = torch.randint(0, cfg.vocab_size, (db, plen), device="cuda", generator=g)
                 _, cache = model.prefill(prompt)
                 st = GraphedStepper(model, cache, db, "cuda")
                 st.capture()
@@ -537,7 +563,8 @@ def run_ours(a):
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": a.steps, "warmup": a.warmup,
         "ms_per_step": ms / a.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic (seeded random-init weights, uniform random token ids)",
-        "config": {"workload": f"mamba-{a.shape}-shaped TP prefill {B}x{S} + graphed decode", "shape": a.shape,
+        "collectives_ms_per_step": coll_ms, "model_load": load_note,
+        "config": {"workload": f"{a.label}mamba-{a.shape}-shaped TP prefill {B}x{S} + graphed decode", "shape": a.shape,
                    "global_batch": B, "seq_len": S, "tp": ws, "parallelism": f"tp{ws}",
                    "precision_map": a.spec if a.spec != "mixed" else
                    "int8-per-token, out_proj of layers 0 and last 4 in fp16",
@@ -576,7 +603,17 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-tokens", type=int, default=1024)
     ap.add_argument("--ref-layers", type=int, default=4)
+    ap.add_argument("--config5", action="store_true",
+                    help="BASELINE configuration 5: 2.8b shape, prefill 8 x 8192, every site int8, 512 graphed "
+                         "decode steps at batch 64, weights sliced per rank from a checkpoint on disk")
+    ap.add_argument("--from-checkpoint", action="store_true", help="load through from_pretrained_shard")
     a = ap.parse_args()
+    a.label = ""
+    if a.config5:
+        a.shape, a.batch, a.seqlen, a.spec = "2.8b", 8, 8192, "int8"
+        a.decode_batches, a.decode_steps, a.decode_prompts = [64], 512, [64]
+        a.from_checkpoint, a.no_accuracy = True, True
+        a.label = "configuration 5: "
     if a.warmup < 3 and a.impl == "ours":
         print("note: fewer than 3 warm-up steps", file=sys.stderr)
     if a.impl == "reference":

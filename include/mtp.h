@@ -15,6 +15,10 @@
  * package's GraphedStepper runs warm-up steps first).  No torch types appear
  * here; the Python package binds this header with ctypes.
  *
+ * Devices: the library serves one device per process (one rank per process), except
+ * the allocation-free reduction scratch and the reductions' row scratch, which are kept
+ * per device; the status words of the GEMM and of the fused scan are per process.
+ *
  * Layout conventions: matrices are row-major; a "token row" is one position
  * of one sequence, tokens ordered (batch, position).  Element type codes are
  * MTP_F32 / MTP_BF16 / MTP_F16.
@@ -191,6 +195,12 @@ int mtp_comm_destroy(mtp_comm *c);
  * after a synchronize; a timed-out reduction leaves its outputs undefined). */
 int mtp_comm_status(mtp_comm *c, int *status);
 int mtp_comm_reset_status(mtp_comm *c);
+/* Recovery after MTP_ERR_TIMEOUT: zeroes the context's flags, epochs, exit counters and
+ * status word.  A timed-out reduction or decode step leaves flags and epochs that no longer
+ * agree across ranks, so with no kernel in flight on any rank, every rank calls this (and
+ * mtp_decode_reset on its decode plan), then the ranks meet at a host barrier before the
+ * next reduction or step. */
+int mtp_comm_reset_state(mtp_comm *c);
 /* Launch shape of the context's reductions: max_ctas > 0 caps a reduction's grid at
  * max_ctas CTAs and selects the low-register kernel variant, so a reduction can run
  * on the SMs beside a GEMM or scan of another stream (compute/communication overlap
@@ -203,6 +213,14 @@ int mtp_comm_set_max_ctas(mtp_comm *c, int max_ctas);
  * reduce calls choose (0 without a context or at world size 1).  For bandwidth reports;
  * the reference counts payload bytes per call at tp_utils.py:24-26, :38-40, :114-116. */
 int mtp_comm_sent_bytes(mtp_comm *c, int mode, int rows, int cols, int rdt, double *bytes);
+
+/* Phase trace of the pipelined reductions on this context (diagnostics; off by default).
+ * records > 0 allocates a ring of that many launch records of 131 uint64 each: [0] grid
+ * size, [1] rounds, [2] 1 for the two-shot protocol, then from [3] (CTA 0) and [67] (the
+ * last CTA) the %globaltimer ns at start and after each push / wait / reduce / signal
+ * step of each round; 0 frees it.  Not allowed while a reduction is in flight. */
+int mtp_comm_set_trace(mtp_comm *c, int records);
+int mtp_comm_read_trace(mtp_comm *c, uint64_t *out, int capacity, int *n_records);
 
 /* AllReduce #1 epilogue (tp_model.py:106-108, :159-161): sum the fp32
  * partial [rows, R+2N] over ranks in `mode`, round the sums to dt_dtype (the
@@ -278,7 +296,8 @@ int mtp_decode_bind_cache(mtp_decode_plan *plan, void *const *conv_state, float 
 int mtp_decode_step(mtp_decode_plan *plan, mtp_decode_cache *cache, const int64_t *ids, void *normed, void *stream);
 /* MTP_OK, or MTP_ERR_TIMEOUT after a barrier or peer wait gave up (synchronous read). */
 int mtp_decode_status(mtp_decode_plan *plan, int *status);
-/* Clears the barrier, abort and status words after a timeout. */
+/* Clears the barrier, abort, status and per-row flag words after a timeout (synchronous).
+ * The comm context needs mtp_comm_reset_state on every rank as well before the next step. */
 int mtp_decode_reset(mtp_decode_plan *plan);
 /* Phase timing of later steps (off by default): with tracing on, each step stores
  * nb = 2 + 5 n_layer %globaltimer stamps of CTA 0: out[0] = start, out[1] = end of

@@ -50,7 +50,10 @@ _SIGS = {
     "mtp_comm_destroy": [_vp],
     "mtp_comm_status": [_vp, C.POINTER(_i)],
     "mtp_comm_reset_status": [_vp],
+    "mtp_comm_reset_state": [_vp],
     "mtp_comm_set_max_ctas": [_vp, _i],
+    "mtp_comm_set_trace": [_vp, _i],
+    "mtp_comm_read_trace": [_vp, C.POINTER(_u64), _i, C.POINTER(_i)],
     "mtp_comm_sent_bytes": [_vp, _i, _i, _i, _i, C.POINTER(_d)],
     "mtp_reduce_xproj": [_vp, _i, _vp, _i, _i, _i, _vp, _i, _vp, _vp],
     "mtp_reduce_outproj": [_vp, _i, _vp, _i, _i, _vp, _vp, _vp, _f, _vp, _i, _vp],

@@ -35,15 +35,13 @@ def _shapes(cfg: MambaConfig):
     return e, d, n, r, k
 
 
-def random_init_state_dict(cfg: MambaConfig, seed: int = 0, dtype=torch.float32,
-                           device="cpu", layers=None) -> dict[str, torch.Tensor]:
-    """Returns the HF-named state dict.  Values are drawn in float32 from a
-    generator on ``device`` (CPU draws are reproducible across machines) and
-    then cast to ``dtype``.  ``layers`` restricts which layers are returned
-    (the generator still advances over the skipped ones, so values match)."""
+def _random_init_groups(cfg: MambaConfig, seed: int, dtype, device, layers=None):
+    """Yields (group, {name: tensor}) in draw order: ("embeddings", ...), then
+    ("layer i", ...) for each layer, then ("norm_f", ...).  Values are drawn in
+    float32 from a generator on ``device`` (CPU draws are reproducible across machines)
+    and cast to ``dtype``; skipped layers still advance the generator."""
     g = torch.Generator(device=device).manual_seed(seed)
     e, d, n, r, k = _shapes(cfg)
-    sd: dict[str, torch.Tensor] = {}
 
     def normal(*shape):
         return torch.randn(*shape, generator=g, device=device, dtype=torch.float32) * 0.02
@@ -51,7 +49,7 @@ def random_init_state_dict(cfg: MambaConfig, seed: int = 0, dtype=torch.float32,
     def uniform(bound, *shape):
         return (torch.rand(*shape, generator=g, device=device, dtype=torch.float32) * 2 - 1) * bound
 
-    sd["backbone.embeddings.weight"] = normal(cfg.vocab_size, d).to(dtype)
+    yield "embeddings", {"backbone.embeddings.weight": normal(cfg.vocab_size, d).to(dtype)}
     kb = 1.0 / math.sqrt(k)
     for i in range(cfg.n_layer):
         p = f"backbone.layers.{i}."
@@ -76,10 +74,48 @@ def random_init_state_dict(cfg: MambaConfig, seed: int = 0, dtype=torch.float32,
         t["mixer.A_log"] = torch.log(a).contiguous()
         t["mixer.D"] = torch.ones(e, device=device)
         t["norm.weight"] = torch.ones(d, device=device)
-        for kk, v in t.items():
-            sd[p + kk] = v.to(dtype)
-    sd["backbone.norm_f.weight"] = torch.ones(d, device=device, dtype=dtype)
+        yield f"layer {i}", {p + kk: v.to(dtype) for kk, v in t.items()}
+    yield "norm_f", {"backbone.norm_f.weight": torch.ones(d, device=device, dtype=dtype)}
+
+
+def random_init_state_dict(cfg: MambaConfig, seed: int = 0, dtype=torch.float32,
+                           device="cpu", layers=None) -> dict[str, torch.Tensor]:
+    """Returns the HF-named state dict (all groups of _random_init_groups).  ``layers``
+    restricts which layers are returned (values match the full draw)."""
+    sd: dict[str, torch.Tensor] = {}
+    for _, tensors in _random_init_groups(cfg, seed, dtype, device, layers):
+        sd.update(tensors)
     return sd
+
+
+def write_random_checkpoint_by_layer(path: str, cfg: MambaConfig, seed: int = 0, dtype=torch.bfloat16,
+                                     device="cpu") -> str:
+    """Writes the random-init checkpoint as one safetensors shard per layer (plus one for
+    the embedding and norm_f) with a ``model.safetensors.index.json``, drawing and writing
+    one group at a time, so no process ever holds the whole model (the values equal
+    random_init_state_dict with the same seed, dtype and device)."""
+    from safetensors.torch import save_file
+
+    os.makedirs(path, exist_ok=True)
+    with open(os.path.join(path, "config.json"), "w") as f:
+        json.dump(hf_config_dict(cfg), f, indent=1)
+    weight_map, total = {}, 0
+    head = {}
+    for group, tensors in _random_init_groups(cfg, seed, dtype, device):
+        tensors = {k: v.detach().contiguous().cpu() for k, v in tensors.items()}
+        if group in ("embeddings", "norm_f"):  # small: the embedding shard is written last
+            head.update(tensors)
+            continue
+        name = f"model-layer-{int(group.split()[1]):05d}.safetensors"
+        save_file(tensors, os.path.join(path, name))
+        weight_map.update({k: name for k in tensors})
+        total += sum(v.numel() * v.element_size() for v in tensors.values())
+    save_file(head, os.path.join(path, "model-embeddings.safetensors"))
+    weight_map.update({k: "model-embeddings.safetensors" for k in head})
+    total += sum(v.numel() * v.element_size() for v in head.values())
+    with open(os.path.join(path, "model.safetensors.index.json"), "w") as f:
+        json.dump({"metadata": {"total_size": total}, "weight_map": weight_map}, f, indent=1)
+    return path
 
 
 def hf_config_dict(cfg: MambaConfig) -> dict:

@@ -171,7 +171,7 @@ struct EpiOut {
   float eps;
   int out_dtype;        // OUTPROJ: dtype of bias / norm_w / normed
   int rdt;              // dtype the reduced values are rounded to (the collective's return dtype)
-  int wide;             // rows take the 16-column granule layout (RMSNorm sum order of reduce_wide_kernel)
+  int wide;             // rows take the 16-column granule layout (RMSNorm sum order of WideOps)
 };
 
 // Round to the collective's return dtype: the reference's reductions return the
@@ -203,7 +203,7 @@ template <int EPI>
 __device__ __forceinline__ void epilogue_row(const EpiOut &e, const float *val, int r, int cols, int lane) {
   if (EPI == EPI_OUTPROJ && e.wide) {
     // lane l owns the 16-column granules 16 (32 i + l), summed four values at a time in column
-    // order: the order of reduce_wide_kernel, so both variants give the same bits
+    // order: the order of the wide-row pipelined kernel, so both variants give the same bits
     float ss = 0.f;
     float *res = e.resid + (size_t)r * cols;
     for (int c0 = 16 * lane; c0 < cols; c0 += 512) {
@@ -286,12 +286,16 @@ __device__ __forceinline__ void epilogue_row(const EpiOut &e, const float *val, 
 
 // ----------------------------------------------------------------- flags
 
-// Signal phase `phase` of CTA j to `targets` (bitmask of ranks), after all threads' stores.
+// Signal phase `phase` of CTA j to `targets` (bitmask of ranks), after all threads' stores:
+// the CTA barrier orders every thread's stores before the flag-writing threads, whose
+// system-scope fence and release store then publish them (one fence per target rank, not
+// one per thread: a system fence waits for the thread's outstanding remote stores).
 __device__ __forceinline__ void signal(const CommDev &d, int site, int phase, uint32_t epoch, uint32_t targets) {
-  __threadfence_system();
   __syncthreads();
-  if (threadIdx.x < (unsigned)d.ws && (targets >> threadIdx.x) & 1u)
+  if (threadIdx.x < (unsigned)d.ws && (targets >> threadIdx.x) & 1u) {
+    __threadfence_system();
     st_release_sys(flag_ptr(d.peer[threadIdx.x], d, site, phase, d.rank, blockIdx.x), epoch);
+  }
 }
 
 // Wait until every rank in `sources` signalled phase `phase` of CTA j.  Returns false on timeout.
@@ -308,8 +312,10 @@ __device__ __forceinline__ bool wait_all(const CommDev &d, int site, int phase, 
         break;
       }
     }
+    __threadfence();
   }
-  __threadfence();
+  // the acquiring threads' loads, then the barrier, order the peers' data before every
+  // thread's reads
   __syncthreads();
   return *abort_sm == 0;
 }
@@ -564,6 +570,61 @@ __device__ __forceinline__ void load_gather_v(const char *g, RowV<VPL> &R, int r
   }
 }
 
+// The out_proj epilogue on a register row (narrow layout): bias, residual add (resid
+// updated in place), then, when normed is requested, R = norm_w * (h * rsqrt(mean(h^2)
+// + eps)) in fp32 (else R = h).  store_rows_v stores R in the output dtype.
+template <int VPL>
+__device__ __forceinline__ void outproj_norm_v(const EpiOut &e, RowV<VPL> &R, int r, int cols, int lane) {
+  float ss = 0.f;
+  float *res = e.resid + (size_t)r * cols;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = (i * 32 + lane) * 4;
+    if (c >= cols) break;
+    float4 v = R.v[i];
+    if (e.bias) {
+      v.x += ld_any(e.bias, e.out_dtype, c); v.y += ld_any(e.bias, e.out_dtype, c + 1);
+      v.z += ld_any(e.bias, e.out_dtype, c + 2); v.w += ld_any(e.bias, e.out_dtype, c + 3);
+    }
+    const float4 h0 = *reinterpret_cast<const float4 *>(res + c);
+    const float4 h = make_float4(h0.x + v.x, h0.y + v.y, h0.z + v.z, h0.w + v.w);
+    *reinterpret_cast<float4 *>(res + c) = h;
+    ss = __fadd_rn(ss, sq4(h));
+    R.v[i] = h;
+  }
+  if (!e.normed) return;
+  const float rs = rsqrtf(warp_sum(ss) / (float)cols + e.eps);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = (i * 32 + lane) * 4;
+    if (c >= cols) break;
+    const float4 h = R.v[i];
+    float o[4] = {h.x * rs, h.y * rs, h.z * rs, h.w * rs};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) o[q] = ld_any(e.norm_w, e.out_dtype, c + q) * o[q];
+    R.v[i] = make_float4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+template <int VPL>
+__device__ __forceinline__ void store_rows_v(void *dst, int dtype, const RowV<VPL> &R, int r, int cols, int lane) {
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = (i * 32 + lane) * 4;
+    if (c >= cols) break;
+    const float4 o = R.v[i];
+    if (dtype == MTP_F32) {
+      *reinterpret_cast<float4 *>(reinterpret_cast<float *>(dst) + (size_t)r * cols + c) = o;
+    } else {
+      __nv_bfloat162 a = __floats2bfloat162_rn(o.x, o.y), b = __floats2bfloat162_rn(o.z, o.w);
+      uint2 u;
+      u.x = *reinterpret_cast<uint32_t *>(&a);
+      u.y = *reinterpret_cast<uint32_t *>(&b);
+      *reinterpret_cast<uint2 *>(reinterpret_cast<__nv_bfloat16 *>(dst) + (size_t)r * cols + c) = u;
+    }
+  }
+}
+
 template <int EPI, int VPL>
 __device__ __forceinline__ void epilogue_v(const EpiOut &e, RowV<VPL> &R, int r, int cols, int lane) {
   if (EPI == EPI_PLAIN) {
@@ -587,126 +648,9 @@ __device__ __forceinline__ void epilogue_v(const EpiOut &e, RowV<VPL> &R, int r,
       }
     }
   } else {
-    float ss = 0.f;
-    float *res = e.resid + (size_t)r * cols;
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      const int c = (i * 32 + lane) * 4;
-      if (c >= cols) break;
-      float4 v = R.v[i];
-      if (e.bias) {
-        v.x += ld_any(e.bias, e.out_dtype, c); v.y += ld_any(e.bias, e.out_dtype, c + 1);
-        v.z += ld_any(e.bias, e.out_dtype, c + 2); v.w += ld_any(e.bias, e.out_dtype, c + 3);
-      }
-      const float4 h0 = *reinterpret_cast<const float4 *>(res + c);
-      const float4 h = make_float4(h0.x + v.x, h0.y + v.y, h0.z + v.z, h0.w + v.w);
-      *reinterpret_cast<float4 *>(res + c) = h;
-      ss = __fadd_rn(ss, sq4(h));
-      R.v[i] = h;
-    }
-    if (e.normed) {
-      const float rs = rsqrtf(warp_sum(ss) / (float)cols + e.eps);
-#pragma unroll
-      for (int i = 0; i < VPL; ++i) {
-        const int c = (i * 32 + lane) * 4;
-        if (c >= cols) break;
-        const float4 h = R.v[i];
-        float o[4] = {h.x * rs, h.y * rs, h.z * rs, h.w * rs};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) o[q] = ld_any(e.norm_w, e.out_dtype, c + q) * o[q];
-        if (e.out_dtype == MTP_F32) {
-          *reinterpret_cast<float4 *>(reinterpret_cast<float *>(e.normed) + (size_t)r * cols + c) = make_float4(o[0], o[1], o[2], o[3]);
-        } else {
-          __nv_bfloat162 a = __floats2bfloat162_rn(o[0], o[1]), b = __floats2bfloat162_rn(o[2], o[3]);
-          uint2 u;
-          u.x = *reinterpret_cast<uint32_t *>(&a);
-          u.y = *reinterpret_cast<uint32_t *>(&b);
-          *reinterpret_cast<uint2 *>(reinterpret_cast<__nv_bfloat16 *>(e.normed) + (size_t)r * cols + c) = u;
-        }
-      }
-    }
+    outproj_norm_v(e, R, r, cols, lane);
+    if (e.normed) store_rows_v(e.normed, e.out_dtype, R, r, cols, lane);
   }
-}
-
-template <int MODE, int EPI, int VPL>
-__global__ void __launch_bounds__(WPB * 32, (VPL >= 16 ? 2 : 3)) reduce_rows_kernel(CommDev d, bool has_comm, int site,
-                                                               const float *__restrict__ partial, int rows, int cols,
-                                                               bool two_shot, EpiOut e) {
-  MTP_PDL_WAIT();
-  MTP_PDL_TRIGGER();
-  __shared__ int abort_sm;
-  __shared__ uint32_t epoch_sm;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int j = blockIdx.x, G = gridDim.x;
-  RowV<VPL> R;
-  if (!has_comm) {
-    for (int r = j * WPB + warp; r < rows; r += G * WPB) {
-      load_rowv<false>(partial + (size_t)r * cols, cols, lane, R);
-      roundtrip_v<MODE>(R);
-      round_v(R, e.rdt);
-      epilogue_v<EPI>(e, R, r, cols, lane);
-    }
-    return;
-  }
-  uint32_t *ep = reinterpret_cast<uint32_t *>(d.peer[d.rank] + d.off_epoch) + site;
-  if (threadIdx.x == 0) {
-    abort_sm = 0;
-    epoch_sm = *reinterpret_cast<volatile uint32_t *>(ep) + 1u;
-  }
-  __syncthreads();
-  const uint32_t epoch = epoch_sm;
-  auto finish = [&]() {
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      __threadfence();
-      unsigned int *done = reinterpret_cast<unsigned int *>(d.peer[d.rank] + d.off_done) + site;
-      if (atomicAdd(done, 1u) == (unsigned)G - 1u) {
-        *done = 0u;
-        *reinterpret_cast<volatile uint32_t *>(ep) = epoch;
-        __threadfence();
-      }
-    }
-  };
-  const size_t half = (size_t)(epoch & 1u) * d.ws * d.slot_bytes[site];
-  const uint32_t all = (1u << d.ws) - 1u;
-  const int chunk = (rows + d.ws - 1) / d.ws;
-  for (int r = j * WPB + warp; r < rows; r += G * WPB) {
-    load_rowv<false>(partial + (size_t)r * cols, cols, lane, R);
-    const float sc = MODE == MTP_RED_INT8TOK ? row_scale(rowv_amax(R)) : 0.f;
-    const size_t my_slot = d.off_recv[site] + half + (size_t)d.rank * d.slot_bytes[site];
-    if (two_shot) {
-      write_wire_v<MODE>(d.peer[r / chunk] + my_slot, R, r, rows, cols, lane, sc);
-    } else {
-      for (int k = 0; k < d.ws; ++k) write_wire_v<MODE>(d.peer[(d.rank + k) % d.ws] + my_slot, R, r, rows, cols, lane, sc);
-    }
-  }
-  signal(d, site, 0, epoch, all);
-  if (!wait_all(d, site, 0, epoch, all, &abort_sm)) { finish(); return; }
-  char *slots[MAX_WS];
-  for (int k = 0; k < d.ws; ++k) slots[k] = d.peer[d.rank] + d.off_recv[site] + half + (size_t)k * d.slot_bytes[site];
-  if (!two_shot) {
-    for (int r = j * WPB + warp; r < rows; r += G * WPB) {
-      reduce_v<MODE>(slots, d.ws, r, rows, cols, lane, R);
-      round_v(R, e.rdt);
-      epilogue_v<EPI>(e, R, r, cols, lane);
-    }
-    finish();
-    return;
-  }
-  for (int r = j * WPB + warp; r < rows; r += G * WPB) {
-    if (r / chunk != d.rank) continue;
-    reduce_v<MODE>(slots, d.ws, r, rows, cols, lane, R);
-    round_v(R, e.rdt);
-    for (int k = 0; k < d.ws; ++k) store_gather_v(d.peer[(d.rank + k) % d.ws] + d.off_gath[site], R, r, cols, lane, e.rdt);
-  }
-  signal(d, site, 1, epoch, all);
-  if (!wait_all(d, site, 1, epoch, all, &abort_sm)) { finish(); return; }
-  const char *gath_local = d.peer[d.rank] + d.off_gath[site];
-  for (int r = j * WPB + warp; r < rows; r += G * WPB) {
-    load_gather_v(gath_local, R, r, cols, lane, e.rdt);
-    epilogue_v<EPI>(e, R, r, cols, lane);
-  }
-  finish();
 }
 
 // ----------------------------------------------------------------- wide-row reduction (16-column granules)
@@ -942,24 +886,10 @@ __device__ __forceinline__ void load_vec16(const void *p, int dtype, int c, floa
   }
 }
 
-// Epilogue of a reduced row in the 16-column layout.  The RMSNorm sum of squares runs over
-// the lane's granules in column order, four values at a time (sq4), then across the warp:
-// the same order as epilogue_row gives the wide layout, so every kernel variant computes the
-// same bits.  Bias, norm_w and normed need 16-byte aligned rows (checked on the host).
-template <int EPI, int NC>
-__device__ __forceinline__ void epilogue_w(const EpiOut &e, RowW<NC> &R, int r, int cols, int lane) {
-  if (EPI == EPI_PLAIN) {
-#pragma unroll
-    for (int i = 0; i < NC; ++i) {
-      const int c = 16 * (i * 32 + lane);
-      if (c >= cols) break;
-      float4 *o = reinterpret_cast<float4 *>(e.out + (size_t)r * cols + c);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) o[j] = make_float4(R.v[i][4 * j], R.v[i][4 * j + 1], R.v[i][4 * j + 2], R.v[i][4 * j + 3]);
-    }
-    return;
-  }
-  // EPI_OUTPROJ
+// The out_proj epilogue in the 16-column layout (as outproj_norm_v): bias, residual add,
+// then R = norm_w * (h * rs) when normed is requested; store_rows_w stores R.
+template <int NC>
+__device__ __forceinline__ void outproj_norm_w(const EpiOut &e, RowW<NC> &R, int r, int cols, int lane) {
   float ss = 0.f;
   float *res = e.resid + (size_t)r * cols;
 #pragma unroll
@@ -985,46 +915,173 @@ __device__ __forceinline__ void epilogue_w(const EpiOut &e, RowW<NC> &R, int r, 
       R.v[i][4 * j] = h.x; R.v[i][4 * j + 1] = h.y; R.v[i][4 * j + 2] = h.z; R.v[i][4 * j + 3] = h.w;
     }
   }
-  if (e.normed) {
-    const float rs = rsqrtf(warp_sum(ss) / (float)cols + e.eps);
+  if (!e.normed) return;
+  const float rs = rsqrtf(warp_sum(ss) / (float)cols + e.eps);
 #pragma unroll
-    for (int i = 0; i < NC; ++i) {
-      const int c = 16 * (i * 32 + lane);
-      if (c >= cols) break;
-      float w[16], o[16];
-      load_vec16(e.norm_w, e.out_dtype, c, w);
+  for (int i = 0; i < NC; ++i) {
+    const int c = 16 * (i * 32 + lane);
+    if (c >= cols) break;
+    float w[16];
+    load_vec16(e.norm_w, e.out_dtype, c, w);
 #pragma unroll
-      for (int k = 0; k < 16; ++k) o[k] = w[k] * (R.v[i][k] * rs);
-      if (e.out_dtype == MTP_F32) {
-        float4 *p = reinterpret_cast<float4 *>(reinterpret_cast<float *>(e.normed) + (size_t)r * cols + c);
+    for (int k = 0; k < 16; ++k) R.v[i][k] = w[k] * (R.v[i][k] * rs);
+  }
+}
+
+template <int NC>
+__device__ __forceinline__ void store_rows_w(void *dst, int dtype, const RowW<NC> &R, int r, int cols, int lane) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) p[j] = make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
-      } else {
-        uint4 *p = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(e.normed) + (size_t)r * cols + c);
-        p[0] = pack_bf16x8(o);
-        p[1] = pack_bf16x8(o + 8);
-      }
+  for (int i = 0; i < NC; ++i) {
+    const int c = 16 * (i * 32 + lane);
+    if (c >= cols) break;
+    if (dtype == MTP_F32) {
+      float4 *p = reinterpret_cast<float4 *>(reinterpret_cast<float *>(dst) + (size_t)r * cols + c);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) p[j] = make_float4(R.v[i][4 * j], R.v[i][4 * j + 1], R.v[i][4 * j + 2], R.v[i][4 * j + 3]);
+    } else {
+      uint4 *p = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(dst) + (size_t)r * cols + c);
+      p[0] = pack_bf16x8(R.v[i]);
+      p[1] = pack_bf16x8(R.v[i] + 8);
     }
   }
 }
 
-template <int MODE, int EPI, int NC>
-__global__ void __launch_bounds__(WPB * 32, 2) reduce_wide_kernel(CommDev d, bool has_comm, int site,
-                                                                  const float *__restrict__ partial, int rows,
-                                                                  int cols, bool two_shot, EpiOut e) {
+// Epilogue of a reduced row in the 16-column layout.  The RMSNorm sum of squares runs over
+// the lane's granules in column order, four values at a time (sq4), then across the warp:
+// the same order as epilogue_row gives the wide layout, so every kernel variant computes the
+// same bits.  Bias, norm_w and normed need 16-byte aligned rows (checked on the host).
+template <int EPI, int NC>
+__device__ __forceinline__ void epilogue_w(const EpiOut &e, RowW<NC> &R, int r, int cols, int lane) {
+  if (EPI == EPI_PLAIN) {
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const int c = 16 * (i * 32 + lane);
+      if (c >= cols) break;
+      float4 *o = reinterpret_cast<float4 *>(e.out + (size_t)r * cols + c);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o[j] = make_float4(R.v[i][4 * j], R.v[i][4 * j + 1], R.v[i][4 * j + 2], R.v[i][4 * j + 3]);
+    }
+    return;
+  }
+  // EPI_OUTPROJ
+  outproj_norm_w(e, R, r, cols, lane);
+  if (e.normed) store_rows_w(e.normed, e.out_dtype, R, r, cols, lane);
+}
+
+// ----------------------------------------------------------------- pipelined reduction kernel
+// Row operations of the two register layouts (narrow: float4 chunks, wide: 16-column
+// granules), so one kernel body drives both.
+template <int MODE_, int EPI_, int VPL>
+struct NarrowOps {
+  static constexpr int MODE = MODE_, EPI = EPI_, MINB = VPL >= 16 ? 2 : 3;
+  using Row = RowV<VPL>;
+  static __device__ __forceinline__ void load(const float *p, int cols, int lane, Row &R) { load_rowv<false>(p, cols, lane, R); }
+  static __device__ __forceinline__ float amax(const Row &R) { return rowv_amax(R); }
+  static __device__ __forceinline__ void roundtrip(Row &R) { roundtrip_v<MODE>(R); }
+  static __device__ __forceinline__ void round(Row &R, int rdt) { round_v(R, rdt); }
+  static __device__ __forceinline__ void wire(char *dst, const Row &R, int r, int rows, int cols, int lane, float sc) {
+    write_wire_v<MODE>(dst, R, r, rows, cols, lane, sc);
+  }
+  static __device__ __forceinline__ void reduce(char *const *slots, int nsrc, int r, int rows, int cols, int lane, Row &R) {
+    reduce_v<MODE>(slots, nsrc, r, rows, cols, lane, R);
+  }
+  static __device__ __forceinline__ void store_gather(char *g, const Row &R, int r, int cols, int lane, int rdt) {
+    store_gather_v(g, R, r, cols, lane, rdt);
+  }
+  static __device__ __forceinline__ void load_gather(const char *g, Row &R, int r, int cols, int lane, int rdt) {
+    load_gather_v(g, R, r, cols, lane, rdt);
+  }
+  static __device__ __forceinline__ void epilogue(const EpiOut &e, Row &R, int r, int cols, int lane) {
+    epilogue_v<EPI>(e, R, r, cols, lane);
+  }
+  static __device__ __forceinline__ void norm(const EpiOut &e, Row &R, int r, int cols, int lane) {
+    outproj_norm_v(e, R, r, cols, lane);
+  }
+  static __device__ __forceinline__ void store_normed(const EpiOut &e, const Row &R, int r, int cols, int lane) {
+    store_rows_v(e.normed, e.out_dtype, R, r, cols, lane);
+  }
+};
+
+template <int MODE_, int EPI_, int NC>
+struct WideOps {
+  static constexpr int MODE = MODE_, EPI = EPI_, MINB = 2;
+  using Row = RowW<NC>;
+  static __device__ __forceinline__ void load(const float *p, int cols, int lane, Row &R) { load_roww<false>(p, cols, lane, R); }
+  static __device__ __forceinline__ float amax(const Row &R) { return roww_amax(R); }
+  static __device__ __forceinline__ void roundtrip(Row &R) { roundtrip_w<MODE>(R); }
+  static __device__ __forceinline__ void round(Row &R, int rdt) { round_w(R, rdt); }
+  static __device__ __forceinline__ void wire(char *dst, const Row &R, int r, int rows, int cols, int lane, float sc) {
+    write_wire_w<MODE>(dst, R, r, rows, cols, lane, sc);
+  }
+  static __device__ __forceinline__ void reduce(char *const *slots, int nsrc, int r, int rows, int cols, int lane, Row &R) {
+    reduce_w<MODE>(slots, nsrc, r, rows, cols, lane, R);
+  }
+  static __device__ __forceinline__ void store_gather(char *g, const Row &R, int r, int cols, int lane, int rdt) {
+    store_gather_w(g, R, r, cols, lane, rdt);
+  }
+  static __device__ __forceinline__ void load_gather(const char *g, Row &R, int r, int cols, int lane, int rdt) {
+    load_gather_w(g, R, r, cols, lane, rdt);
+  }
+  static __device__ __forceinline__ void epilogue(const EpiOut &e, Row &R, int r, int cols, int lane) {
+    epilogue_w<EPI>(e, R, r, cols, lane);
+  }
+  static __device__ __forceinline__ void norm(const EpiOut &e, Row &R, int r, int cols, int lane) {
+    outproj_norm_w(e, R, r, cols, lane);
+  }
+  static __device__ __forceinline__ void store_normed(const EpiOut &e, const Row &R, int r, int cols, int lane) {
+    store_rows_w(e.normed, e.out_dtype, R, r, cols, lane);
+  }
+};
+
+// Flag phases of the pipelined protocol (phases 0 and 1 belong to the unpipelined
+// scratch kernel and to the decode kernel, which flag with the bare epoch).
+constexpr int PH_PUSH = 2, PH_GATHER = 3;
+constexpr uint32_t ROUNDS_PER_EPOCH = 256;  // flag value of round k of a call: epoch * 256 + k
+
+// Fence this thread's stores of the round, then flag `targets` for up to two (phase, value)
+// pairs (the push round and the gather round of the two-shot pipeline).
+__device__ __forceinline__ void signal_rounds(const CommDev &d, int site, int pa, uint32_t va, bool da, int pb,
+                                              uint32_t vb, bool db) {
+  __syncthreads();
+  if (threadIdx.x < (unsigned)d.ws) {
+    __threadfence_system();
+    if (da) st_release_sys(flag_ptr(d.peer[threadIdx.x], d, site, pa, d.rank, blockIdx.x), va);
+    if (db) st_release_sys(flag_ptr(d.peer[threadIdx.x], d, site, pb, d.rank, blockIdx.x), vb);
+  }
+}
+
+// One reduction launch, pipelined in rounds.  CTA j owns the row slices s = 0, 1, ... with
+// rows (s G + j) WPB + warp (the same rows on every rank); round k is slices
+// [k rpw, (k+1) rpw).  One-shot: a round's wire rows go to every rank and are reduced one
+// round later, after every rank's flag for that round -- so the NVLink transfer of round
+// k overlaps the reduce and epilogue of round k-1.  Two-shot: round k's wire rows go to
+// their owner rank (rows split in ws contiguous chunks); one round later the owner reduces
+// them and pushes the rounded result rows to every rank's gather buffer; one round after
+// that every rank runs the epilogue.  Every rank reduces in rank order, so all ranks hold
+// the same bits.  Flag values grow with the round; every wait is bounded.
+template <class Ops>
+__global__ void __launch_bounds__(WPB * 32, Ops::MINB) reduce_pipe_kernel(CommDev d, bool has_comm, int site,
+                                                                           const float *__restrict__ partial, int rows,
+                                                                           int cols, bool two_shot, bool sp, int rpw,
+                                                                           EpiOut e) {
+  constexpr int MODE = Ops::MODE;
   MTP_PDL_WAIT();
   MTP_PDL_TRIGGER();
   __shared__ int abort_sm;
   __shared__ uint32_t epoch_sm;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int j = blockIdx.x, G = gridDim.x;
-  RowW<NC> R;
+  typename Ops::Row R;
+  const int S = rows > j * WPB ? (rows - j * WPB + G * WPB - 1) / (G * WPB) : 0;  // slices of this CTA
+  auto row_of = [&](int sl) { return (sl * G + j) * WPB + warp; };
   if (!has_comm) {
-    for (int r = j * WPB + warp; r < rows; r += G * WPB) {
-      load_roww<false>(partial + (size_t)r * cols, cols, lane, R);
-      roundtrip_w<MODE>(R);
-      round_w(R, e.rdt);
-      epilogue_w<EPI>(e, R, r, cols, lane);
+    for (int sl = 0; sl < S; ++sl) {
+      const int r = row_of(sl);
+      if (r >= rows) continue;
+      Ops::load(partial + (size_t)r * cols, cols, lane, R);
+      Ops::roundtrip(R);
+      Ops::round(R, e.rdt);
+      Ops::epilogue(e, R, r, cols, lane);
     }
     return;
   }
@@ -1051,41 +1108,104 @@ __global__ void __launch_bounds__(WPB * 32, 2) reduce_wide_kernel(CommDev d, boo
   const uint32_t all = (1u << d.ws) - 1u;
   const int chunk = (rows + d.ws - 1) / d.ws;
   const size_t my_slot = d.off_recv[site] + half + (size_t)d.rank * d.slot_bytes[site];
-  for (int r = j * WPB + warp; r < rows; r += G * WPB) {
-    load_roww<false>(partial + (size_t)r * cols, cols, lane, R);
-    const float sc = MODE == MTP_RED_INT8TOK ? row_scale(roww_amax(R)) : 0.f;
-    if (two_shot) {
-      write_wire_w<MODE>(d.peer[r / chunk] + my_slot, R, r, rows, cols, lane, sc);
-    } else {
-      for (int k = 0; k < d.ws; ++k) write_wire_w<MODE>(d.peer[(d.rank + k) % d.ws] + my_slot, R, r, rows, cols, lane, sc);
-    }
-  }
-  signal(d, site, 0, epoch, all);
-  if (!wait_all(d, site, 0, epoch, all, &abort_sm)) { finish(); return; }
   char *slots[MAX_WS];
   for (int k = 0; k < d.ws; ++k) slots[k] = d.peer[d.rank] + d.off_recv[site] + half + (size_t)k * d.slot_bytes[site];
+  const int K = (S + rpw - 1) / rpw;
+  const uint32_t v0 = epoch * ROUNDS_PER_EPOCH;
+  // optional phase trace: thread 0 of CTA 0 and of the last CTA stamp each event
+  unsigned long long *tr = nullptr;
+  int tn = 0;
+  if (d.trace && threadIdx.x == 0 && (j == 0 || j == G - 1)) {
+    __shared__ unsigned int rec_sm;
+    if (j == 0) rec_sm = atomicAdd(d.trace_count, 1u);
+    else rec_sm = atomicAdd(d.trace_count + 1, 1u);
+    unsigned long long *rec = d.trace + (size_t)(rec_sm % (unsigned)d.trace_cap) * TRACE_WORDS;
+    if (j == 0) { rec[0] = G; rec[1] = K; rec[2] = two_shot; }
+    tr = rec + 3 + (j == 0 ? 0 : 64);
+    tr[tn++] = globaltimer_ns();
+  }
+  auto stamp = [&]() {
+    if (tr && tn < 64) tr[tn++] = globaltimer_ns();
+  };
+  auto push_round = [&](int k) {
+    for (int i = 0; i < rpw; ++i) {
+      const int sl = k * rpw + i, r = row_of(sl);
+      if (sl >= S || r >= rows) continue;
+      Ops::load(partial + (size_t)r * cols, cols, lane, R);
+      const float sc = MODE == MTP_RED_INT8TOK ? row_scale(Ops::amax(R)) : 0.f;
+      if (two_shot) {
+        Ops::wire(d.peer[r / chunk] + my_slot, R, r, rows, cols, lane, sc);
+      } else {
+        for (int q = 0; q < d.ws; ++q) Ops::wire(d.peer[(d.rank + q) % d.ws] + my_slot, R, r, rows, cols, lane, sc);
+      }
+    }
+  };
   if (!two_shot) {
-    for (int r = j * WPB + warp; r < rows; r += G * WPB) {
-      reduce_w<MODE>(slots, d.ws, r, rows, cols, lane, R);
-      round_w(R, e.rdt);
-      epilogue_w<EPI>(e, R, r, cols, lane);
+    for (int k = 0; k <= K; ++k) {
+      if (k < K) push_round(k);
+      stamp();
+      if (k >= 1) {
+        if (!wait_all(d, site, PH_PUSH, v0 + (uint32_t)(k - 1), all, &abort_sm)) { finish(); return; }
+        stamp();
+        for (int i = 0; i < rpw; ++i) {
+          const int sl = (k - 1) * rpw + i, r = row_of(sl);
+          if (sl >= S || r >= rows) continue;
+          Ops::reduce(slots, d.ws, r, rows, cols, lane, R);
+          Ops::round(R, e.rdt);
+          Ops::epilogue(e, R, r, cols, lane);
+        }
+        stamp();
+      }
+      if (k < K) signal_rounds(d, site, PH_PUSH, v0 + (uint32_t)k, true, PH_GATHER, 0u, false);
+      stamp();
     }
     finish();
     return;
   }
-  // owner rows: the rows of rank d.rank's chunk that this warp covers
-  for (int r = j * WPB + warp; r < rows; r += G * WPB) {
-    if (r / chunk != d.rank) continue;
-    reduce_w<MODE>(slots, d.ws, r, rows, cols, lane, R);
-    round_w(R, e.rdt);
-    for (int k = 0; k < d.ws; ++k) store_gather_w(d.peer[(d.rank + k) % d.ws] + d.off_gath[site], R, r, cols, lane, e.rdt);
-  }
-  signal(d, site, 1, epoch, all);
-  if (!wait_all(d, site, 1, epoch, all, &abort_sm)) { finish(); return; }
   const char *gath_local = d.peer[d.rank] + d.off_gath[site];
-  for (int r = j * WPB + warp; r < rows; r += G * WPB) {
-    load_gather_w(gath_local, R, r, cols, lane, e.rdt);
-    epilogue_w<EPI>(e, R, r, cols, lane);
+  for (int k = 0; k <= K + 1; ++k) {
+    if (k < K) push_round(k);
+    stamp();
+    if (k >= 1 && k <= K) {
+      if (!wait_all(d, site, PH_PUSH, v0 + (uint32_t)(k - 1), all, &abort_sm)) { finish(); return; }
+      stamp();
+      for (int i = 0; i < rpw; ++i) {
+        const int sl = (k - 1) * rpw + i, r = row_of(sl);
+        if (sl >= S || r >= rows || r / chunk != d.rank) continue;
+        Ops::reduce(slots, d.ws, r, rows, cols, lane, R);
+        Ops::round(R, e.rdt);
+        if constexpr (Ops::EPI == EPI_OUTPROJ) {
+          if (sp) {  // the owner runs the epilogue; the normed row is what every rank gathers
+            Ops::norm(e, R, r, cols, lane);
+            for (int q = 0; q < d.ws; ++q)
+              Ops::store_gather(d.peer[(d.rank + q) % d.ws] + d.off_gath[site], R, r, cols, lane, e.out_dtype);
+            continue;
+          }
+        }
+        for (int q = 0; q < d.ws; ++q) Ops::store_gather(d.peer[(d.rank + q) % d.ws] + d.off_gath[site], R, r, cols, lane, e.rdt);
+      }
+      stamp();
+    }
+    if (k >= 2) {
+      if (!wait_all(d, site, PH_GATHER, v0 + (uint32_t)(k - 2), all, &abort_sm)) { finish(); return; }
+      stamp();
+      for (int i = 0; i < rpw; ++i) {
+        const int sl = (k - 2) * rpw + i, r = row_of(sl);
+        if (sl >= S || r >= rows) continue;
+        if constexpr (Ops::EPI == EPI_OUTPROJ) {
+          if (sp) {  // the gathered row is the normed row: copy it out
+            Ops::load_gather(gath_local, R, r, cols, lane, e.out_dtype);
+            Ops::store_normed(e, R, r, cols, lane);
+            continue;
+          }
+        }
+        Ops::load_gather(gath_local, R, r, cols, lane, e.rdt);
+        Ops::epilogue(e, R, r, cols, lane);
+      }
+      stamp();
+    }
+    if (k <= K) signal_rounds(d, site, PH_PUSH, v0 + (uint32_t)k, k < K, PH_GATHER, v0 + (uint32_t)(k - 1), k >= 1);
+    stamp();
   }
   finish();
 }
@@ -1120,85 +1240,95 @@ __global__ void dequant_sum_kernel(const uint8_t *__restrict__ pl, int ws, int r
 }
 
 // ----------------------------------------------------------------- host
-static float *g_scratch = nullptr;
-static size_t g_scratch_bytes = 0;
-
 // Fixed row scratch for mtp_allreduce_noalloc: a file-scope device array, so that
 // entry point never allocates.  Every GPU that loads the library holds these
 // 4 MiB until the process exits.  Host code must not hand the symbol itself to a
 // kernel (in host code it only names a host-side stand-in); the device address
-// comes from cudaGetSymbolAddress, looked up once per device.
+// comes from cudaGetSymbolAddress, looked up once per device.  The per-device
+// addresses are atomics, so first calls from several host threads do not race.
 constexpr size_t NOALLOC_SCRATCH_FLOATS = (size_t)1 << 20;
 static __device__ __align__(256) float g_noalloc_scratch[NOALLOC_SCRATCH_FLOATS];
-constexpr int NOALLOC_MAX_DEVICES = 64;
-static float *g_noalloc_ptr[NOALLOC_MAX_DEVICES] = {};
+constexpr int MAX_DEVICES = 64;
+static std::atomic<float *> g_noalloc_ptr[MAX_DEVICES];
+
+static int current_device(int *dev) {
+  if (cudaGetDevice(dev) != cudaSuccess) return fail(MTP_ERR_CUDA, "cudaGetDevice failed");
+  if (*dev < 0 || *dev >= MAX_DEVICES) return fail(MTP_ERR_UNSUPPORTED, "device index out of range");
+  return MTP_OK;
+}
 
 // Device address of g_noalloc_scratch on the current device (set up on first use).
 static int noalloc_scratch(float **out) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return fail(MTP_ERR_CUDA, "cudaGetDevice failed");
-  if (dev < 0 || dev >= NOALLOC_MAX_DEVICES) return fail(MTP_ERR_UNSUPPORTED, "device index out of range");
-  if (!g_noalloc_ptr[dev]) {
-    void *p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (int rc = current_device(&dev)) return rc;
+  float *p = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+  if (!p) {
+    void *q = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&q, g_noalloc_scratch);
     if (e != cudaSuccess)
       return fail(MTP_ERR_CUDA, std::string("cudaGetSymbolAddress(g_noalloc_scratch): ") + cudaGetErrorString(e));
-    g_noalloc_ptr[dev] = static_cast<float *>(p);
+    p = static_cast<float *>(q);
+    g_noalloc_ptr[dev].store(p, std::memory_order_release);  // every thread finds the same address
   }
-  *out = g_noalloc_ptr[dev];
+  *out = p;
   return MTP_OK;
 }
 
-// Per-warp row scratch of the reduction kernels.  Grown, never freed: a captured CUDA graph
-// may still hold an older pointer.  The first call (eager, before any capture) sizes it.
+// Per-warp row scratch of the reduction kernels, one per device.  Grown, never freed: a
+// captured CUDA graph may still hold an older pointer.  The first call on a device (eager,
+// before any capture) sizes it.  Growth is not thread-safe: one host thread per device.
+static float *g_scratch[MAX_DEVICES] = {};
+static size_t g_scratch_bytes[MAX_DEVICES] = {};
+
 static float *row_scratch(size_t bytes) {
-  if (bytes > g_scratch_bytes) {
+  int dev = 0;
+  if (current_device(&dev)) return nullptr;
+  if (bytes > g_scratch_bytes[dev]) {
     float *p = nullptr;
     if (bytes < ((size_t)32 << 20)) bytes = (size_t)32 << 20;
     if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
-    g_scratch = p;
-    g_scratch_bytes = bytes;
+    g_scratch[dev] = p;
+    g_scratch_bytes[dev] = bytes;
   }
-  return g_scratch;
+  return g_scratch[dev];
 }
 
-// Resident CTAs per SM of a register-row kernel instance (queried once).  With a comm
-// context the grid is sized to fill every SM at that occupancy: CTA j only waits for CTA
-// j of the other ranks, and CTAs are dispatched in index order, so every launched CTA
-// becomes resident once the preceding kernel has drained.
-// Rows wide enough (and outputs aligned) for reduce_wide_kernel.  The EPI_XPROJ split
-// (dt_low | B|C) keeps the narrow kernels: its rows are at most a few hundred values.
+// Rows wide enough (and outputs aligned) for the 16-column granule layout.  The EPI_XPROJ
+// split (dt_low | B|C) keeps the narrow layout: its rows are at most a few hundred values.
 static bool wide_ok(int epi, int cols, const EpiOut &e) {
   if (epi == EPI_XPROJ || cols % 16 != 0 || cols < 512 || cols > 3072) return false;
   if (epi == EPI_PLAIN) return aligned16(e.out);
   return aligned16(e.resid) && (!e.bias || aligned16(e.bias)) && (!e.normed || (aligned16(e.normed) && aligned16(e.norm_w)));
 }
 
-// Resident CTAs per SM of a wide-row kernel instance (queried once per instance).
-template <int M, int E, int NC>
-static int wide_occupancy() {
+// Resident CTAs per SM of a pipelined kernel instance (queried once per instance).  With a
+// comm context the grid is sized to fill every SM at that occupancy: CTA j only waits for
+// CTA j of the other ranks, and CTAs are dispatched in index order, so every launched CTA
+// becomes resident once the preceding kernel has drained.
+template <class Ops>
+static int pipe_occupancy() {
   static int occ = 0;
   if (occ == 0) {
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, reduce_wide_kernel<M, E, NC>, WPB * 32, 0) != cudaSuccess ||
-        n < 1)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, reduce_pipe_kernel<Ops>, WPB * 32, 0) != cudaSuccess || n < 1)
       n = 1;
     occ = n;
   }
   return occ;
 }
 
-template <int M, int E, int V>
-static int rows_kernel_occupancy() {
-  static int occ = 0;
-  if (occ == 0) {
-    int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, reduce_rows_kernel<M, E, V>, WPB * 32, 0) != cudaSuccess ||
-        n < 1)
-      n = 1;
-    occ = n;
-  }
-  return occ;
+template <class Ops>
+static void launch_pipe(const CommDev &d, bool has_comm, int site, const float *pp, int nr, int cols, bool two_shot,
+                        bool sp, const EpiOut &e, int sms, cudaStream_t s) {
+  const int Gwant = ceil_div(nr, WPB);
+  int cap = has_comm ? sms * pipe_occupancy<Ops>() : sms * 8;
+  if (has_comm && cap > G_MAX) cap = G_MAX;
+  const int G = Gwant < cap ? Gwant : cap;
+  // rows per warp per round: about 8 rounds per launch (each round costs a fence and a flag)
+  const int slices = ceil_div(nr, G * WPB);
+  const int rpw = ceil_div(slices, 8);
+  launch_pdl(reduce_pipe_kernel<Ops>, dim3(G), dim3(WPB * 32), 0, s, d, has_comm, site, pp, nr, cols, two_shot, sp, rpw,
+             e);
 }
 
 // Wire bytes of one row in `mode`, and of one reduced row in the result dtype.
@@ -1208,7 +1338,7 @@ static size_t wire_row_bytes(int mode, int cols) {
 static size_t rdt_row_bytes(int rdt, int cols) { return (rdt == MTP_BF16 ? 2 : 4) * (size_t)cols; }
 
 // Protocol of one reduction launch of nr rows: fewer bytes sent per rank wins; small
-// messages stay one-shot (one flag round).  MTP_COMM_PROTOCOL=oneshot|twoshot overrides.
+// messages stay one-shot (fewer flag rounds).  MTP_COMM_PROTOCOL=oneshot|twoshot overrides.
 static bool use_two_shot(int ws, int mode, int nr, int cols, int rdt) {
   if (ws < 2) return false;
   const size_t wire_row = wire_row_bytes(mode, cols), rdt_row = rdt_row_bytes(rdt, cols);
@@ -1277,37 +1407,39 @@ static int run_reduce(mtp_comm *c, int site, int mode, const float *partial, int
     }
     CommDev d{};
     if (has_comm) d = c->d;
-    const bool two_shot = has_comm && use_two_shot(c->d.ws, mode, nr, cols, e.rdt);
+    // sequence-parallel out_proj epilogue: each row's owner rank applies the residual and
+    // the next RMSNorm and every rank gathers the normed rows (the residual rows of other
+    // owners are then not kept on this rank); needs the normed output and the two-shot
+    // protocol, which it implies.  MTP_COMM_SP=0 turns it off, =1 forces it at 2 ranks.
+    bool sp = EPI == EPI_OUTPROJ && has_comm && ee.normed != nullptr && !capped;
+    if (sp) {
+      const char *env = getenv("MTP_COMM_SP");
+      if (env && !strcmp(env, "0")) sp = false;
+      else if (c->d.ws < 4 && !(env && !strcmp(env, "1"))) sp = false;
+    }
+    const bool two_shot = has_comm && (sp || use_two_shot(c->d.ws, mode, nr, cols, e.rdt));
     const float *pp = partial + (size_t)r0 * cols;
     // wide rows in 16-column granules (16-byte accesses) when the width and the output
     // pointers allow it, else the register-row kernel, else the scratch kernel
     ee.wide = wide_ok(EPI, cols, ee) ? 1 : 0;
     if (!capped && ee.wide) {
       const int nc = (cols + 511) / 512;
-      const int Gwant = ceil_div(nr, WPB);
-#define MTP_RW(M, NCC)                                                                                           \
-  do {                                                                                                           \
-    int cap_ = has_comm ? sms * wide_occupancy<M, EPI, NCC>() : sms * 8;                                         \
-    if (cap_ > G_MAX && has_comm) cap_ = G_MAX;                                                                  \
-    const int Gv = Gwant < cap_ ? Gwant : cap_;                                                                  \
-    launch_pdl(reduce_wide_kernel<M, EPI, NCC>, dim3(Gv), dim3(WPB * 32), 0, s, d, has_comm, site, pp, nr, cols, \
-               two_shot, ee);                                                                                    \
-  } while (0)
-#define MTP_RW_MODE(NCC)                                    \
+#define MTP_PW(M, NCC) launch_pipe<WideOps<M, EPI, NCC>>(d, has_comm, site, pp, nr, cols, two_shot, sp, ee, sms, s)
+#define MTP_PW_MODE(NCC)                                    \
   do {                                                      \
-    if (mode == MTP_RED_FP32) MTP_RW(MTP_RED_FP32, NCC);      \
-    else if (mode == MTP_RED_FP16) MTP_RW(MTP_RED_FP16, NCC); \
-    else MTP_RW(MTP_RED_INT8TOK, NCC);                        \
+    if (mode == MTP_RED_FP32) MTP_PW(MTP_RED_FP32, NCC);      \
+    else if (mode == MTP_RED_FP16) MTP_PW(MTP_RED_FP16, NCC); \
+    else MTP_PW(MTP_RED_INT8TOK, NCC);                        \
   } while (0)
       switch (nc) {
-        case 2: MTP_RW_MODE(2); break;
-        case 3: MTP_RW_MODE(3); break;
-        case 4: MTP_RW_MODE(4); break;
-        case 5: MTP_RW_MODE(5); break;
-        default: MTP_RW_MODE(6); break;
+        case 2: MTP_PW_MODE(2); break;
+        case 3: MTP_PW_MODE(3); break;
+        case 4: MTP_PW_MODE(4); break;
+        case 5: MTP_PW_MODE(5); break;
+        default: MTP_PW_MODE(6); break;
       }
-#undef MTP_RW_MODE
-#undef MTP_RW
+#undef MTP_PW_MODE
+#undef MTP_PW
       int rc = check_launch("reduce");
       if (rc) return rc;
       continue;
@@ -1315,30 +1447,22 @@ static int run_reduce(mtp_comm *c, int site, int mode, const float *partial, int
     // register-row kernel when the width allows it
     const int vpl = (cols % 4 != 0 || capped) ? 0 : cols <= 256 ? 2 : cols <= 512 ? 4 : cols <= 1024 ? 8 : cols <= 2048 ? 16 : cols <= 3072 ? 24 : 0;
     if (vpl) {
-      const int Gwant = ceil_div(nr, WPB);
-#define MTP_RV(M, V)                                                                                             \
-  do {                                                                                                           \
-    int cap_ = has_comm ? sms * rows_kernel_occupancy<M, EPI, V>() : sms * 8;                                    \
-    if (cap_ > G_MAX && has_comm) cap_ = G_MAX;                                                                  \
-    const int Gv = Gwant < cap_ ? Gwant : cap_;                                                                  \
-    launch_pdl(reduce_rows_kernel<M, EPI, V>, dim3(Gv), dim3(WPB * 32), 0, s, d, has_comm, site, pp, nr, cols,   \
-               two_shot, ee);                                                                                    \
-  } while (0)
-#define MTP_RV_MODE(V)                                      \
+#define MTP_PV(M, V) launch_pipe<NarrowOps<M, EPI, V>>(d, has_comm, site, pp, nr, cols, two_shot, sp, ee, sms, s)
+#define MTP_PV_MODE(V)                                      \
   do {                                                      \
-    if (mode == MTP_RED_FP32) MTP_RV(MTP_RED_FP32, V);      \
-    else if (mode == MTP_RED_FP16) MTP_RV(MTP_RED_FP16, V); \
-    else MTP_RV(MTP_RED_INT8TOK, V);                        \
+    if (mode == MTP_RED_FP32) MTP_PV(MTP_RED_FP32, V);      \
+    else if (mode == MTP_RED_FP16) MTP_PV(MTP_RED_FP16, V); \
+    else MTP_PV(MTP_RED_INT8TOK, V);                        \
   } while (0)
       switch (vpl) {
-        case 2: MTP_RV_MODE(2); break;
-        case 4: MTP_RV_MODE(4); break;
-        case 8: MTP_RV_MODE(8); break;
-        case 16: MTP_RV_MODE(16); break;
-        default: MTP_RV_MODE(24); break;
+        case 2: MTP_PV_MODE(2); break;
+        case 4: MTP_PV_MODE(4); break;
+        case 8: MTP_PV_MODE(8); break;
+        case 16: MTP_PV_MODE(16); break;
+        default: MTP_PV_MODE(24); break;
       }
-#undef MTP_RV_MODE
-#undef MTP_RV
+#undef MTP_PV_MODE
+#undef MTP_PV
     } else {
 #define MTP_RED_LAUNCH(M) \
   launch_pdl(reduce_kernel<M, EPI>, dim3(G), dim3(WPB * 32), 0, s, d, has_comm, site, pp, nr, cols, two_shot, scr, ee)
@@ -1370,7 +1494,7 @@ int mtp_comm_create(int rank, int world_size, int max_rows, int cols_x, int cols
   auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
   size_t off = 0;
   c->d.off_flags = off;
-  off = al(off + sizeof(uint32_t) * 2 * 2 * MAX_WS * G_MAX);
+  off = al(off + sizeof(uint32_t) * 2 * NPHASE * MAX_WS * G_MAX);
   c->d.off_epoch = off;
   off = al(off + sizeof(uint32_t) * 2);
   c->d.off_done = off;
@@ -1431,6 +1555,7 @@ int mtp_comm_open_peers(mtp_comm *c, const void *handles) {
 int mtp_comm_destroy(mtp_comm *c) {
   if (!c) return MTP_OK;
   cudaDeviceSynchronize();
+  if (c->d.trace) cudaFree(c->d.trace);
   for (int k = 0; k < c->d.ws; ++k)
     if (k != c->d.rank && c->d.peer[k]) cudaIpcCloseMemHandle(c->d.peer[k]);
   if (c->base) cudaFree(c->base);
@@ -1445,9 +1570,50 @@ int mtp_comm_status(mtp_comm *c, int *status) {
   return MTP_OK;
 }
 
+int mtp_comm_set_trace(mtp_comm *c, int records) {
+  MTP_REQUIRE(c && records >= 0, "bad arguments");
+  if (c->d.trace) {
+    cudaDeviceSynchronize();
+    cudaFree(c->d.trace);
+    c->d.trace = nullptr;
+    c->d.trace_count = nullptr;
+    c->d.trace_cap = 0;
+  }
+  if (records == 0) return MTP_OK;
+  const size_t bytes = (size_t)records * TRACE_WORDS * 8 + 16;
+  void *p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return fail(MTP_ERR_CUDA, "cudaMalloc of the trace buffer failed");
+  cudaMemset(p, 0, bytes);
+  c->d.trace = static_cast<unsigned long long *>(p);
+  c->d.trace_count = reinterpret_cast<unsigned int *>(static_cast<char *>(p) + (size_t)records * TRACE_WORDS * 8);
+  c->d.trace_cap = records;
+  return cudaDeviceSynchronize() == cudaSuccess ? MTP_OK : fail(MTP_ERR_CUDA, "trace set-up failed");
+}
+
+int mtp_comm_read_trace(mtp_comm *c, uint64_t *out, int capacity, int *n_records) {
+  MTP_REQUIRE(c && out && n_records && c->d.trace, "tracing is off or bad arguments");
+  unsigned int cnt[2] = {0, 0};
+  if (cudaMemcpy(cnt, c->d.trace_count, 8, cudaMemcpyDeviceToHost) != cudaSuccess) return fail(MTP_ERR_CUDA, "read trace");
+  int n = (int)(cnt[0] < (unsigned)c->d.trace_cap ? cnt[0] : (unsigned)c->d.trace_cap);
+  if (n * TRACE_WORDS > capacity) n = capacity / TRACE_WORDS;
+  if (n > 0 && cudaMemcpy(out, c->d.trace, (size_t)n * TRACE_WORDS * 8, cudaMemcpyDeviceToHost) != cudaSuccess)
+    return fail(MTP_ERR_CUDA, "read trace");
+  *n_records = n;
+  return MTP_OK;
+}
+
 int mtp_comm_set_max_ctas(mtp_comm *c, int max_ctas) {
   MTP_REQUIRE(c && max_ctas >= 0, "bad arguments");
   c->max_ctas = max_ctas;
+  return MTP_OK;
+}
+
+int mtp_comm_reset_state(mtp_comm *c) {
+  MTP_REQUIRE(c, "null argument");
+  // flags, epochs, exit counters and the status word (everything before the receive slots)
+  if (cudaDeviceSynchronize() != cudaSuccess || cudaMemset(c->base, 0, c->d.off_recv[0]) != cudaSuccess ||
+      cudaDeviceSynchronize() != cudaSuccess)
+    return fail(MTP_ERR_CUDA, "reset of the comm state failed");
   return MTP_OK;
 }
 

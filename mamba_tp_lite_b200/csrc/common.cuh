@@ -64,6 +64,18 @@ __device__ __forceinline__ float softplus_fast(float x) {
 }
 
 
+// softplus with two MUFU operations (ex2, lg2) instead of three: max(x, 0) + log1p(t),
+// t = e^-|x| in (0, 1]; log1p(t) is the hardware log of 1 + t for t >= 2^-12 (absolute
+// error about 6e-8, so relative error <= 2.5e-4 there) and t - t^2/2 below (relative error
+// < 2^-25).  For outputs rounded to bf16 (relative step 2^-8) after the tensor-core GEMMs.
+__device__ __forceinline__ float softplus_bf16out(float x) {
+  const float t = __expf(-fabsf(x));
+  const float small = t * fmaf(-0.5f, t, 1.0f);
+  const float l = __logf(1.0f + t);
+  const float r = fmaxf(x, 0.f) + (t < 2.44140625e-4f ? small : l);
+  return x > 20.f ? x : r;
+}
+
 // SiLU with the hardware exponential and a fast divide, x / (1 + e^-x).
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 

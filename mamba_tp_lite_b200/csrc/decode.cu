@@ -329,9 +329,12 @@ __device__ __forceinline__ void row_push(const DecParams &p, int site, int mode,
       }
     }
   }
-  __threadfence_system();
+  // barrier first, then one system fence per flag-writing thread (not per thread)
   __syncthreads();
-  if (tid < d.ws) st_release_sys(flag_ptr(d.peer[tid], d, site, 0, d.rank, row), epoch);
+  if (tid < d.ws) {
+    __threadfence_system();
+    st_release_sys(flag_ptr(d.peer[tid], d, site, 0, d.rank, row), epoch);
+  }
 }
 
 // Wait for row `row` of every rank (bounded); false on timeout.
@@ -350,8 +353,8 @@ __device__ __forceinline__ bool row_wait(const DecParams &p, int site, int row, 
         break;
       }
     }
+    __threadfence();
   }
-  __threadfence();
   __syncthreads();
   return *s_flag != 0;
 }
@@ -853,6 +856,7 @@ struct mtp_decode_plan {
   unsigned long long *trace_buf = nullptr;
   int n_trace = 0;
   size_t cnt_bytes = 0;
+  size_t lflags_bytes = 0;  // per-row publication flags + local epoch
 };
 
 struct mtp_decode_cache {
@@ -1000,6 +1004,7 @@ int mtp_decode_plan_create(const mtp_decode_layer *layers, int n_layer, const vo
   p.cnt = reinterpret_cast<unsigned *>(base + o_cnt);
   p.ncnt = ncnt;
   P->cnt_bytes = sizeof(unsigned) * ncnt;
+  P->lflags_bytes = (size_t)MB * 4 + 4;
   P->trace_buf = reinterpret_cast<unsigned long long *>(base + o_trace);
   P->n_trace = (int)n_trace;
   p.trace = nullptr;
@@ -1071,7 +1076,9 @@ int mtp_decode_status(mtp_decode_plan *P, int *status) {
 
 int mtp_decode_reset(mtp_decode_plan *P) {
   MTP_REQUIRE(P, "bad arguments");
-  if (cudaMemset(P->bar, 0, 64) != cudaSuccess || cudaMemset(P->p.cnt, 0, P->cnt_bytes) != cudaSuccess)
+  // an aborted step leaves row flags ahead of the local epoch: clear both with the counters
+  if (cudaMemset(P->bar, 0, 64) != cudaSuccess || cudaMemset(P->p.cnt, 0, P->cnt_bytes) != cudaSuccess ||
+      cudaMemset(P->p.lflags, 0, P->lflags_bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess)
     return fail(MTP_ERR_CUDA, "reset of the decode counters failed");
   return MTP_OK;
 }

@@ -6,9 +6,10 @@
 //   warp 1      allocates 512 TMEM columns (two 128 x bn fp32 accumulators) and one lane issues
 //               tcgen05.mma (kind::f16, M=128, N=bn, K=16 per instruction), releasing ring slots
 //               and signalling finished accumulators with tcgen05.commit;
-//   warps 2-9   epilogue: two warps per TMEM lane quarter, alternating 16-column chunks;
-//               tcgen05.ld 32 lanes x 16 columns, fused epilogue op, stores; overlaps the next
-//               tile's MMAs thanks to the second accumulator.
+//   warps 2-13  epilogue: three warps per TMEM lane quarter, alternating 16-column chunks;
+//               tcgen05.ld 32 lanes x 16 columns, fused epilogue op, then the 32 x 16 chunk is
+//               staged in shared memory and written by a TMA store (or, with unaligned C,
+//               stored directly); overlaps the next tile's MMAs thanks to the second accumulator.
 // Every mbarrier wait is bounded (globaltimer); on expiry the CTA records MTP_ERR_TIMEOUT in a
 // device word, drains its in-flight copies and MMAs with bounded waits, frees TMEM and returns.
 #include <cuda.h>
@@ -27,6 +28,10 @@ constexpr int EPI_PARTS = NUM_EPI_WARPS / 4;  // warps sharing a lane quarter sp
 constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+// Epilogue staging for TMA stores: per epilogue warp two 32-row x 16-column bf16 chunks
+// (double buffer) or one fp32 chunk, 2 KB, after the barrier block.
+constexpr int STAGE_C_BYTES = 2048;
+constexpr int SMEM_BYTES_TMA_STORE = SMEM_BYTES + NUM_EPI_WARPS * STAGE_C_BYTES;
 
 struct Params {
   void *C;
@@ -37,7 +42,8 @@ struct Params {
   int c_dtype, epi, bias_dtype;
   int bn, tiles_m, tiles_n, num_tiles, group_m;
   uint32_t idesc;
-  int vec_ok;  // 16-byte vector stores allowed
+  int vec_ok;     // 16-byte vector stores allowed
+  int tma_store;  // the epilogue stages 32 x 16 chunks in shared memory and writes them with TMA
 };
 
 __device__ __forceinline__ void tile_coords(const Params &p, int t, int &mt, int &nt) {
@@ -63,6 +69,20 @@ __device__ __forceinline__ void load_bias16(const Params &p, int n0, float (&b)[
       const float4 v = __ldg(bp + i);
       b[4 * i] = v.x; b[4 * i + 1] = v.y; b[4 * i + 2] = v.z; b[4 * i + 3] = v.w;
     }
+  } else if (p.bias_dtype == MTP_BF16 && n0 + 16 <= p.N &&
+             (reinterpret_cast<uintptr_t>((const __nv_bfloat16 *)p.bias + n0) & 15) == 0) {
+    const uint4 *bp = reinterpret_cast<const uint4 *>((const __nv_bfloat16 *)p.bias + n0);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const uint4 u = __ldg(bp + i);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[k]));
+        b[8 * i + 2 * k] = f.x;
+        b[8 * i + 2 * k + 1] = f.y;
+      }
+    }
   } else {
 #pragma unroll
     for (int i = 0; i < 16; ++i) b[i] = (n0 + i < p.N) ? load_bias(p, n0 + i) : 0.f;
@@ -70,16 +90,10 @@ __device__ __forceinline__ void load_bias16(const Params &p, int n0, float (&b)[
 }
 
 // Apply the epilogue to 16 accumulator columns [n0, n0+16) of row `row` and store.
+__device__ __forceinline__ void epilogue_op(const Params &p, float (&v)[16], const float (&b)[16]);
+
 __device__ __forceinline__ void epilogue_store(const Params &p, int row, int n0, float (&v)[16], const float (&b)[16]) {
-  if (p.epi == MTP_EPI_BIAS_SOFTPLUS) {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      v[i] = softplus_fast(v[i] + b[i]);
-    }
-  } else if (p.epi == MTP_EPI_BIAS) {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] += b[i];
-  }
+  epilogue_op(p, v, b);
   if (row >= p.M) return;
   const bool full = p.vec_ok && (n0 + 16 <= p.N);
   if (p.c_dtype == MTP_F32) {
@@ -111,8 +125,54 @@ __device__ __forceinline__ void epilogue_store(const Params &p, int row, int n0,
   }
 }
 
+// The epilogue op (bias / softplus) without the store.  A bf16 output is rounded to 8
+// bits of mantissa, so its softplus takes the two-MUFU form.
+__device__ __forceinline__ void epilogue_op(const Params &p, float (&v)[16], const float (&b)[16]) {
+  if (p.epi == MTP_EPI_BIAS_SOFTPLUS) {
+    if (p.c_dtype == MTP_BF16) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = softplus_bf16out(v[i] + b[i]);
+      return;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = softplus_fast(v[i] + b[i]);
+  } else if (p.epi == MTP_EPI_BIAS) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] += b[i];
+  }
+}
+
+// Row `lane` of a 32 x 16 staging chunk (row-major, 16 values per row) from registers.
+__device__ __forceinline__ void stage_row(const Params &p, unsigned char *buf, int lane, const float (&v)[16]) {
+  if (p.c_dtype == MTP_F32) {
+    float4 *o = reinterpret_cast<float4 *>(buf + (size_t)lane * 64);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  } else {
+    uint32_t w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+      w[i] = *reinterpret_cast<uint32_t *>(&h2);
+    }
+    uint4 *o = reinterpret_cast<uint4 *>(buf + (size_t)lane * 32);
+    o[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    o[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
+}
+
+// TMA store of a staged 32 x 16 chunk to C[m0 .. m0+31][n0 .. n0+15] (rows and columns
+// outside C are clipped by the copy); one bulk group per chunk.
+__device__ __forceinline__ void tma_store_chunk(const CUtensorMap *tm, uint32_t src, int n0, int m0) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tm), "r"(src),
+               "r"(n0), "r"(m0)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC, const Params p) {
   extern __shared__ __align__(1024) unsigned char smem_dyn[];
   const uint32_t raw = smem_u32(smem_dyn);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -226,9 +286,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------------------ epilogue (warps 2..9)
+    // ------------------------------------------------------------ epilogue (warps 2..13)
     const int q = warp & 3;              // TMEM lane quarter this warp may access
     const int part = (warp - 2) >> 2;    // chunks part, part + EPI_PARTS, ... of the lane quarter
+    // TMA-store staging: this warp's 2 KB (two bf16 chunks or one fp32 chunk)
+    unsigned char *stage_c = gbase + STAGES * STAGE_BYTES + 256 + (size_t)(warp - 2) * STAGE_C_BYTES;
+    const bool dbl = p.c_dtype != MTP_F32;
+    int cidx = 0;
+    auto emit = [&](int mt, int n0, float (&v)[16], const float (&b)[16]) {
+      const int row = mt * BM + q * 32 + lane;
+      if (!p.tma_store) {
+        epilogue_store(p, row, n0, v, b);
+        return;
+      }
+      epilogue_op(p, v, b);
+      const int m0 = mt * BM + q * 32;
+      unsigned char *buf = stage_c + (dbl ? (cidx & 1) * 1024 : 0);
+      ++cidx;
+      // the store that last read this buffer must have finished reading it
+      if (lane == 0) {
+        if (dbl) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+        else asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      }
+      __syncwarp();
+      stage_row(p, buf, lane, v);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> async proxy
+      __syncwarp();
+      if (lane == 0 && m0 < p.M) tma_store_chunk(&tmC, smem_u32(buf), n0, m0);
+    };
     int local = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
       const int a = local & 1;
@@ -237,7 +322,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       int mt, nt;
       tile_coords(p, t, mt, nt);
-      const int row = mt * BM + q * 32 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN_MAX);
       // this warp's 16-column chunks are j, j + 16 EPI_PARTS, ...: two per TMEM wait
       constexpr int CS = 16 * EPI_PARTS;
@@ -255,13 +339,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         } else {
           tmem_ld16(tbase + (uint32_t)j, v);
         }
-        if (n0 < p.N) epilogue_store(p, row, n0, v, b);
-        if (two && n0 + CS < p.N) epilogue_store(p, row, n0 + CS, v2, b2);
+        if (n0 < p.N) emit(mt, n0, v, b);
+        if (two && n0 + CS < p.N) emit(mt, n0 + CS, v2, b2);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(a));
     }
+    // every TMA store of this warp has completed before the CTA exits
+    if (p.tma_store && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
@@ -319,18 +406,30 @@ int gemm_tc(const void *A, const void *B, void *C, int M, int N, int K, int lda,
   p.timeout_ns = 2000000000ull;
   p.err = device_err_word();
   if (!p.err) return fail(MTP_ERR_CUDA, "could not allocate the GEMM status word");
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tcm;
   int rc = make_tmap(&ta, A, M, K, lda, BM);
   if (rc) return rc;
   rc = make_tmap(&tb, B, N, K, ldb, p.bn);
   if (rc) return rc;
+  // epilogue through shared memory and TMA stores (MTP_GEMM_TMA_STORE=0: direct stores)
+  static const bool tma_store_on = [] {
+    const char *e = getenv("MTP_GEMM_TMA_STORE");
+    return !(e && e[0] == '0');
+  }();
+  p.tma_store = tma_store_on && p.vec_ok && N >= 16 && M >= 32;
+  memset(&tcm, 0, sizeof(tcm));
+  if (p.tma_store) {
+    rc = make_tmap_c(&tcm, C, M, N, ldc, c_dtype);
+    if (rc) return rc;
+  }
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES_TMA_STORE);
     attr = true;
   }
   const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
-  launch_pdl(gemm_tc_kernel, dim3(grid), dim3(NUM_THREADS), SMEM_BYTES, stream, ta, tb, p);
+  launch_pdl(gemm_tc_kernel, dim3(grid), dim3(NUM_THREADS), p.tma_store ? SMEM_BYTES_TMA_STORE : SMEM_BYTES, stream,
+             ta, tb, tcm, p);
   return check_launch("gemm_tc");
 }
 

@@ -144,6 +144,25 @@ inline int make_tmap(CUtensorMap *tm, const void *ptr, int rows, int cols, int l
 }
 
 
+// 2-D tensor map for the TMA stores of a GEMM epilogue: row-major [rows, cols] of bf16 or
+// fp32 with leading dimension ld (elements); box 16 columns x 32 rows, no swizzle (the
+// staging chunk is plain row-major).  Base 16-byte aligned and ld * element size a multiple
+// of 16 bytes (the caller checks).
+inline int make_tmap_c(CUtensorMap *tm, const void *ptr, int rows, int cols, int ld, int dtype) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(MTP_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const size_t es = dtype == MTP_F32 ? 4 : 2;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * es};
+  cuuint32_t box[2] = {16u, 32u};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(tm, dtype == MTP_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                  const_cast<void *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MTP_ERR_ARG, "cuTensorMapEncodeTiled (C) failed with code " + std::to_string((int)r));
+  return MTP_OK;
+}
+
 // Instruction descriptor of tcgen05.mma kind::f16 with bf16 A/B, fp32 D, both K-major.
 constexpr uint32_t idesc_bf16(int m, int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);

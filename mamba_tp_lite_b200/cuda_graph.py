@@ -34,7 +34,7 @@ def _spec_names(spec) -> set:
 class GraphedStepper:
     """Captures ``model.step(static_ids, cache)`` once, then replays it."""
 
-    def __init__(self, model, cache, batch_size: int, device: str, n_warmup: int = 3):
+    def __init__(self, model, cache, batch_size: int, device: str, n_warmup: int = 3, greedy: bool = False):
         if str(device) not in ("cuda",) and not str(device).startswith("cuda") or not torch.cuda.is_available():
             raise CUDAGraphUnsupported("CUDA graphs require a CUDA device; there is no CPU path.")
         names = _spec_names(getattr(model, "allreduce_dtype", "fp32"))
@@ -47,6 +47,8 @@ class GraphedStepper:
         self.device = device
         self.static_ids = torch.zeros((batch_size, 1), dtype=torch.long, device=device)
         self.static_logits = None
+        self.static_next = None  # with greedy=True: argmax of the captured step's logits [b, 1]
+        self.greedy = greedy
         self.graph = None
         self.n_warmup = n_warmup
 
@@ -66,6 +68,8 @@ class GraphedStepper:
         try:
             with torch.cuda.graph(self.graph), torch.no_grad():
                 self.static_logits = self.model.step(self.static_ids, self.cache)
+                if self.greedy:  # device argmax in the same graph: no host round trip per token
+                    self.static_next = self.model.greedy_next(self.static_logits)
         except RuntimeError as e:
             self.graph = None
             raise CUDAGraphUnsupported(f"CUDA graph capture failed: {e}") from e
@@ -75,7 +79,17 @@ class GraphedStepper:
         self.graph.replay()
         return self.static_logits
 
+    def replay_greedy(self) -> torch.Tensor:
+        """Greedy decoding on the device: feeds the previous replay's argmax back as the
+        next ids and replays; returns the aliased [b, 1] argmax of this step."""
+        if self.static_next is None:
+            raise RuntimeError("capture with greedy=True first")
+        self.static_ids.copy_(self.static_next)
+        self.graph.replay()
+        return self.static_next
+
     def release(self) -> None:
         """Drops the graph (before destroying process groups)."""
         self.graph = None
         self.static_logits = None
+        self.static_next = None

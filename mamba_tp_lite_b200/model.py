@@ -28,23 +28,32 @@ __all__ = ["MambaConfig", "load_hf_state_dict", "LayerCache", "MambaCache", "RMS
            "MambaLM"]
 
 
-def load_hf_state_dict(hf_path: str) -> dict[str, torch.Tensor]:
-    """All tensors of a single-file or sharded (``model.safetensors.index.json``)
-    HF checkpoint directory (model.py:28-47)."""
-    from safetensors.torch import load_file
-
+def _checkpoint_files(hf_path: str) -> list[str]:
+    """The safetensors files of a checkpoint directory: the single ``model.safetensors``,
+    else every shard an ``model.safetensors.index.json`` maps a tensor to."""
     single = os.path.join(hf_path, "model.safetensors")
-    index = os.path.join(hf_path, "model.safetensors.index.json")
     if os.path.exists(single):
-        return load_file(single)
-    if os.path.exists(index):
-        with open(index) as f:
-            weight_map = json.load(f)["weight_map"]
-        sd = {}
-        for shard in sorted(set(weight_map.values())):
-            sd.update(load_file(os.path.join(hf_path, shard)))
-        return sd
-    raise FileNotFoundError(f"no model.safetensors or model.safetensors.index.json under {hf_path}")
+        return [single]
+    index = os.path.join(hf_path, "model.safetensors.index.json")
+    if not os.path.exists(index):
+        raise FileNotFoundError(f"{hf_path}: neither model.safetensors nor model.safetensors.index.json exists")
+    with open(index) as f:
+        shards = set(json.load(f)["weight_map"].values())
+    return [os.path.join(hf_path, name) for name in sorted(shards)]
+
+
+def load_hf_state_dict(hf_path: str) -> dict[str, torch.Tensor]:
+    """Every tensor of an HF Mamba checkpoint directory by name, as model.py:28-47 returns
+    them (same keys and values; FileNotFoundError when the directory holds no
+    checkpoint).  Tensors are read through safetensors' file handles one at a time."""
+    from safetensors import safe_open
+
+    tensors: dict[str, torch.Tensor] = {}
+    for path in _checkpoint_files(hf_path):
+        with safe_open(path, framework="pt") as handle:
+            for name in handle.keys():
+                tensors[name] = handle.get_tensor(name)
+    return tensors
 
 
 @dataclass
@@ -345,11 +354,24 @@ class _LMKernels:
         return out
 
     @torch.no_grad()
-    def generate(self, input_ids: torch.Tensor, max_new_tokens: int, greedy: bool = True):
-        """Prefill, then greedy decode through the cache (model.py:355-365)."""
+    def generate(self, input_ids: torch.Tensor, max_new_tokens: int, greedy: bool = True, graphed: bool = False):
+        """Prefill, then greedy decode through the cache (model.py:355-365).  With
+        graphed=True the decode steps replay one CUDA graph holding the step and the
+        device argmax, each replay fed by the previous one's token: no host
+        synchronisation per token, and the same tokens as the eager loop."""
         logits, cache = self.prefill(input_ids)
         next_id = self.greedy_next(logits)
         tokens = [input_ids, next_id]
+        if graphed and max_new_tokens > 1:
+            from .cuda_graph import GraphedStepper
+
+            st = GraphedStepper(self, cache, input_ids.shape[0], str(input_ids.device), greedy=True)
+            st.capture()
+            st.static_next.copy_(next_id)
+            for _ in range(max_new_tokens - 1):
+                tokens.append(st.replay_greedy().clone())
+            st.release()
+            return torch.cat(tokens, dim=1)
         for _ in range(max_new_tokens - 1):
             logits = self.step(next_id, cache)
             next_id = self.greedy_next(logits)

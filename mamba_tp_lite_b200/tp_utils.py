@@ -118,7 +118,7 @@ class Comm:
     def __init__(self, group, rank: int, ws: int, cols_x: int, cols_out: int, max_rows: int | None = None,
                  timeout_s: float | None = None):
         self.rank, self.ws = rank, ws
-        self.max_rows = max_rows or int(os.environ.get("MTP_COMM_MAX_ROWS", "8192"))
+        self.max_rows = max_rows or int(os.environ.get("MTP_COMM_MAX_ROWS", "32768"))
         timeout_s = timeout_s if timeout_s is not None else float(os.environ.get("MTP_COMM_TIMEOUT_S", "60"))
         h = C.c_void_p()
         L.call("mtp_comm_create", rank, ws, self.max_rows, cols_x, cols_out, float(timeout_s), C.byref(h))
@@ -142,6 +142,11 @@ class Comm:
 
     def reset_status(self) -> None:
         L.call("mtp_comm_reset_status", self.handle)
+
+    def reset_state(self) -> None:
+        """After a timeout: zeroes flags, epochs and status (every rank, nothing in flight,
+        then a host barrier); see mtp_comm_reset_state."""
+        L.call("mtp_comm_reset_state", self.handle)
 
     def set_max_ctas(self, max_ctas: int) -> None:
         """Caps the grid of this context's reductions (0: default); see mtp_comm_set_max_ctas."""

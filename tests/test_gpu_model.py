@@ -178,6 +178,22 @@ def test_graphed_decode_bit_exact_vs_eager(dtype):
     st.release()
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("batch", [1, 3])
+def test_graphed_greedy_generate_equals_eager(dtype, batch):
+    """generate(graphed=True): step + device argmax in one CUDA graph, each replay fed by
+    the previous token on the device -- the same greedy tokens as the eager loop
+    (model.py:355-365)."""
+    cfg = MambaConfig(d_model=128, n_layer=2, vocab_size=512, dt_rank=8)
+    sd = random_init_state_dict(cfg, seed=4, dtype=dtype)
+    m = TPMambaLM.from_state_dict_shard(cfg, sd, 0, 1, dtype=dtype, allreduce_dtype="int8", device=dev())
+    ids = torch.randint(0, cfg.vocab_size, (batch, 12), generator=torch.Generator().manual_seed(8)).to(dev())
+    eager = m.generate(ids, 20)
+    graphed = m.generate(ids, 20, graphed=True)
+    assert eager.shape == (batch, 12 + 20)
+    assert torch.equal(eager, graphed)
+
+
 def test_launch_counter_counts_library_kernels():
     cfg, _, m = _small_model()
     ids = torch.zeros(1, 4, dtype=torch.long, device=dev())

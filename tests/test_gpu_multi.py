@@ -159,8 +159,11 @@ def _suite(rank, init_file, q, ws):
         comm = get_comm(None, rank, ws, 48, d)
         part = torch.randn(rows, d, generator=torch.Generator().manual_seed(7 + rank)).cuda() * 2
         w = torch.randn(d, generator=torch.Generator().manual_seed(9)).cuda().to(torch.bfloat16)
-        for proto in ("oneshot", "twoshot", "capped"):
+        chunk = (rows + ws - 1) // ws  # rows [rank * chunk, (rank + 1) * chunk) are this rank's
+        own = slice(rank * chunk, min(rows, (rank + 1) * chunk))
+        for proto in ("oneshot", "twoshot", "capped", "sp"):
             os.environ["MTP_COMM_PROTOCOL"] = "oneshot" if proto == "capped" else proto
+            os.environ["MTP_COMM_SP"] = "1" if proto == "sp" else "0"
             comm.set_max_ctas(16 if proto == "capped" else 0)
             for mode in (L.RED_FP32, L.RED_FP16, L.RED_INT8TOK):
                 resid = torch.ones(rows, d, device="cuda")
@@ -168,9 +171,12 @@ def _suite(rank, init_file, q, ws):
                 L.call("mtp_reduce_outproj", comm.ptr, mode, L.ptr(part), rows, d, None, L.ptr(resid), L.ptr(w),
                        1e-5, L.ptr(normed), L.BF16, L.stream_ptr())
                 torch.cuda.synchronize()
-                out["proto"][(proto, mode)] = (_digest(resid.cpu().numpy()), _digest(normed.float().cpu().numpy()))
+                r_np = resid.cpu().numpy()
+                out["proto"][(proto, mode)] = (_digest(r_np), _digest(normed.float().cpu().numpy()),
+                                               _digest(r_np[own]))
         comm.set_max_ctas(0)
         os.environ.pop("MTP_COMM_PROTOCOL")
+        os.environ.pop("MTP_COMM_SP")
         comm.check()
         # ---- overlapped micro-batch prefill == serial prefill
         sd = random_init_state_dict(cfg, seed=8, dtype=torch.bfloat16)
@@ -280,7 +286,13 @@ def test_two_shot_bf16_gather_equals_one_shot(ws):
         assert res[0]["proto"][("capped", mode)] == a, mode  # 16 CTAs, low-register kernel: same bits
         for r in range(1, ws):
             for proto in ("oneshot", "twoshot", "capped"):
-                assert res[r]["proto"][(proto, mode)] == a, (r, proto, mode)
+                assert res[r]["proto"][(proto, mode)][:2] == a[:2], (r, proto, mode)
+        # sequence-parallel epilogue: the same normed bits on every rank, and each rank's
+        # residual rows equal the full epilogue's on the rows it owns
+        for r in range(ws):
+            sp, full = res[r]["proto"][("sp", mode)], res[r]["proto"][("oneshot", mode)]
+            assert sp[1] == a[1], (r, mode)
+            assert sp[2] == full[2], (r, mode)
 
 
 # ------------------------------------------------------------------ overlapped micro-batch prefill == serial prefill
@@ -367,11 +379,23 @@ def _decode_timeout_worker(rank, init_file, q, ws):
             m.step(torch.zeros(2, 1, dtype=torch.long, device="cuda"), cache)
             torch.cuda.synchronize()
             result = (m._mtp_decode.status(), comm.status(), time.time() - t0)
-            m._mtp_decode.reset()
-            comm.reset_status()
             assert (torch.ones(8, device="cuda") * 2).sum().item() == 16  # context still usable
+        # recovery: both ranks reset the decode plan and the comm context, then meet
         dist.barrier()
-        q.put((rank, result))
+        comm = get_comm(None, rank, ws, cfg.dt_rank + 2 * cfg.d_state, cfg.d_model)
+        m._mtp_decode.reset()
+        comm.reset_state()
+        dist.barrier()
+        # a decode step (persistent kernel, peer reductions) and a plain reduction now succeed
+        _, cache = m.prefill(ids)
+        step = m.step(torch.zeros(2, 1, dtype=torch.long, device="cuda"), cache).float().cpu().numpy()
+        from mamba_tp_lite_b200 import _lib as L
+        x = torch.full((64, 64), float(rank + 1), device="cuda")
+        y = torch.empty_like(x)
+        L.call("mtp_allreduce", comm.ptr, 1, L.RED_FP32, L.ptr(x), L.ptr(y), 64, 64, L.stream_ptr())
+        torch.cuda.synchronize()
+        after = (m._mtp_decode.status(), comm.status(), float(y[0, 0]), step)
+        q.put((rank, (result, after)))
         _finish()
     except Exception as e:
         q.put((rank, f"{type(e).__name__}: {e}"))
@@ -382,7 +406,13 @@ def test_decode_kernel_with_absent_peer_times_out_with_status():
     from mamba_tp_lite_b200 import _lib as L
 
     res = _spawn(_decode_timeout_worker, 2)
-    plan_status, comm_status, elapsed = res[0]
+    plan_status, comm_status, elapsed = res[0][0]
     assert plan_status == L.MTP_ERR_TIMEOUT and comm_status == L.MTP_ERR_TIMEOUT
     assert 0.5 < elapsed < 30
-    assert res[1] == (0, 0, 0.0)
+    assert res[1][0] == (0, 0, 0.0)
+    # after mtp_decode_reset + mtp_comm_reset_state on every rank: clean statuses, the
+    # reduction sums both ranks, and the decode step is identical on both ranks
+    for r in (0, 1):
+        p_st, c_st, red, _ = res[r][1]
+        assert p_st == 0 and c_st == 0 and red == 3.0, (r, res[r][1][:3])
+    assert np.array_equal(res[0][1][3], res[1][1][3])

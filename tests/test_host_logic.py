@@ -130,6 +130,61 @@ def test_from_pretrained_shard_slices_like_reference(ws, sharded_files):
             np.testing.assert_array_equal(m.embedding.weight.detach().numpy(), osd["backbone.embeddings.weight"])
 
 
+@pytest.mark.parametrize("sharded_files", [False, True])
+def test_load_hf_state_dict_reads_every_tensor(sharded_files):
+    """model.load_hf_state_dict returns every tensor of a single-file or sharded
+    checkpoint with its values (model.py:28-47) and raises FileNotFoundError on a
+    directory without one."""
+    from mamba_tp_lite_b200.model import load_hf_state_dict
+
+    cfg = MambaConfig(d_model=64, n_layer=2, vocab_size=120, dt_rank=8)
+    with tempfile.TemporaryDirectory() as d:
+        sd = random_init_state_dict(cfg, seed=0)
+        make_random_checkpoint(d, cfg, seed=0, max_shard_bytes=200_000 if sharded_files else None)
+        got = load_hf_state_dict(d)
+        assert set(got) == set(sd)
+        for k, v in sd.items():
+            assert torch.equal(got[k], v), k
+    with tempfile.TemporaryDirectory() as empty:
+        with pytest.raises(FileNotFoundError):
+            load_hf_state_dict(empty)
+
+
+def test_checkpoint_written_by_layer_loads_per_rank():
+    """The per-layer checkpoint writer (never holds the whole model) gives the values of
+    random_init_state_dict, and from_pretrained_shard slices it per rank."""
+    from mamba_tp_lite_b200.checkpoint import write_random_checkpoint_by_layer
+    from mamba_tp_lite_b200.model import load_hf_state_dict
+
+    cfg = MambaConfig(d_model=64, n_layer=3, vocab_size=120, dt_rank=8)
+    sd = random_init_state_dict(cfg, seed=5, dtype=torch.bfloat16)
+    with tempfile.TemporaryDirectory() as d:
+        write_random_checkpoint_by_layer(d, cfg, seed=5, dtype=torch.bfloat16)
+        assert os.path.exists(os.path.join(d, "model.safetensors.index.json"))
+        got = load_hf_state_dict(d)
+        assert set(got) == set(sd) and all(torch.equal(got[k], sd[k]) for k in sd)
+        osd = O.state_dict_numpy(sd)
+        for r in range(2):
+            m = TPMambaLM.from_pretrained_shard(d, r, 2, dtype=torch.bfloat16, device="cpu")
+            want = O.shard_mixer(O.mixer_params(osd, 1), r, 2)
+            np.testing.assert_array_equal(m.layers[1].mixer.out_proj.weight.detach().float().numpy(), want["out_proj.weight"])
+
+
+def test_quant_metrics_match_oracle():
+    """quant_eval.quant_metrics against the oracle's restatement of quant_eval.py:48-60."""
+    from mamba_tp_lite_b200.quant_eval import quant_metrics, summarize
+
+    g = torch.Generator().manual_seed(3)
+    ref = torch.randn(3, 17, 50, generator=g)
+    q = ref + 0.3 * torch.randn(3, 17, 50, generator=g)
+    got = quant_metrics(ref, q)
+    want = O.quant_metrics(ref.numpy(), q.numpy())
+    for k in ("kl", "top1", "top5_ordered", "top5_unordered"):
+        np.testing.assert_allclose(got[k].numpy(), np.asarray(want[k]), rtol=1e-5, atol=1e-6, err_msg=k)
+    s = summarize(got)
+    assert abs(s["top1"]["mean"] - float(got["top1"].mean())) < 1e-12
+
+
 def test_load_shard_from_dense_correct_and_naive():
     cfg = MambaConfig(d_model=32, n_layer=1, vocab_size=64, d_state=8)
     torch.manual_seed(0)

@@ -18,7 +18,8 @@ def _reference_path(mode, x, rows, cols):
 
 
 @pytest.mark.parametrize("mode", [L.RED_FP32, L.RED_FP16, L.RED_INT8TOK])
-@pytest.mark.parametrize("rows,cols", [(37, 18), (300, 2050), (4096, 160)])
+# the last two bind the grid to the fixed scratch: 1 CTA (8 rows per warp) and 2 CTAs
+@pytest.mark.parametrize("rows,cols", [(37, 18), (300, 2050), (4096, 160), (64, 131072), (300, 65536)])
 def test_noalloc_matches_allocating_entry_point_twice(mode, rows, cols):
     assert torch.cuda.is_available()
     outs = []
