@@ -69,10 +69,12 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
     if failed:
         raise RuntimeError(f"nvcc failed for {failed}")
     if force or _stale(LIB, objs):
-        cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcuda"] * 0
+        tmp = LIB + ".tmp"  # link beside, then rename: a reader never sees a half-written library
+        cmd = [nvcc()] + ARCH + ["-shared", "-o", tmp] + objs
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.check_call(cmd)
+        os.replace(tmp, LIB)
     return LIB
 
 

@@ -1055,7 +1055,7 @@ __device__ __forceinline__ void signal_rounds(const CommDev &d, int site, int pa
 // [k rpw, (k+1) rpw).  One-shot: a round's wire rows go to every rank and are reduced one
 // round later, after every rank's flag for that round -- so the NVLink transfer of round
 // k overlaps the reduce and epilogue of round k-1.  Two-shot: round k's wire rows go to
-// their owner rank (rows split in ws contiguous chunks); one round later the owner reduces
+// their owner rank (rows round-robin over the ranks); one round later the owner reduces
 // them and pushes the rounded result rows to every rank's gather buffer; one round after
 // that every rank runs the epilogue.  Every rank reduces in rank order, so all ranks hold
 // the same bits.  Flag values grow with the round; every wait is bounded.
@@ -1106,7 +1106,10 @@ __global__ void __launch_bounds__(WPB * 32, Ops::MINB) reduce_pipe_kernel(CommDe
   };
   const size_t half = (size_t)(epoch & 1u) * d.ws * d.slot_bytes[site];
   const uint32_t all = (1u << d.ws) - 1u;
-  const int chunk = (rows + d.ws - 1) / d.ws;
+  // two-shot ownership: rows round-robin over the ranks, so in every round each CTA's
+  // warps hold rows of every owner and each rank does 1/ws of the owner work of the round
+  // (contiguous row chunks would give each round's rows to one or two ranks)
+  auto owner_of = [&](int r) { return r % d.ws; };
   const size_t my_slot = d.off_recv[site] + half + (size_t)d.rank * d.slot_bytes[site];
   char *slots[MAX_WS];
   for (int k = 0; k < d.ws; ++k) slots[k] = d.peer[d.rank] + d.off_recv[site] + half + (size_t)k * d.slot_bytes[site];
@@ -1134,7 +1137,7 @@ __global__ void __launch_bounds__(WPB * 32, Ops::MINB) reduce_pipe_kernel(CommDe
       Ops::load(partial + (size_t)r * cols, cols, lane, R);
       const float sc = MODE == MTP_RED_INT8TOK ? row_scale(Ops::amax(R)) : 0.f;
       if (two_shot) {
-        Ops::wire(d.peer[r / chunk] + my_slot, R, r, rows, cols, lane, sc);
+        Ops::wire(d.peer[owner_of(r)] + my_slot, R, r, rows, cols, lane, sc);
       } else {
         for (int q = 0; q < d.ws; ++q) Ops::wire(d.peer[(d.rank + q) % d.ws] + my_slot, R, r, rows, cols, lane, sc);
       }
@@ -1171,7 +1174,7 @@ __global__ void __launch_bounds__(WPB * 32, Ops::MINB) reduce_pipe_kernel(CommDe
       stamp();
       for (int i = 0; i < rpw; ++i) {
         const int sl = (k - 1) * rpw + i, r = row_of(sl);
-        if (sl >= S || r >= rows || r / chunk != d.rank) continue;
+        if (sl >= S || r >= rows || owner_of(r) != d.rank) continue;
         Ops::reduce(slots, d.ws, r, rows, cols, lane, R);
         Ops::round(R, e.rdt);
         if constexpr (Ops::EPI == EPI_OUTPROJ) {
@@ -1317,6 +1320,16 @@ static int pipe_occupancy() {
   return occ;
 }
 
+// Target rounds per reduction launch: MTP_COMM_ROUNDS_X (x_proj site, default 1) and
+// MTP_COMM_ROUNDS_OUT (out_proj site and plain reductions, default 1).  Each extra round
+// costs a fence and a flag round trip; on B200 one round was fastest at every size measured
+// ([32768, 160] and [32768, 2048] at 2 and 4 ranks: +10 to +40% per doubling of rounds).
+static int pipe_rounds(int epi) {
+  const char *e = getenv(epi == EPI_XPROJ ? "MTP_COMM_ROUNDS_X" : "MTP_COMM_ROUNDS_OUT");
+  const int v = e ? atoi(e) : 0;
+  return v > 0 && v <= 64 ? v : 1;
+}
+
 template <class Ops>
 static void launch_pipe(const CommDev &d, bool has_comm, int site, const float *pp, int nr, int cols, bool two_shot,
                         bool sp, const EpiOut &e, int sms, cudaStream_t s) {
@@ -1324,9 +1337,10 @@ static void launch_pipe(const CommDev &d, bool has_comm, int site, const float *
   int cap = has_comm ? sms * pipe_occupancy<Ops>() : sms * 8;
   if (has_comm && cap > G_MAX) cap = G_MAX;
   const int G = Gwant < cap ? Gwant : cap;
-  // rows per warp per round: about 8 rounds per launch (each round costs a fence and a flag)
+  // rows per warp per round from the target number of rounds (each round costs a fence and
+  // a flag round trip between the ranks; more rounds overlap more NVLink with HBM work)
   const int slices = ceil_div(nr, G * WPB);
-  const int rpw = ceil_div(slices, 8);
+  const int rpw = ceil_div(slices, pipe_rounds(Ops::EPI));
   launch_pdl(reduce_pipe_kernel<Ops>, dim3(G), dim3(WPB * 32), 0, s, d, has_comm, site, pp, nr, cols, two_shot, sp, rpw,
              e);
 }
@@ -1410,12 +1424,13 @@ static int run_reduce(mtp_comm *c, int site, int mode, const float *partial, int
     // sequence-parallel out_proj epilogue: each row's owner rank applies the residual and
     // the next RMSNorm and every rank gathers the normed rows (the residual rows of other
     // owners are then not kept on this rank); needs the normed output and the two-shot
-    // protocol, which it implies.  MTP_COMM_SP=0 turns it off, =1 forces it at 2 ranks.
+    // protocol, which it implies.  B200, [32768, 2048] int8 / fp16: 338 / 472 us at 2 ranks
+    // (one-shot 366 / 634), 409 / 641 us at 4 (two-shot without it 453 / 684).
+    // MTP_COMM_SP=0 turns it off.
     bool sp = EPI == EPI_OUTPROJ && has_comm && ee.normed != nullptr && !capped;
     if (sp) {
       const char *env = getenv("MTP_COMM_SP");
       if (env && !strcmp(env, "0")) sp = false;
-      else if (c->d.ws < 4 && !(env && !strcmp(env, "1"))) sp = false;
     }
     const bool two_shot = has_comm && (sp || use_two_shot(c->d.ws, mode, nr, cols, e.rdt));
     const float *pp = partial + (size_t)r0 * cols;

@@ -120,6 +120,28 @@ def bench_scan(a):
             "frac_of_hbm": gbs / peaks()["hbm_gbs"], "algorithmic_bytes": nbytes, "Gexp_per_s": exps / (ms / 1e3) / 1e9}
 
 
+def bench_conv(a):
+    """conv1d + SiLU over the x half of in_proj's output (the x_proj input) at the 1.4b TP=1
+    shard: reads x [T, Es] out of xz [T, 2Es], writes xc [T, Es] (bf16)."""
+    B, Lq, es = a.batch, a.seqlen, a.channels
+    T = B * Lq
+    dt_ = torch.bfloat16
+    xz = torch.randn(T, 2 * es, device="cuda", dtype=dt_)
+    w = torch.randn(es, 4, device="cuda", dtype=dt_) * 0.5
+    b = torch.randn(es, device="cuda", dtype=dt_) * 0.5
+    xc = torch.empty(T, es, device="cuda", dtype=dt_)
+
+    def run():
+        L.call("mtp_conv1d_silu", L.ptr(xz), 2 * es, L.ptr(w), L.ptr(b), None, L.ptr(xc), es, B, Lq, es, 4, L.BF16,
+               L.stream_ptr())
+
+    ms = _time(run, a.warmup, a.iters)
+    nbytes = 2 * T * es * 2
+    gbs = nbytes / (ms / 1e3) / 1e9
+    return {"kernel": "conv1d_silu", "B": B, "L": Lq, "Es": es, "avg_ms": ms, "GBps": gbs,
+            "frac_of_hbm": gbs / peaks()["hbm_gbs"], "algorithmic_bytes": nbytes}
+
+
 def bench_step(a):
     B, es, n, R = a.batch, a.channels, 16, a.rank
     dt_ = torch.bfloat16
@@ -307,6 +329,10 @@ def main():
     s.add_argument("--variant", choices=["xc", "raw"], default="xc",
                    help="xc: the scan over the conv output (prefill path); raw: conv inside the scan")
     s.add_argument("--dt", choices=["bf16", "f32"], default="bf16", help="dt element type (unfused scan)")
+    cv = sub.add_parser("conv")
+    cv.add_argument("--batch", type=int, default=32)
+    cv.add_argument("--seqlen", type=int, default=1024)
+    cv.add_argument("--channels", type=int, default=4096)
     st = sub.add_parser("step")
     st.add_argument("--batch", type=int, default=32)
     st.add_argument("--channels", type=int, default=4096)
@@ -325,12 +351,12 @@ def main():
     dcd.add_argument("--layers", type=int, default=0, help="override n_layer (0: the shape's)")
     dcd.add_argument("--batch", type=int, default=1)
     dcd.add_argument("--spec", default="mixed")
-    for p in (g, s, st, r, dcd):
+    for p in (g, s, cv, st, r, dcd):
         p.add_argument("--warmup", type=int, default=3)
         p.add_argument("--iters", type=int, default=10)
     a = ap.parse_args()
     L.load()
-    res = {"gemm": bench_gemm, "scan": bench_scan, "step": bench_step, "allreduce": bench_allreduce,
+    res = {"gemm": bench_gemm, "scan": bench_scan, "conv": bench_conv, "step": bench_step, "allreduce": bench_allreduce,
            "decode": bench_decode}[a.what](a)
     if res is not None:
         print(json.dumps(res), flush=True)

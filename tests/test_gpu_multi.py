@@ -159,8 +159,7 @@ def _suite(rank, init_file, q, ws):
         comm = get_comm(None, rank, ws, 48, d)
         part = torch.randn(rows, d, generator=torch.Generator().manual_seed(7 + rank)).cuda() * 2
         w = torch.randn(d, generator=torch.Generator().manual_seed(9)).cuda().to(torch.bfloat16)
-        chunk = (rows + ws - 1) // ws  # rows [rank * chunk, (rank + 1) * chunk) are this rank's
-        own = slice(rank * chunk, min(rows, (rank + 1) * chunk))
+        own = np.arange(rank, rows, ws)  # the sequence-parallel epilogue's rows of this rank (r % ws)
         for proto in ("oneshot", "twoshot", "capped", "sp"):
             os.environ["MTP_COMM_PROTOCOL"] = "oneshot" if proto == "capped" else proto
             os.environ["MTP_COMM_SP"] = "1" if proto == "sp" else "0"
