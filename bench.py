@@ -345,6 +345,43 @@ def accuracy_vs_fp32(model, ids):
     return out
 
 
+def trace_collectives(model, ids, n_layer: int, rank: int, ws: int):
+    """One untimed prefill with the reductions' phase trace on: per site, the mean over
+    the layers of each rank's kernel time and of the time its CTA 0 spent in bounded
+    flag waits for other ranks (arrival skew between ranks plus the peers' push time),
+    as lists indexed by rank."""
+    import torch
+    import torch.distributed as dist
+
+    from mamba_tp_lite_b200.tp_utils import all_comms
+
+    comms = all_comms()
+    if len(comms) != 1:
+        return None
+    c = comms[0]
+    c.set_trace(2 * n_layer + 8)
+    dist.barrier()
+    model.prefill(ids)
+    torch.cuda.synchronize()
+    recs = c.read_trace()
+    c.set_trace(0)
+    mine = {}
+    for si, site in enumerate(("x_proj", "out_proj")):
+        rs = [r for i, r in enumerate(recs[:2 * n_layer]) if i % 2 == si and r["ctas"]]
+        if rs:
+            mine[site] = (sum(r["ctas"][0]["kernel_us"] for r in rs) / len(rs),
+                          sum(r["ctas"][0]["wait_us"] for r in rs) / len(rs), rs[0]["two_shot"])
+    allr = [None] * ws
+    dist.all_gather_object(allr, mine)
+    out = {}
+    for site in ("x_proj", "out_proj"):
+        if all(site in m for m in allr):
+            out[site] = {"protocol": "two-shot" if allr[0][site][2] else "one-shot",
+                         "kernel_us_by_rank": [round(m[site][0], 1) for m in allr],
+                         "wait_us_by_rank": [round(m[site][1], 1) for m in allr]}
+    return out
+
+
 def run_ours(a):
     import torch
     import torch.distributed as dist
@@ -477,6 +514,11 @@ def run_ours(a):
     # the reductions run between the compute kernels on one stream: all of their time is exposed
     coll_ms = sum(kern[k]["total_ms"] for k in ("reduce_x", "reduce_out") if k in kern) / a.steps
 
+    # ------------------------------------------------ where the collectives wait (TP > 1)
+    comm_trace = None
+    if ws > 1 and not a.no_comm_trace:
+        comm_trace = trace_collectives(model, ids, cfg.n_layer, rank, ws)
+
     # ------------------------------------------------ end to end through the API, host ids
     host_ids = ids.cpu().pin_memory()
     nxt_host = torch.empty(B, 1, dtype=torch.int64).pin_memory()
@@ -501,7 +543,13 @@ def run_ours(a):
     if not a.no_decode:
         # HBM bytes of one decode step on this rank: every weight once (the tied embedding
         # as the lm_head) + per sequence the SSM state (fp32) and conv history read and written
-        w_bytes = sum(p.numel() * p.element_size() for p in model.parameters())
+        # (the lm_head reads only this rank's V / ws embedding rows when it is vocabulary-parallel)
+        emb_bytes = model.embedding.weight.numel() * model.embedding.weight.element_size()
+        w_bytes = sum(p.numel() * p.element_size() for p in model.parameters()) - emb_bytes
+        if model._vocab_parallel_comm(max(a.decode_batches)) is not None:
+            w_bytes += emb_bytes // ws
+        else:
+            w_bytes += emb_bytes
         st_bytes = cfg.n_layer * 2 * (es_rank * cfg.d_state * 4 + es_rank * (cfg.d_conv - 1) * 2)
         by_prompt = {}
         for plen in a.decode_prompts:
@@ -563,7 +611,7 @@ def run_ours(a):
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": a.steps, "warmup": a.warmup,
         "ms_per_step": ms / a.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic (seeded random-init weights, uniform random token ids)",
-        "collectives_ms_per_step": coll_ms, "model_load": load_note,
+        "collectives_ms_per_step": coll_ms, "collective_waits": comm_trace, "model_load": load_note,
         "config": {"workload": f"{a.label}mamba-{a.shape}-shaped TP prefill {B}x{S} + graphed decode", "shape": a.shape,
                    "global_batch": B, "seq_len": S, "tp": ws, "parallelism": f"tp{ws}",
                    "precision_map": a.spec if a.spec != "mixed" else
@@ -600,6 +648,7 @@ def main():
     ap.add_argument("--ref-sample-tokens", type=int, default=128,
                     help="tokens of one reference CPU sample (1 sequence, all layers)")
     ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-comm-trace", action="store_true", help="TP > 1: skip the traced prefill of the collectives")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-tokens", type=int, default=1024)
     ap.add_argument("--ref-layers", type=int, default=4)

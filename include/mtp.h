@@ -258,6 +258,23 @@ int mtp_allreduce(mtp_comm *c, int site, int mode, const float *in, float *out, 
  * on the GPU (different streams, different host threads) race on it. */
 int mtp_allreduce_noalloc(int mode, const float *in, float *out, int rows, int cols, void *stream);
 
+/* ---------------------------------------------------------------- vocabulary-parallel lm_head
+ * The reference replicates the tied lm_head on every rank (TPMambaLM.lm_head,
+ * tp_model.py:302-303: logits = x @ embedding.weight^T, every rank reading all V rows).
+ * Vocabulary-parallel form: rank k computes only logits columns [col0, col0 + cols)
+ * (mtp_vocab_shard: ceil(V / ws) rounded up to a multiple of 8, the last rank the
+ * remainder) and the ranks exchange their columns over the context's peer memory, so
+ * every rank returns the full [rows, V] logits, bit-identical to the replicated GEMM
+ * (same kernel and summation order per element).  Used for few rows (decode steps):
+ * each rank then reads V / ws embedding rows instead of V.  normed [rows, K], emb
+ * [V, K] (the tied embedding), out [rows, V], all of `dtype` (MTP_F32 / MTP_BF16).
+ * rows x shard x element size must fit one receive slot of the out_proj site
+ * (max_rows x (4 cols_out + 16) bytes).  c NULL or world size 1: the plain GEMM.
+ * Collective: every rank calls it with the same rows, V and dtype. */
+int mtp_vocab_shard(int V, int world_size, int rank, int *col0, int *cols);
+int mtp_lm_head_vocab_parallel(mtp_comm *c, const void *normed, int rows, int K, int ld_normed, const void *emb, int V,
+                               int ld_emb, int dtype, void *out, int ld_out, void *stream);
+
 /* ---------------------------------------------------------------- persistent decode
  * One cooperative launch per decode step runs every layer of the model for a batch
  * of single tokens: embedding gather (tp_model.py:318), per layer the block's

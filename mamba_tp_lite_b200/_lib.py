@@ -59,6 +59,8 @@ _SIGS = {
     "mtp_reduce_outproj": [_vp, _i, _vp, _i, _i, _vp, _vp, _vp, _f, _vp, _i, _vp],
     "mtp_allreduce": [_vp, _i, _i, _vp, _vp, _i, _i, _vp],
     "mtp_allreduce_noalloc": [_i, _vp, _vp, _i, _i, _vp],
+    "mtp_vocab_shard": [_i, _i, _i, C.POINTER(_i), C.POINTER(_i)],
+    "mtp_lm_head_vocab_parallel": [_vp, _vp, _i, _i, _i, _vp, _i, _i, _i, _vp, _i, _vp],
     "mtp_decode_plan_create": [_vp, _i, _vp, _vp, _i, _i, _i, _i, _i, _f, _i, _i, _vp, C.POINTER(_vp)],
     "mtp_decode_bind_cache": [_vp, _vp, _vp, _i, C.POINTER(_vp)],
     "mtp_decode_step": [_vp, _vp, _vp, _vp, _vp],
@@ -128,6 +130,13 @@ def comm_sent_bytes(comm, mode: int, rows: int, cols: int, rdt: int) -> float:
     out = C.c_double(0.0)
     call("mtp_comm_sent_bytes", comm, mode, rows, cols, rdt, C.byref(out))
     return out.value
+
+
+def vocab_shard(V: int, ws: int, rank: int) -> tuple[int, int]:
+    """(first column, columns) of ``rank``'s logits in the vocabulary-parallel lm_head."""
+    c0, n = C.c_int(0), C.c_int(0)
+    call("mtp_vocab_shard", V, ws, rank, C.byref(c0), C.byref(n))
+    return c0.value, n.value
 
 
 def stream_ptr(stream=None) -> int:

@@ -1492,6 +1492,88 @@ static int run_reduce(mtp_comm *c, int site, int mode, const float *partial, int
   return MTP_OK;
 }
 
+// ----------------------------------------------------------------- vocabulary-column gather
+// Vocabulary-parallel lm_head: rank k holds logits columns [k shard, min(V, (k+1) shard)) of
+// every row (shard = vocab_shard()); one launch gives every rank all of them.  Element units
+// are U (16 bytes when every row start and shard boundary is 16-byte aligned, else the
+// logits element).  CTA j handles units [j per, (j+1) per) of the [rows, shard] block, the
+// same range on every rank: it copies its own columns into `out`, pushes them to every
+// peer's receive slot of `site` (half by epoch parity, as the reductions), raises its
+// flag, waits (bounded) for CTA j of every rank and copies the peers' columns out.  The
+// epoch / parity protocol is the reductions' own, so the launch can follow or precede a
+// reduction on the same site.
+template <typename U>
+__global__ void __launch_bounds__(256) gather_cols_kernel(CommDev d, int site, U *out, long ldo, int rows,
+                                                          int shard_u, int total_u) {
+  MTP_PDL_WAIT();
+  MTP_PDL_TRIGGER();
+  __shared__ int abort_sm;
+  __shared__ uint32_t epoch_sm;
+  const int j = blockIdx.x, G = gridDim.x;
+  uint32_t *ep = reinterpret_cast<uint32_t *>(d.peer[d.rank] + d.off_epoch) + site;
+  if (threadIdx.x == 0) {
+    abort_sm = 0;
+    epoch_sm = *reinterpret_cast<volatile uint32_t *>(ep) + 1u;
+  }
+  __syncthreads();
+  const uint32_t epoch = epoch_sm;
+  const size_t half = (size_t)(epoch & 1u) * d.ws * d.slot_bytes[site];
+  const uint32_t all = (1u << d.ws) - 1u;
+  const long n = (long)rows * shard_u;
+  const long per = (n + G - 1) / G, lo = (long)j * per, hi = lo + per < n ? lo + per : n;
+  auto cols_of = [&](int k) {
+    const int c = total_u - k * shard_u;
+    return c < shard_u ? c : shard_u;
+  };
+  const int mine = cols_of(d.rank);
+  const long col0 = (long)d.rank * shard_u;
+  for (int q = 1; q < d.ws; ++q) {
+    const int dst = (d.rank + q) % d.ws;  // stagger destinations across ranks
+    U *slot = reinterpret_cast<U *>(d.peer[dst] + d.off_recv[site] + half + (size_t)d.rank * d.slot_bytes[site]);
+    for (long i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+      const long r = i / shard_u;
+      const int c = (int)(i - r * shard_u);
+      if (c < mine) slot[i] = out[r * ldo + col0 + c];
+    }
+  }
+  signal(d, site, 0, epoch, all);
+  bool ok = wait_all(d, site, 0, epoch, all, &abort_sm);
+  if (ok) {
+    for (int q = 1; q < d.ws; ++q) {
+      const int src = (d.rank + q) % d.ws;
+      const U *slot = reinterpret_cast<const U *>(d.peer[d.rank] + d.off_recv[site] + half + (size_t)src * d.slot_bytes[site]);
+      const int cs = cols_of(src);
+      const long c0 = (long)src * shard_u;
+      for (long i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        const long r = i / shard_u;
+        const int c = (int)(i - r * shard_u);
+        if (c < cs) out[r * ldo + c0 + c] = __ldcg(slot + i);
+      }
+    }
+  }
+  // the last CTA to leave publishes the epoch for the next call
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    unsigned int *done = reinterpret_cast<unsigned int *>(d.peer[d.rank] + d.off_done) + site;
+    if (atomicAdd(done, 1u) == (unsigned)G - 1u) {
+      *done = 0u;
+      *reinterpret_cast<volatile uint32_t *>(ep) = epoch;
+      __threadfence();
+    }
+  }
+}
+
+// Columns of each rank in the vocabulary-parallel lm_head: ceil(V / ws) rounded up to a
+// multiple of 8 (16-byte boundaries for 2-byte logits), the last rank the remainder.
+int vocab_shard(int V, int ws) {
+  const int s = (V + ws - 1) / ws;
+  return (s + 7) / 8 * 8;
+}
+
+int gemm_cols_as_full(const void *A, const void *B, void *C, int M, int N_full, int col0, int cols, int K, int lda,
+                      int ldb, int ldc, int dtype, cudaStream_t s);
+
 }  // namespace mtp
 
 using namespace mtp;
@@ -1719,6 +1801,57 @@ int mtp_dequant_sum(const uint8_t *payloads, int ws, int rows, int cols, float *
   const size_t n = (size_t)rows * cols;
   launch_pdl(dequant_sum_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, (cudaStream_t)stream, payloads, ws, rows, cols, out);
   return check_launch("dequant_sum");
+}
+
+int mtp_vocab_shard(int V, int world_size, int rank, int *col0, int *cols) {
+  MTP_REQUIRE(V > 0 && world_size >= 1 && rank >= 0 && rank < world_size && col0 && cols, "bad arguments");
+  const int sh = vocab_shard(V, world_size);
+  MTP_REQUIRE((long)sh * (world_size - 1) < V, "vocabulary too small for the rank count");
+  *col0 = sh * rank;
+  *cols = V - sh * rank < sh ? V - sh * rank : sh;
+  return MTP_OK;
+}
+
+int mtp_lm_head_vocab_parallel(mtp_comm *c, const void *normed, int rows, int K, int ld_normed, const void *emb, int V,
+                               int ld_emb, int dtype, void *out, int ld_out, void *stream) {
+  MTP_REQUIRE(normed && emb && out && rows >= 0 && K > 0 && V > 0, "bad arguments");
+  MTP_REQUIRE(dtype == MTP_F32 || dtype == MTP_BF16, "dtype must be F32 or BF16");
+  MTP_REQUIRE(ld_normed >= K && ld_emb >= K && ld_out >= V, "leading dimensions too small");
+  if (rows == 0) return MTP_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const bool has_comm = c && c->d.ws > 1;
+  if (!has_comm) return mtp_gemm(normed, emb, out, rows, V, K, ld_normed, ld_emb, ld_out, dtype, dtype, MTP_EPI_STORE,
+                                 nullptr, 0, stream);
+  MTP_REQUIRE(c->opened, "comm context peers not opened");
+  const int ws = c->d.ws, rank = c->d.rank, site = 1;
+  int col0 = 0, cols = 0;
+  int rc = mtp_vocab_shard(V, ws, rank, &col0, &cols);
+  if (rc) return rc;
+  const int sh = vocab_shard(V, ws);
+  const size_t es = dtype == MTP_F32 ? 4 : 2;
+  MTP_REQUIRE((size_t)rows * sh * es <= c->d.slot_bytes[site], "rows x vocabulary shard exceed the receive slot");
+  rc = gemm_cols_as_full(normed, emb, out, rows, V, col0, cols, K, ld_normed, ld_emb, ld_out, dtype, s);
+  if (rc) return rc;
+  const bool v16 = aligned16(out) && ((size_t)ld_out * es) % 16 == 0 && ((size_t)sh * es) % 16 == 0 &&
+                   ((size_t)V * es) % 16 == 0;
+  const int upe = v16 ? (int)(16 / es) : 1;  // elements per unit
+  const int shard_u = sh / upe, total_u = V / upe;
+  const long n = (long)rows * shard_u;
+  int G = (int)((n + 1023) / 1024);
+  const int gmax = 2 * num_sms() < G_MAX ? 2 * num_sms() : G_MAX;
+  if (G > gmax) G = gmax;
+  if (G < 1) G = 1;
+  CommDev d = c->d;
+  if (v16)
+    launch_pdl(gather_cols_kernel<uint4>, dim3(G), dim3(256), 0, s, d, site, (uint4 *)out, (long)(ld_out / upe), rows,
+               shard_u, total_u);
+  else if (es == 4)
+    launch_pdl(gather_cols_kernel<uint32_t>, dim3(G), dim3(256), 0, s, d, site, (uint32_t *)out, (long)ld_out, rows,
+               shard_u, total_u);
+  else
+    launch_pdl(gather_cols_kernel<uint16_t>, dim3(G), dim3(256), 0, s, d, site, (uint16_t *)out, (long)ld_out, rows,
+               shard_u, total_u);
+  return check_launch("gather_cols");
 }
 
 }  // extern "C"

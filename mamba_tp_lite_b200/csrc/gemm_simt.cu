@@ -227,11 +227,17 @@ __global__ void __launch_bounds__(256) gemv_splitk_kernel(const T *__restrict__ 
   }
 }
 
+// The GEMV variant for [M, N] x K: K split over a CTA's threads for small N (more CTAs
+// than rows of W otherwise), one warp per row of W else.  The two sum K in different orders.
+static bool gemv_splits_k(int M, int N, int K) { return N <= 4096 && K >= 512 && M <= 8; }
+
 template <typename T>
-static int launch_gemv(const T *X, int ldx, const T *W, int ldw, int M, int N, int K, EpiArgs e, cudaStream_t s) {
+static int launch_gemv(const T *X, int ldx, const T *W, int ldw, int M, int N, int K, EpiArgs e, cudaStream_t s,
+                       int split = -1) {
   constexpr int ROWS = 2;
   const bool vec = aligned16(X) && aligned16(W) && (ldx % 8 == 0) && (ldw % 8 == 0);
-  if (N <= 4096 && K >= 512 && M <= 8) {  // small N: every CTA splits K over its 256 threads
+  if (split < 0) split = gemv_splits_k(M, N, K) ? 1 : 0;
+  if (split) {  // small N: every CTA splits K over its 256 threads
     constexpr int RB = 2;
     dim3 g(ceil_div(N, RB));
     if (M <= 1) launch_pdl(gemv_splitk_kernel<T, 1, RB>, dim3(g), dim3(256), 0, s, X, ldx, W, ldw, M, N, K, vec, e);
@@ -247,6 +253,38 @@ static int launch_gemv(const T *X, int ldx, const T *W, int ldw, int M, int N, i
   else if (M <= 4) { grid.y = 1; launch_pdl(gemv_kernel<T, 4, ROWS>, dim3(grid), dim3(256), 0, s, X, ldx, W, ldw, M, N, K, vec, e); }
   else { grid.y = ceil_div(M, 8); launch_pdl(gemv_kernel<T, 8, ROWS>, dim3(grid), dim3(256), 0, s, X, ldx, W, ldw, M, N, K, vec, e); }
   return check_launch("gemv");
+}
+
+// Columns [col0, col0 + cols) of C = A x B^T for a B of N_full rows, computed by the
+// kernel (and so with the per-element summation order) that mtp_gemm picks for the whole
+// [M, N_full] product: the vocabulary-parallel lm_head gives the same bits as the
+// replicated one.  B and C are the full matrices; C's other columns are not touched.
+int gemm_cols_as_full(const void *A, const void *B, void *C, int M, int N_full, int col0, int cols, int K, int lda,
+                      int ldb, int ldc, int dtype, cudaStream_t s) {
+  MTP_REQUIRE(A && B && C && M >= 0 && K > 0 && col0 >= 0 && cols > 0 && col0 + cols <= N_full, "bad arguments");
+  MTP_REQUIRE(dtype == MTP_F32 || dtype == MTP_BF16, "dtype must be F32 or BF16");
+  if (M == 0) return MTP_OK;
+  const size_t es = dtype == MTP_F32 ? 4 : 2;
+  const void *Bs = (const char *)B + (size_t)col0 * ldb * es;
+  void *Cs = (char *)C + (size_t)col0 * es;
+  EpiArgs e{Cs, ldc, dtype, MTP_EPI_STORE, nullptr, 0};
+  if (dtype == MTP_BF16 && M > 16 && gemm_tc_eligible(A, B, M, N_full, K, lda, ldb)) {
+    MTP_REQUIRE(aligned16(Bs), "vocabulary shard of B not 16-byte aligned");
+    return gemm_tc(A, Bs, Cs, M, cols, K, lda, ldb, ldc, dtype, MTP_EPI_STORE, nullptr, 0, s);
+  }
+  if (M <= 64) {
+    const int split = gemv_splits_k(M, N_full, K) ? 1 : 0;
+    if (dtype == MTP_F32) return launch_gemv((const float *)A, lda, (const float *)Bs, ldb, M, cols, K, e, s, split);
+    return launch_gemv((const __nv_bfloat16 *)A, lda, (const __nv_bfloat16 *)Bs, ldb, M, cols, K, e, s, split);
+  }
+  dim3 grid(ceil_div(cols, 64), ceil_div(M, 64));
+  if (dtype == MTP_F32)
+    launch_pdl(gemm_simt_kernel<float>, dim3(grid), dim3(256), 0, s, (const float *)A, (const float *)Bs, M, cols, K,
+               lda, ldb, e);
+  else
+    launch_pdl(gemm_simt_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, s, (const __nv_bfloat16 *)A,
+               (const __nv_bfloat16 *)Bs, M, cols, K, lda, ldb, e);
+  return check_launch("gemm_simt");
 }
 
 }  // namespace mtp

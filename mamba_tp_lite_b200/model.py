@@ -175,11 +175,30 @@ class _LMKernels:
     def _next_norm_w(self, i):
         return self.layers[i + 1].norm.weight if i + 1 < len(self.layers) else self.norm_f.weight
 
+    def _vocab_parallel_comm(self, rows: int):
+        """Comm context for a vocabulary-parallel lm_head of ``rows`` rows, or None for the
+        replicated one.  Tensor-parallel models only, up to MTP_VOCAB_PARALLEL_ROWS rows
+        (default 256; 0 turns it off): beyond that, gathering [rows, V] logits over NVLink
+        costs more than the replicated GEMM it divides (1.4b, 32 x 1024 rows: ~3 GB)."""
+        ws = getattr(self, "world_size", 1)
+        if ws < 2 or rows > int(os.environ.get("MTP_VOCAB_PARALLEL_ROWS", "256")):
+            return None
+        from .tp_utils import get_comm
+
+        cfg = self.cfg
+        return get_comm(self.group, self.rank, ws, cfg.dt_rank + 2 * cfg.d_state, cfg.d_model)
+
     def _lm_head(self, normed: torch.Tensor) -> torch.Tensor:
         w = self.embedding.weight
         logits = torch.empty(normed.shape[0], w.shape[0], device=normed.device, dtype=w.dtype)
         from . import _mixer
 
+        comm = self._vocab_parallel_comm(normed.shape[0])
+        if comm is not None:  # this rank's vocabulary columns, then an exchange over peer memory
+            L.call("mtp_lm_head_vocab_parallel", comm.ptr, L.ptr(normed), normed.shape[0], w.shape[1],
+                   normed.stride(0), L.ptr(w), w.shape[0], w.stride(0), L.dtype_code(w.dtype), L.ptr(logits),
+                   logits.stride(0), L.stream_ptr())
+            return logits
         ev = _mixer._prof_begin() if normed.shape[0] > 64 else None
         L.call("mtp_gemm", L.ptr(normed), L.ptr(w), L.ptr(logits), normed.shape[0], w.shape[0], w.shape[1],
                normed.stride(0), w.stride(0), logits.stride(0), L.dtype_code(w.dtype), L.dtype_code(logits.dtype),

@@ -7,7 +7,8 @@ dimension.  in_proj's x rows and z rows are each sliced by channel
 per channel; x_proj and out_proj are sliced along their input (contraction)
 dimension, so each rank produces a partial sum that is reduced across ranks:
 exactly two reductions per block (AllReduce #1 after x_proj, #2 after
-out_proj).  The embedding / tied lm_head are replicated.
+out_proj).  The embedding is replicated; the tied lm_head is vocabulary-parallel
+for few rows (see TPMambaLM) and replicated otherwise.
 """
 from __future__ import annotations
 
@@ -124,8 +125,12 @@ class TPMambaBlock(nn.Module):
 
 
 class TPMambaLM(_LMKernels, nn.Module):
-    """Tensor-parallel LM (tp_model.py:271-384): sharded mixers, replicated
-    embedding / tied lm_head."""
+    """Tensor-parallel LM (tp_model.py:271-384): sharded mixers, a replicated
+    embedding, and the tied lm_head vocabulary-parallel for up to
+    MTP_VOCAB_PARALLEL_ROWS rows (default 256: decode steps, short prompts) -- each
+    rank multiplies by its V / ws embedding rows and the ranks exchange the logits
+    columns over peer memory, bit-identical to the reference's replicated lm_head --
+    and replicated for longer inputs."""
 
     def __init__(self, cfg: MambaConfig, rank: int, world_size: int, group=None, allreduce_dtype="fp32"):
         super().__init__()

@@ -152,6 +152,33 @@ class Comm:
         """Caps the grid of this context's reductions (0: default); see mtp_comm_set_max_ctas."""
         L.call("mtp_comm_set_max_ctas", self.handle, int(max_ctas))
 
+    def set_trace(self, records: int) -> None:
+        """Ring of ``records`` phase-trace records of this context's reductions (0 frees
+        it); see mtp_comm_set_trace.  Nothing may be in flight."""
+        L.call("mtp_comm_set_trace", self.handle, int(records))
+
+    def read_trace(self) -> list[dict]:
+        """The recorded launches in launch order (after a synchronize).  Per launch: the
+        protocol, the rounds, and for CTA 0 and the last CTA the kernel time and the time
+        spent in the bounded flag waits (``wait_us``: waiting for the peers' pushes, and
+        in the two-shot protocol for the owners' gathered rows), i.e. the part of the
+        collective that waited for other ranks rather than moving or reducing bytes."""
+        cap = 4096
+        buf = (C.c_uint64 * (cap * TRACE_WORDS))()
+        n = C.c_int(0)
+        L.call("mtp_comm_read_trace", self.handle, buf, cap * TRACE_WORDS, C.byref(n))
+        out = []
+        for i in range(min(n.value, cap)):
+            rec = buf[i * TRACE_WORDS:(i + 1) * TRACE_WORDS]
+            two, rounds = bool(rec[2]), int(rec[1])
+            ctas = []
+            for base in (3, 67):
+                st = [v for v in rec[base:base + 64] if v]
+                if st:
+                    ctas.append(_trace_waits(st, two, rounds))
+            out.append({"two_shot": two, "rounds": rounds, "grid": int(rec[0]), "ctas": ctas})
+        return out
+
     def check(self) -> None:
         """Raises if a bounded wait of a reduction timed out (after a synchronize)."""
         torch.cuda.synchronize()
@@ -163,6 +190,40 @@ class Comm:
         if self.handle:
             L.call("mtp_comm_destroy", self.handle)
             self.handle = C.c_void_p()
+
+
+TRACE_WORDS = 131  # u64 per trace record (include/mtp.h, mtp_comm_set_trace)
+
+
+def _trace_waits(stamps: list[int], two_shot: bool, rounds: int) -> dict:
+    """Kernel and wait time (us) of one CTA's %globaltimer stamps.  The stamp order
+    follows the round loop of the reduction kernel: one-shot, per round k in 0..K: after
+    the push, [after the wait, after the reduce], after the signal; two-shot, per k in
+    0..K+1: after the push, [after the push wait, after the owner reduce], [after the
+    gather wait, after the copy-out], after the signal."""
+    t0 = stamps[0]
+    i, wait = 1, 0
+    for k in range(rounds + (2 if two_shot else 1)):
+        if i >= len(stamps):
+            break
+        prev = stamps[i]  # after the push step
+        i += 1
+        waits = []
+        if two_shot:
+            if 1 <= k <= rounds:
+                waits.append(1)
+            if k >= 2:
+                waits.append(2)
+        elif k >= 1:
+            waits.append(1)
+        for _ in waits:
+            if i + 1 >= len(stamps):
+                break
+            wait += stamps[i] - prev  # bounded flag wait
+            prev = stamps[i + 1]
+            i += 2
+        i += 1  # after the signal
+    return {"kernel_us": (stamps[-1] - t0) / 1e3, "wait_us": wait / 1e3}
 
 
 def exchange_handles(mine: bytes, group, ws: int) -> list[bytes]:

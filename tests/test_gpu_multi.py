@@ -8,6 +8,8 @@ world sizes 2, 4 and 8 (each skipped when the box has fewer GPUs):
 * the TP model matches the oracle's TP emulation at the same world size with identical
   results on every rank, graphed decode equals eager decode bitwise, and the persistent
   decode kernel agrees with the per-layer chain;
+* the vocabulary-parallel lm_head gives the replicated lm_head's logits and greedy tokens,
+  bitwise;
 * the out_proj epilogue gives the same bits through one-shot, two-shot and capped grids,
   and the overlapped micro-batch prefill equals the serial prefill bitwise.
 
@@ -154,6 +156,22 @@ def _suite(rank, init_file, q, ws):
                     all(torch.equal(a, b) for a, b in zip(eager, graphed)), count, chain,
                     getattr(m, "_mtp_decode", None) is not None)
                 del m
+        # ---- vocabulary-parallel lm_head (default up to 256 rows) == replicated lm_head, bitwise
+        out["vocab"] = {}
+        for dtype in (torch.float32, torch.bfloat16):
+            sd = random_init_state_dict(cfg, seed=5, dtype=dtype)
+            m = TPMambaLM.from_state_dict_shard(cfg, sd, rank, ws, dtype=dtype, allreduce_dtype="int8", device="cuda")
+            for vp in ("0", "256"):
+                os.environ["MTP_VOCAB_PARALLEL_ROWS"] = vp
+                lg, cache = m.prefill(ids.cuda())                       # 144 rows
+                lg1, _ = m.prefill(ids[:1, :20].cuda())                 # 20 rows
+                st = m.step(torch.full((2, 1), 7, dtype=torch.long, device="cuda"), cache)  # 2 rows
+                toks = m.generate(ids[:, :9].cuda(), 4, graphed=True)   # graphed greedy decode
+                out["vocab"][(str(dtype), vp)] = (_digest(lg.float().cpu().numpy()),
+                                                  _digest(lg1.float().cpu().numpy()),
+                                                  _digest(st.float().cpu().numpy()), toks.cpu().numpy())
+            os.environ.pop("MTP_VOCAB_PARALLEL_ROWS")
+            del m
         # ---- out_proj epilogue through one-shot, two-shot and a capped grid
         rows, d = 3000, 1024
         comm = get_comm(None, rank, ws, 48, d)
@@ -271,6 +289,23 @@ def test_tp_model_matches_oracle_and_ranks_agree(ws, dtype_name):
         else:
             met = O.quant_metrics(ref, lg0)
             assert met["kl"].mean() <= 2e-3 and met["top1"].mean() >= 0.95, (spec, met)
+
+
+# ------------------------------------------------------------------ vocabulary-parallel lm_head
+@pytest.mark.parametrize("ws", WS_LIST)
+def test_vocab_parallel_lm_head_equals_replicated(ws):
+    """Each rank computes V / ws logits columns and the ranks exchange them over peer
+    memory: prefill logits (tensor-core and CUDA-core paths), step logits (GEMV path)
+    and graphed greedy tokens are bit-identical to the replicated lm_head on every rank."""
+    if _ngpu() < ws:
+        pytest.skip(f"needs {ws} GPUs")
+    res = suite(ws)
+    for dtype in ("torch.float32", "torch.bfloat16"):
+        rep = res[0]["vocab"][(dtype, "0")]
+        for r in range(ws):
+            got, ref = res[r]["vocab"][(dtype, "256")], res[r]["vocab"][(dtype, "0")]
+            assert got[:3] == ref[:3] == rep[:3], (dtype, r)
+            assert np.array_equal(got[3], ref[3]) and np.array_equal(got[3], rep[3]), (dtype, r)
 
 
 # ------------------------------------------------------------------ protocols agree (out_proj epilogue, bf16 gather)

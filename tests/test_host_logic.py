@@ -44,6 +44,22 @@ def test_library_reports_errors_without_a_gpu():
     assert "null pointer" in L.load().mtp_last_error().decode()
 
 
+@pytest.mark.parametrize("V,ws", [(50280, 2), (50280, 4), (50280, 8), (1000, 8), (1000, 3), (64, 2)])
+def test_vocab_shard_split(V, ws):
+    """The vocabulary-parallel lm_head's column split (host arithmetic, no kernel): every
+    column once, in rank order, shard boundaries on 8-column (16-byte bf16) multiples."""
+    spans = [L.vocab_shard(V, ws, r) for r in range(ws)]
+    assert spans[0][0] == 0 and sum(n for _, n in spans) == V
+    for (c0, n), (c1, _) in zip(spans, spans[1:]):
+        assert c1 == c0 + n and n % 8 == 0
+    assert all(n > 0 for _, n in spans)
+
+
+def test_vocab_shard_rejects_too_few_columns():
+    c0, n = L.C.c_int(0), L.C.c_int(0)
+    assert L.load().mtp_vocab_shard(20, 8, 0, L.C.byref(c0), L.C.byref(n)) == L.MTP_ERR_ARG
+
+
 def test_product_has_no_cpu_fallback():
     cfg = MambaConfig(d_model=32, n_layer=1, vocab_size=64, d_state=8)
     m = MambaMixer(cfg, 0)
