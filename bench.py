@@ -349,7 +349,8 @@ def trace_collectives(model, ids, n_layer: int, rank: int, ws: int):
     """One untimed prefill with the reductions' phase trace on: per site, the mean over
     the layers of each rank's kernel time and of the time its CTA 0 spent in bounded
     flag waits for other ranks (arrival skew between ranks plus the peers' push time),
-    as lists indexed by rank."""
+    as lists indexed by rank.  Sites whose reduction is fused into the GEMM epilogue
+    (x_proj) have no traced reduction launch and are absent."""
     import torch
     import torch.distributed as dist
 
@@ -366,8 +367,8 @@ def trace_collectives(model, ids, n_layer: int, rank: int, ws: int):
     recs = c.read_trace()
     c.set_trace(0)
     mine = {}
-    for si, site in enumerate(("x_proj", "out_proj")):
-        rs = [r for i, r in enumerate(recs[:2 * n_layer]) if i % 2 == si and r["ctas"]]
+    for site in ("x_proj", "out_proj"):
+        rs = [r for r in recs if r["site"] == site and r["ctas"]]
         if rs:
             mine[site] = (sum(r["ctas"][0]["kernel_us"] for r in rs) / len(rs),
                           sum(r["ctas"][0]["wait_us"] for r in rs) / len(rs), rs[0]["two_shot"])
@@ -500,6 +501,12 @@ def run_ours(a):
         if name in gemms:
             tf = v["work"] / (v["avg_ms"] / 1000.0) / 1e12
             row.update({"bound": "tensor", "achieved_TFLOPs": tf, "frac": tf / pk})
+        elif name == "x_proj+reduce_x":
+            # the x_proj GEMM whose epilogue writes AllReduce #1's wire rows, plus (TP > 1) the
+            # kernel that reduces them: one site, FLOPs of the GEMM over the whole time
+            tf = v["work"] / (v["avg_ms"] / 1000.0) / 1e12
+            row.update({"bound": "tensor + nvlink" if ws > 1 else "tensor", "achieved_TFLOPs": tf, "frac": tf / pk,
+                        "note": "GEMM with AllReduce #1 in its epilogue (no fp32 partial written)"})
         elif name in ("reduce_x", "reduce_out"):
             # work = bytes this rank sends to its peers (0 at TP=1: the wire format's round trip only)
             gbs = v["work"] / (v["avg_ms"] / 1000.0) / 1e9

@@ -114,8 +114,8 @@ int mtp_scan_prefill(const void *xz, int ld_xz, const void *dt, int ld_dt, int d
  * computed once per layer); z is read from columns [Es, 2Es) of xz and the raw x
  * columns [0, Es) of xz only for the final conv history.  Other arguments as
  * mtp_scan_prefill (conv weights are not needed).  State pairs are updated with
- * packed fp32 arithmetic and part of the state exponentials is evaluated on the FP32
- * pipe (the polynomial of mtp_exp2_fma).  Replaces tp_model.py:101-103 and :113-129
+ * packed fp32 arithmetic; optionally (MTP_SCAN_POLY pairs per thread, 0 by default) part
+ * of the state exponentials is evaluated on the FP32 pipe (the polynomial of mtp_exp2_fma).  Replaces tp_model.py:101-103 and :113-129
  * (model.py:210-241), the Python loop over t at tp_model.py:124-126. */
 int mtp_scan_prefill_xc(const void *xc, int ld_xc, const void *xz, int ld_xz, const void *dt, int ld_dt,
                         int dt_dtype, const float *bc, int ld_bc, const void *A_log, const void *Dp,
@@ -216,7 +216,7 @@ int mtp_comm_sent_bytes(mtp_comm *c, int mode, int rows, int cols, int rdt, doub
 
 /* Phase trace of the pipelined reductions on this context (diagnostics; off by default).
  * records > 0 allocates a ring of that many launch records of 131 uint64 each: [0] grid
- * size, [1] rounds, [2] 1 for the two-shot protocol, then from [3] (CTA 0) and [67] (the
+ * size, [1] rounds, [2] bit 0: the two-shot protocol, bits 8+: the site, then from [3] (CTA 0) and [67] (the
  * last CTA) the %globaltimer ns at start and after each push / wait / reduce / signal
  * step of each round; 0 frees it.  Not allowed while a reduction is in flight. */
 int mtp_comm_set_trace(mtp_comm *c, int records);
@@ -237,6 +237,21 @@ int mtp_reduce_xproj(mtp_comm *c, int mode, const float *partial, int rows, int 
 int mtp_reduce_outproj(mtp_comm *c, int mode, const float *partial, int rows, int D, const void *bias,
                        float *resid, const void *norm_w, float eps, void *normed, int out_dtype,
                        void *stream);
+/* x_proj GEMM fused with AllReduce #1 (tp_model.py:106-108: x_dbl = x_proj(x), reduced
+ * across ranks, split into dt | B | C): partial = xc[rows, K] . w[N, K]^T (bf16 operands,
+ * fp32 accumulate) is never written; the GEMM's epilogue quantises / casts each row to the
+ * wire format of `mode` and, at world size 1, applies the wire round trip and writes
+ * dt_low [rows, R] (dt_dtype, also the rounding dtype of the reduced values) and bc
+ * [rows, N-R] fp32 directly; at world size > 1 it writes the wire rows into every rank's
+ * receive slot of the x_proj site and flags them, and a second kernel reduces every row
+ * over the ranks in rank order and splits it.  xc and w are ab_dtype (the fused form
+ * needs MTP_BF16).  Bit-identical to mtp_gemm into `partial`
+ * followed by mtp_reduce_xproj, which is what runs when the shape does not fit the fused
+ * form (N % 16, N <= 192, R % 16, 16-byte aligned operands and outputs, rows within the
+ * context's slots, no grid cap; MTP_XPROJ_FUSED=0 forces it): `partial` [rows, N] fp32 is
+ * only used then and may be NULL for shapes that fit. */
+int mtp_xproj_fused(mtp_comm *c, int mode, const void *xc, int ld_xc, const void *w, int ld_w, int ab_dtype, int rows,
+                    int N, int K, int R, float *partial, void *dt_low, int dt_dtype, float *bc, void *stream);
 /* Plain reduction (the isolated site of the collective microbenchmark):
  * out[rows, cols] (fp32) = reduce(in) over ranks; site selects the buffers. */
 int mtp_allreduce(mtp_comm *c, int site, int mode, const float *in, float *out, int rows, int cols,

@@ -58,6 +58,7 @@ _SIGS = {
     "mtp_reduce_xproj": [_vp, _i, _vp, _i, _i, _i, _vp, _i, _vp, _vp],
     "mtp_reduce_outproj": [_vp, _i, _vp, _i, _i, _vp, _vp, _vp, _f, _vp, _i, _vp],
     "mtp_allreduce": [_vp, _i, _i, _vp, _vp, _i, _i, _vp],
+    "mtp_xproj_fused": [_vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _i, _vp, _vp],
     "mtp_allreduce_noalloc": [_i, _vp, _vp, _i, _i, _vp],
     "mtp_vocab_shard": [_i, _i, _i, C.POINTER(_i), C.POINTER(_i)],
     "mtp_lm_head_vocab_parallel": [_vp, _vp, _i, _i, _i, _vp, _i, _i, _i, _vp, _i, _vp],

@@ -124,6 +124,30 @@ class MixerKernels:
                 _prof_end(ev, "reduce_x", L.comm_sent_bytes(ctx, mode, rows, partial.shape[1],
                                                             L.dtype_code(dt_low.dtype)))
 
+    def _xproj_fused(self, xc, partial, dt_low, bc) -> bool:
+        """x_proj GEMM fused with AllReduce #1 (tp_model.py:106-108): the GEMM's epilogue
+        writes the wire rows (or, at world size 1, dt_low | B|C after the wire round trip),
+        so the fp32 partial is not written; ``partial`` is only the fallback buffer of the
+        library for shapes the fused form does not take.  False (nothing launched) for the
+        torch.distributed variants and while micro-batches overlap."""
+        cfg = self.cfg
+        name = None if self._site_modes is None else self._site_modes["x_proj"]
+        if OVERLAP_STREAM is not None or (name is not None and name not in KERNEL_MODES):
+            return False
+        ctx, mode = None, L.RED_FP32
+        if name is not None:
+            count_collective(self.comm, name, partial.shape, self._dt())
+            mode = KERNEL_MODES[name]
+            ctx = comm_for(self)
+        T, n_out = partial.shape
+        w = self.x_proj.weight
+        ev = _prof_begin()
+        L.call("mtp_xproj_fused", ctx, mode, L.ptr(xc), xc.stride(0), L.ptr(w), w.stride(0), L.dtype_code(xc.dtype), T,
+               n_out, xc.shape[1], cfg.dt_rank, L.ptr(partial), L.ptr(dt_low), L.dtype_code(dt_low.dtype), L.ptr(bc),
+               L.stream_ptr())
+        _prof_end(ev, "x_proj+reduce_x", 2.0 * T * n_out * xc.shape[1])
+        return True
+
     def _reduce_out(self, partial, resid, norm_w, eps, normed):
         """AllReduce #2 (tp_model.py:132-134) fused with the bias, the block
         residual and the next RMSNorm."""
@@ -199,10 +223,11 @@ class MixerKernels:
                B, Lq, es, k, L.dtype_code(dt_), L.stream_ptr())
         _prof_end(ev, "conv1d", 2 * T * es * xz.element_size())  # x read, xc written
         partial_x = torch.empty(T, r + 2 * n, device=dev, dtype=torch.float32)
-        self._gemm(xc, self.x_proj.weight, partial_x, tag="x_proj")
         dt_low = torch.empty(T, r, device=dev, dtype=dt_)
         bc = torch.empty(T, 2 * n, device=dev, dtype=torch.float32)
-        self._reduce_x(partial_x, dt_low, bc)
+        if not self._xproj_fused(xc, partial_x, dt_low, bc):
+            self._gemm(xc, self.x_proj.weight, partial_x, tag="x_proj")
+            self._reduce_x(partial_x, dt_low, bc)
         yield
         y = torch.empty(T, es, device=dev, dtype=dt_)
         conv_final = conv_out if conv_out is not None else torch.empty(B, es, k - 1, device=dev, dtype=dt_)

@@ -25,6 +25,7 @@
 #include <vector>
 #include "common.cuh"
 #include "comm_dev.cuh"
+#include "wire.cuh"
 
 namespace mtp {
 
@@ -40,17 +41,6 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-// Per-row int8 quantisation (tp_utils.py:111-112), IEEE divide and round-half-even.
-__device__ __forceinline__ float row_scale(float amax) { return __fdiv_rn(fmaxf(amax, 1e-8f), 127.0f); }
-__device__ __forceinline__ int quant1(float x, float scale) {
-  float r = rintf(__fdiv_rn(x, scale));
-  r = fminf(fmaxf(r, -127.0f), 127.0f);
-  return (int)r;
-}
-__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
-  return (uint32_t)(a & 0xff) | ((uint32_t)(b & 0xff) << 8) | ((uint32_t)(c & 0xff) << 16) | ((uint32_t)(d & 0xff) << 24);
-}
-__device__ __forceinline__ float unpack_i8(uint32_t w, int i) { return (float)(int8_t)((w >> (8 * i)) & 0xffu); }
 
 // Row amax of a fp32 row (warp).
 __device__ __forceinline__ float row_amax(const float *row, int cols, int lane) {
@@ -174,11 +164,6 @@ struct EpiOut {
   int wide;             // rows take the 16-column granule layout (RMSNorm sum order of WideOps)
 };
 
-// Round to the collective's return dtype: the reference's reductions return the
-// model dtype (tp_utils.py:42, :131), so a bf16 model sees bf16-rounded sums.
-__device__ __forceinline__ float rnd_rdt(float x, int rdt) {
-  return rdt == MTP_BF16 ? __bfloat162float(__float2bfloat16_rn(x)) : x;
-}
 
 __device__ __forceinline__ float ld_any(const void *p, int dtype, size_t i) {
   return dtype == MTP_F32 ? ((const float *)p)[i] : __bfloat162float(((const __nv_bfloat16 *)p)[i]);
@@ -455,8 +440,6 @@ __device__ __forceinline__ float rowv_amax(const RowV<VPL> &R) {
   return warp_max(m);
 }
 
-__device__ __forceinline__ float dq1(float x, float s) { return __fadd_rn(0.f, __fmul_rn((float)quant1(x, s), s)); }
-__device__ __forceinline__ float h1(float x) { return __half2float(__float2half_rn(x)); }
 
 // world size 1: the wire format's round trip alone, in registers
 template <int MODE, int VPL>
@@ -1123,7 +1106,7 @@ __global__ void __launch_bounds__(WPB * 32, Ops::MINB) reduce_pipe_kernel(CommDe
     if (j == 0) rec_sm = atomicAdd(d.trace_count, 1u);
     else rec_sm = atomicAdd(d.trace_count + 1, 1u);
     unsigned long long *rec = d.trace + (size_t)(rec_sm % (unsigned)d.trace_cap) * TRACE_WORDS;
-    if (j == 0) { rec[0] = G; rec[1] = K; rec[2] = two_shot; }
+    if (j == 0) { rec[0] = G; rec[1] = K; rec[2] = (unsigned long long)two_shot | ((unsigned long long)site << 8); }
     tr = rec + 3 + (j == 0 ? 0 : 64);
     tr[tn++] = globaltimer_ns();
   }
@@ -1492,6 +1475,66 @@ static int run_reduce(mtp_comm *c, int site, int mode, const float *partial, int
   return MTP_OK;
 }
 
+// ----------------------------------------------------------------- x_proj reduction finished after the GEMM
+// Second half of AllReduce #1 when the x_proj GEMM's epilogue wrote the wire rows into
+// every rank's receive slots (gemm_tc_xproj_wire): wait (bounded) for the phase-0 flags
+// of all Gg GEMM CTAs of every rank, reduce every row over the ranks in rank order (one
+// warp per row, the reduction kernels' own arithmetic), round and split into dt_low | B|C;
+// the last CTA to leave advances the site's epoch.
+template <class Ops>
+__global__ void __launch_bounds__(WPB * 32) xproj_finish_kernel(CommDev d, int site, int Gg, int rows, int cols,
+                                                                EpiOut e) {
+  MTP_PDL_WAIT();
+  MTP_PDL_TRIGGER();
+  __shared__ int abort_sm;
+  __shared__ uint32_t epoch_sm;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int j = blockIdx.x, G = gridDim.x;
+  uint32_t *ep = reinterpret_cast<uint32_t *>(d.peer[d.rank] + d.off_epoch) + site;
+  if (threadIdx.x == 0) {
+    abort_sm = 0;
+    epoch_sm = *reinterpret_cast<volatile uint32_t *>(ep) + 1u;
+  }
+  __syncthreads();
+  const uint32_t epoch = epoch_sm;
+  const unsigned long long t0 = globaltimer_ns();  // one bound for all of this CTA's waits
+  volatile int *ab = &abort_sm;
+  for (int i = threadIdx.x; i < d.ws * Gg && !*ab; i += blockDim.x) {
+    const uint32_t *f = flag_ptr(d.peer[d.rank], d, site, 0, i / Gg, i % Gg);
+    uint32_t it = 0;
+    while ((int)(ld_acquire_sys(f) - epoch) < 0) {
+      if ((++it & 63u) == 0 && (*ab || globaltimer_ns() - t0 > d.timeout_ns)) {
+        if (!*ab) atomicExch(reinterpret_cast<int *>(d.peer[d.rank] + d.off_status), MTP_ERR_TIMEOUT);
+        *ab = 1;
+        break;
+      }
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (!abort_sm) {
+    const size_t half = (size_t)(epoch & 1u) * d.ws * d.slot_bytes[site];
+    char *slots[MAX_WS];
+    for (int k = 0; k < d.ws; ++k) slots[k] = d.peer[d.rank] + d.off_recv[site] + half + (size_t)k * d.slot_bytes[site];
+    typename Ops::Row R;
+    for (int r = j * WPB + warp; r < rows; r += G * WPB) {
+      Ops::reduce(slots, d.ws, r, rows, cols, lane, R);
+      Ops::round(R, e.rdt);
+      Ops::epilogue(e, R, r, cols, lane);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    unsigned int *done = reinterpret_cast<unsigned int *>(d.peer[d.rank] + d.off_done) + site;
+    if (atomicAdd(done, 1u) == (unsigned)G - 1u) {
+      *done = 0u;
+      *reinterpret_cast<volatile uint32_t *>(ep) = epoch;
+      __threadfence();
+    }
+  }
+}
+
 // ----------------------------------------------------------------- vocabulary-column gather
 // Vocabulary-parallel lm_head: rank k holds logits columns [k shard, min(V, (k+1) shard)) of
 // every row (shard = vocab_shard()); one launch gives every rank all of them.  Element units
@@ -1573,6 +1616,7 @@ int vocab_shard(int V, int ws) {
 
 int gemm_cols_as_full(const void *A, const void *B, void *C, int M, int N_full, int col0, int cols, int K, int lda,
                       int ldb, int ldc, int dtype, cudaStream_t s);
+bool gemm_tc_eligible(const void *A, const void *B, int M, int N, int K, int lda, int ldb);
 
 }  // namespace mtp
 
@@ -1801,6 +1845,75 @@ int mtp_dequant_sum(const uint8_t *payloads, int ws, int rows, int cols, float *
   const size_t n = (size_t)rows * cols;
   launch_pdl(dequant_sum_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, (cudaStream_t)stream, payloads, ws, rows, cols, out);
   return check_launch("dequant_sum");
+}
+
+int mtp_xproj_fused(mtp_comm *c, int mode, const void *xc, int ld_xc, const void *w, int ld_w, int ab_dtype, int rows,
+                    int N, int K, int R, float *partial, void *dt_low, int dt_dtype, float *bc, void *stream) {
+  MTP_REQUIRE(xc && w && dt_low && bc && rows >= 0 && N > R && R > 0 && K > 0, "bad arguments");
+  MTP_REQUIRE(mode == MTP_RED_FP32 || mode == MTP_RED_FP16 || mode == MTP_RED_INT8TOK, "unknown reduction mode");
+  MTP_REQUIRE(dt_dtype == MTP_F32 || dt_dtype == MTP_BF16, "dt_low must be F32 or BF16");
+  if (rows == 0) return MTP_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const bool has_comm = c && c->d.ws > 1;
+  const char *fenv = getenv("MTP_XPROJ_FUSED");
+  const bool fused_on = !(fenv && fenv[0] == '0');
+  MTP_REQUIRE(ab_dtype == MTP_F32 || ab_dtype == MTP_BF16, "xc / w must be F32 or BF16");
+  const bool fused = fused_on && ab_dtype == MTP_BF16 && gemm_tc_eligible(xc, w, rows, N, K, ld_xc, ld_w) && N % 16 == 0 && N <= 192 &&
+                     R % 16 == 0 && aligned16(dt_low) && aligned16(bc) &&
+                     (!has_comm || (c->opened && N <= c->cols[0] && rows <= c->max_rows && c->max_ctas == 0));
+  if (!fused) {  // the GEMM into the fp32 partial, then the reduction kernel
+    MTP_REQUIRE(partial, "this x_proj shape needs the fp32 partial buffer");
+    int rc = mtp_gemm(xc, w, partial, rows, N, K, ld_xc, ld_w, N, ab_dtype, MTP_F32, MTP_EPI_STORE, nullptr, 0, stream);
+    if (rc) return rc;
+    return mtp_reduce_xproj(c, mode, partial, rows, R, N - R, dt_low, dt_dtype, bc, stream);
+  }
+  XprojWire x{};
+  x.wmode = mode;
+  x.rdt = dt_dtype;
+  x.R = R;
+  x.dt_dtype = dt_dtype;
+  x.ws = has_comm ? c->d.ws : 1;
+  x.rank = has_comm ? c->d.rank : 0;
+  x.dt_low = dt_low;
+  x.bc = bc;
+  const int site = 0;
+  if (has_comm) {
+    const CommDev &d = c->d;
+    for (int k = 0; k < d.ws; ++k) {
+      x.wslot[k] = d.peer[k] + d.off_recv[site] + (size_t)d.rank * d.slot_bytes[site];
+      x.wflag[k] = reinterpret_cast<uint32_t *>(d.peer[k] + d.off_flags) +
+                   ((size_t)(site * NPHASE + 0) * MAX_WS + d.rank) * G_MAX;
+    }
+    x.whalf = (unsigned long long)d.ws * d.slot_bytes[site];
+    x.wepoch = reinterpret_cast<const uint32_t *>(d.peer[d.rank] + d.off_epoch) + site;
+  }
+  int Gg = 0;
+  int rc = gemm_tc_xproj_wire(xc, w, rows, N, K, ld_xc, ld_w, x, &Gg, s);
+  if (rc || !has_comm) return rc;
+  MTP_REQUIRE(Gg <= G_MAX, "GEMM grid exceeds the flag slots");
+  EpiOut e{};
+  e.dt_low = dt_low;
+  e.bc = bc;
+  e.R = R;
+  e.dt_dtype = dt_dtype;
+  e.rdt = dt_dtype;
+  const int sms = num_sms();
+  int G = ceil_div(rows, WPB);
+  if (G > 2 * sms) G = 2 * sms;
+  const int vpl = N <= 128 ? 1 : 2;  // 4 values per lane per chunk: 128 columns per chunk
+  CommDev d = c->d;
+#define MTP_XF(M, V) launch_pdl(xproj_finish_kernel<NarrowOps<M, EPI_XPROJ, V>>, dim3(G), dim3(WPB * 32), 0, s, d, site, Gg, rows, N, e)
+#define MTP_XF_MODE(V)                                      \
+  do {                                                      \
+    if (mode == MTP_RED_FP32) MTP_XF(MTP_RED_FP32, V);      \
+    else if (mode == MTP_RED_FP16) MTP_XF(MTP_RED_FP16, V); \
+    else MTP_XF(MTP_RED_INT8TOK, V);                        \
+  } while (0)
+  if (vpl == 1) MTP_XF_MODE(1);
+  else MTP_XF_MODE(2);
+#undef MTP_XF_MODE
+#undef MTP_XF
+  return check_launch("xproj_finish");
 }
 
 int mtp_vocab_shard(int V, int world_size, int rank, int *col0, int *cols) {

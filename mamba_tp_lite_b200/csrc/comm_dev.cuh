@@ -19,7 +19,7 @@ constexpr int NPHASE = 4;   // flag phases per site
 
 // Phase trace of the pipelined reductions (off unless mtp_comm_set_trace allocated it):
 // per launch one record of TRACE_WORDS u64 written by thread 0 of CTA 0 and of the last
-// CTA: [0] grid, [1] rounds, [2] protocol; then per CTA (CTA 0 at 3, the last at 3 + 64)
+// CTA: [0] grid, [1] rounds, [2] protocol (bit 0) and site (bits 8+); then per CTA (CTA 0 at 3, the last at 3 + 64)
 // the %globaltimer at start and after each event of each round.
 constexpr int TRACE_WORDS = 131;
 

@@ -15,6 +15,7 @@
 #include <cuda.h>
 #include "common.cuh"
 #include "tc_common.cuh"
+#include "wire.cuh"
 
 namespace mtp {
 namespace tc {
@@ -44,6 +45,8 @@ struct Params {
   uint32_t idesc;
   int vec_ok;     // 16-byte vector stores allowed
   int tma_store;  // the epilogue stages 32 x 16 chunks in shared memory and writes them with TMA
+  int wire;       // x_proj reduction epilogue (one N tile holds whole rows; C is not written)
+  XprojWire x;
 };
 
 __device__ __forceinline__ void tile_coords(const Params &p, int t, int &mt, int &nt) {
@@ -170,6 +173,79 @@ __device__ __forceinline__ void tma_store_chunk(const CUtensorMap *tm, uint32_t 
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
 
+// x_proj reduction epilogue for 16 accumulator columns [n0, n0+16) of row `row`.  World
+// size 1: the wire format's round trip (as the reduction kernels' world-size-1 path),
+// rounded to the reduction's return dtype, split into dt_low (columns < R) and B|C.
+// World size > 1: the wire row is written into every rank's receive slot (int8: per-row
+// scale s, written by the chunk-0 thread, and the int8 bytes; fp16 / fp32 values), in the
+// layout the reduction kernels read (tp_utils.py:113).
+__device__ __forceinline__ void wire_chunk(const Params &p, int row, int n0, const float (&v)[16], float s,
+                                           unsigned long long half) {
+  if (p.x.ws <= 1) {
+    float o[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float x = p.x.wmode == MTP_RED_INT8TOK ? dq1(v[i], s) : p.x.wmode == MTP_RED_FP16 ? h1(v[i]) : v[i];
+      o[i] = rnd_rdt(x, p.x.rdt);
+    }
+    if (n0 < p.x.R) {
+      if (p.x.dt_dtype == MTP_F32) {
+        float4 *d = reinterpret_cast<float4 *>((float *)p.x.dt_low + (size_t)row * p.x.R + n0);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) d[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+      } else {
+        uint32_t w[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
+          w[i] = *reinterpret_cast<uint32_t *>(&h2);
+        }
+        uint4 *d = reinterpret_cast<uint4 *>((__nv_bfloat16 *)p.x.dt_low + (size_t)row * p.x.R + n0);
+        d[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        d[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      }
+    } else {
+      float4 *d = reinterpret_cast<float4 *>(p.x.bc + (size_t)row * (p.N - p.x.R) + (n0 - p.x.R));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) d[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+    }
+    return;
+  }
+  uint32_t q[4];
+  uint4 hv[2];
+  if (p.x.wmode == MTP_RED_INT8TOK) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      q[i] = pack4(quant1(v[4 * i], s), quant1(v[4 * i + 1], s), quant1(v[4 * i + 2], s), quant1(v[4 * i + 3], s));
+  } else if (p.x.wmode == MTP_RED_FP16) {
+    uint32_t w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      __half2 h2 = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+      w[i] = *reinterpret_cast<uint32_t *>(&h2);
+    }
+    hv[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    hv[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
+  for (int k = 0; k < p.x.ws; ++k) {
+    char *dst = p.x.wslot[(p.x.rank + k) % p.x.ws] + half;  // stagger destinations across ranks
+    if (p.x.wmode == MTP_RED_INT8TOK) {
+      if (n0 == 0) reinterpret_cast<float *>(dst)[row] = s;
+      uint32_t *d = reinterpret_cast<uint32_t *>(dst + (size_t)4 * p.M + (size_t)row * p.N + n0);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) d[i] = q[i];
+    } else if (p.x.wmode == MTP_RED_FP16) {
+      uint4 *d = reinterpret_cast<uint4 *>(dst + 2 * ((size_t)row * p.N + n0));
+      d[0] = hv[0];
+      d[1] = hv[1];
+    } else {
+      float4 *d = reinterpret_cast<float4 *>(dst + 4 * ((size_t)row * p.N + n0));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) d[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const Params p) {
@@ -215,6 +291,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   MTP_PDL_TRIGGER();
   const uint32_t tmem_base = *tmem_holder;
   const int num_kb = (p.K + BK - 1) / BK;
+  // x_proj reduction epilogue over peer memory: the epoch of this reduction (the finishing
+  // kernel advances the site's epoch word after this launch, so it cannot change here)
+  const uint32_t wire_epoch = (p.wire && p.x.ws > 1) ? *reinterpret_cast<volatile const uint32_t *>(p.x.wepoch) + 1u : 0u;
   const uint32_t tx_bytes = (uint32_t)(A_BYTES + p.bn * BK * 2);
 
   if (warp == 0) {
@@ -315,7 +394,42 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (lane == 0 && m0 < p.M) tma_store_chunk(&tmC, smem_u32(buf), n0, m0);
     };
     int local = 0;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
+    if (p.wire) {
+      // whole rows per tile: every warp of a lane quarter reads all the row's columns for the
+      // row absmax (TMEM reads are cheap; no cross-warp exchange), then writes its own chunks
+      const int nch = p.N / 16;
+      const unsigned long long half = (wire_epoch & 1u) ? p.x.whalf : 0ull;
+      for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
+        const int a = local & 1;
+        const uint32_t use = (uint32_t)(local >> 1);
+        if (!mbar_wait(tfull_bar(a), use & 1u, abort, p.timeout_ns)) break;
+        tc_fence_after();
+        int mt, nt;
+        tile_coords(p, t, mt, nt);
+        const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN_MAX);
+        const int row = mt * BM + q * 32 + lane;
+        float s = 0.f;
+        if (p.x.wmode == MTP_RED_INT8TOK) {
+          float m = 0.f;
+          for (int jc = 0; jc < nch; ++jc) {
+            float v[16];
+            tmem_ld16(tbase + (uint32_t)(16 * jc), v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v[i]));
+          }
+          s = row_scale(m);
+        }
+        for (int jc = part; jc < nch; jc += EPI_PARTS) {
+          float v[16];
+          tmem_ld16(tbase + (uint32_t)(16 * jc), v);
+          if (row < p.M) wire_chunk(p, row, 16 * jc, v, s, half);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tempty_bar(a));
+      }
+    }
+    for (int t = blockIdx.x; t < (p.wire ? 0 : p.num_tiles); t += gridDim.x, ++local) {
       const int a = local & 1;
       const uint32_t use = (uint32_t)(local >> 1);
       if (!mbar_wait(tfull_bar(a), use & 1u, abort, p.timeout_ns)) break;
@@ -354,6 +468,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   if (threadIdx.x == 0 && *abort) atomicExch(p.err, MTP_ERR_TIMEOUT);
+  // x_proj reduction over peer memory: every epilogue store of this CTA is ordered before
+  // the flags by the barrier above, then one system fence and release store per rank
+  if (p.wire && p.x.ws > 1 && threadIdx.x < (unsigned)p.x.ws && !*abort) {
+    __threadfence_system();
+    st_release_sys(p.x.wflag[threadIdx.x] + blockIdx.x, wire_epoch);
+  }
   if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
 }
 
@@ -431,6 +551,53 @@ int gemm_tc(const void *A, const void *B, void *C, int M, int N, int K, int lda,
   launch_pdl(gemm_tc_kernel, dim3(grid), dim3(NUM_THREADS), p.tma_store ? SMEM_BYTES_TMA_STORE : SMEM_BYTES, stream,
              ta, tb, tcm, p);
   return check_launch("gemm_tc");
+}
+
+// The x_proj GEMM with the reduction epilogue (see wire_chunk): C is not written.  Returns
+// the grid size through *grid_out (the finishing kernel waits for that many CTAs per rank).
+int gemm_tc_xproj_wire(const void *A, const void *B, int M, int N, int K, int lda, int ldb, const XprojWire &w,
+                       int *grid_out, cudaStream_t stream) {
+  using namespace tc;
+  MTP_REQUIRE(gemm_tc_eligible(A, B, M, N, K, lda, ldb),
+              "tcgen05 GEMM needs 16-byte aligned A/B, K >= 8 and lda, ldb multiples of 8");
+  MTP_REQUIRE(N % 16 == 0 && N <= 192 && w.R % 16 == 0 && w.R > 0 && w.R < N, "x_proj epilogue: bad widths");
+  Params p{};
+  p.x = w;
+  p.wire = 1;
+  p.C = nullptr;
+  p.bias = nullptr;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ldc = N;
+  p.c_dtype = MTP_F32;
+  p.epi = MTP_EPI_STORE;
+  p.bn = N;  // one N tile: whole rows
+  p.tiles_m = ceil_div(M, BM);
+  p.tiles_n = 1;
+  p.num_tiles = p.tiles_m;
+  p.group_m = 32;
+  p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+  p.vec_ok = 0;
+  p.tma_store = 0;
+  p.timeout_ns = 2000000000ull;
+  p.err = device_err_word();
+  if (!p.err) return fail(MTP_ERR_CUDA, "could not allocate the GEMM status word");
+  CUtensorMap ta, tb, tcm;
+  int rc = make_tmap(&ta, A, M, K, lda, BM);
+  if (rc) return rc;
+  rc = make_tmap(&tb, B, N, K, ldb, p.bn);
+  if (rc) return rc;
+  memset(&tcm, 0, sizeof(tcm));
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES_TMA_STORE);
+    attr = true;
+  }
+  const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
+  *grid_out = grid;
+  launch_pdl(gemm_tc_kernel, dim3(grid), dim3(NUM_THREADS), SMEM_BYTES, stream, ta, tb, tcm, p);
+  return check_launch("gemm_tc_xproj");
 }
 
 int gemm_tc_status(int *status) {

@@ -159,7 +159,7 @@ class Comm:
 
     def read_trace(self) -> list[dict]:
         """The recorded launches in launch order (after a synchronize).  Per launch: the
-        protocol, the rounds, and for CTA 0 and the last CTA the kernel time and the time
+        site, the protocol, the rounds, and for CTA 0 and the last CTA the kernel time and the time
         spent in the bounded flag waits (``wait_us``: waiting for the peers' pushes, and
         in the two-shot protocol for the owners' gathered rows), i.e. the part of the
         collective that waited for other ranks rather than moving or reducing bytes."""
@@ -170,13 +170,14 @@ class Comm:
         out = []
         for i in range(min(n.value, cap)):
             rec = buf[i * TRACE_WORDS:(i + 1) * TRACE_WORDS]
-            two, rounds = bool(rec[2]), int(rec[1])
+            two, rounds, site = bool(rec[2] & 1), int(rec[1]), int(rec[2] >> 8)
             ctas = []
             for base in (3, 67):
                 st = [v for v in rec[base:base + 64] if v]
                 if st:
                     ctas.append(_trace_waits(st, two, rounds))
-            out.append({"two_shot": two, "rounds": rounds, "grid": int(rec[0]), "ctas": ctas})
+            out.append({"site": SITES[site] if site < len(SITES) else site, "two_shot": two, "rounds": rounds,
+                        "grid": int(rec[0]), "ctas": ctas})
         return out
 
     def check(self) -> None:

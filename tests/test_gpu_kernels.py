@@ -376,6 +376,65 @@ def test_reduce_xproj_split():
     np.testing.assert_array_equal(n(bc), O.bf16_round(part[:, R:]))
 
 
+XPROJ_CASES = [  # (rows, R, 2N, K): the 1.4b / 2.8b / 370m / 130m x_proj sites, a ragged last tile, tiny M
+    (32768, 128, 32, 4096), (4100, 160, 32, 640), (1000, 64, 32, 2048), (777, 48, 32, 1536), (37, 16, 32, 256)]
+
+
+@pytest.mark.parametrize("rows,R,N2,K", XPROJ_CASES)
+@pytest.mark.parametrize("mode", [L.RED_FP32, L.RED_FP16, L.RED_INT8TOK])
+@pytest.mark.parametrize("dt_dtype", [L.BF16, L.F32])
+def test_xproj_gemm_epilogue_equals_gemm_then_reduce(rows, R, N2, K, mode, dt_dtype):
+    """World size 1: the x_proj GEMM whose epilogue applies AllReduce #1's wire round
+    trip and the dt | B|C split gives the bits of the GEMM into an fp32 partial followed
+    by the reduction kernel (tp_model.py:106-108), with 1% outlier columns."""
+    N = R + N2
+    g = torch.Generator(device="cpu").manual_seed(rows + R + mode)
+    xc = torch.randn(rows, K, generator=g).to(dev(), BF)
+    w = (torch.randn(N, K, generator=g) * 0.05)
+    w[:, torch.randperm(N, generator=g)[:max(1, N // 100)]] *= 20
+    w = w.to(dev(), BF)
+    tdt = BF if dt_dtype == L.BF16 else torch.float32
+    part = torch.empty(rows, N, device=dev())
+    L.call("mtp_gemm", L.ptr(xc), L.ptr(w), L.ptr(part), rows, N, K, K, K, N, L.BF16, L.F32, L.EPI_STORE, None, 0,
+           L.stream_ptr())
+    dl_ref = torch.empty(rows, R, device=dev(), dtype=tdt)
+    bc_ref = torch.empty(rows, N2, device=dev())
+    L.call("mtp_reduce_xproj", None, mode, L.ptr(part), rows, R, N2, L.ptr(dl_ref), dt_dtype, L.ptr(bc_ref),
+           L.stream_ptr())
+    dl = torch.full((rows, R), float("nan"), device=dev(), dtype=tdt)
+    bc = torch.full((rows, N2), float("nan"), device=dev())
+    launches = L.launch_count()
+    L.call("mtp_xproj_fused", None, mode, L.ptr(xc), K, L.ptr(w), K, L.BF16, rows, N, K, R, None, L.ptr(dl), dt_dtype,
+           L.ptr(bc), L.stream_ptr())
+    assert L.launch_count() - launches == 1  # one kernel: no fp32 partial, no reduction launch
+    torch.cuda.synchronize()
+    assert torch.equal(dl, dl_ref) and torch.equal(bc, bc_ref)
+
+
+def test_xproj_fused_falls_back_for_other_shapes():
+    """Widths the epilogue form does not take (N not a multiple of 16) run the GEMM into
+    the caller's partial and the reduction kernel: the same results as calling both."""
+    rows, R, N2, K = 300, 40, 30, 512
+    N = R + N2
+    xc = torch.randn(rows, K, device=dev(), dtype=BF)
+    w = torch.randn(N, K, device=dev(), dtype=BF) * 0.05
+    part = torch.empty(rows, N, device=dev())
+    dl = torch.empty(rows, R, device=dev(), dtype=BF)
+    bc = torch.empty(rows, N2, device=dev())
+    L.call("mtp_xproj_fused", None, L.RED_INT8TOK, L.ptr(xc), K, L.ptr(w), K, L.BF16, rows, N, K, R, L.ptr(part),
+           L.ptr(dl), L.BF16, L.ptr(bc), L.stream_ptr())
+    part2 = gemm(xc, w, torch.float32)
+    dl2 = torch.empty_like(dl)
+    bc2 = torch.empty_like(bc)
+    L.call("mtp_reduce_xproj", None, L.RED_INT8TOK, L.ptr(part2), rows, R, N2, L.ptr(dl2), L.BF16, L.ptr(bc2),
+           L.stream_ptr())
+    torch.cuda.synchronize()
+    assert torch.equal(dl, dl2) and torch.equal(bc, bc2)
+    with pytest.raises(L.MTPError):
+        L.call("mtp_xproj_fused", None, L.RED_INT8TOK, L.ptr(xc), K, L.ptr(w), K, L.BF16, rows, N, K, R, None,
+               L.ptr(dl), L.BF16, L.ptr(bc), L.stream_ptr())
+
+
 def test_embedding_rmsnorm_argmax():
     V, D = 1000, 256
     table = torch.randn(V, D, device=dev(), dtype=BF)

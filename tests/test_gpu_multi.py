@@ -9,7 +9,8 @@ world sizes 2, 4 and 8 (each skipped when the box has fewer GPUs):
   results on every rank, graphed decode equals eager decode bitwise, and the persistent
   decode kernel agrees with the per-layer chain;
 * the vocabulary-parallel lm_head gives the replicated lm_head's logits and greedy tokens,
-  bitwise;
+  bitwise; so does the x_proj GEMM with AllReduce #1 in its epilogue against the GEMM
+  followed by the reduction kernel;
 * the out_proj epilogue gives the same bits through one-shot, two-shot and capped grids,
   and the overlapped micro-batch prefill equals the serial prefill bitwise.
 
@@ -172,6 +173,21 @@ def _suite(rank, init_file, q, ws):
                                                   _digest(st.float().cpu().numpy()), toks.cpu().numpy())
             os.environ.pop("MTP_VOCAB_PARALLEL_ROWS")
             del m
+        # ---- x_proj GEMM with AllReduce #1 in its epilogue == GEMM + reduction kernel, bitwise
+        out["xfused"] = {}
+        sd = random_init_state_dict(cfg, seed=6, dtype=torch.bfloat16)
+        spec = build_spec({"default": "int8", "overrides": {"1:x_proj": "fp32", "2:x_proj": "fp16"}}, cfg.n_layer)
+        m = TPMambaLM.from_state_dict_shard(cfg, sd, rank, ws, dtype=torch.bfloat16, allreduce_dtype=spec,
+                                            device="cuda")
+        ids3 = torch.randint(0, cfg.vocab_size, (4, 520), generator=torch.Generator().manual_seed(11)).cuda()
+        for fz in ("0", "1"):
+            os.environ["MTP_XPROJ_FUSED"] = fz
+            lg, cache = m.prefill(ids3)
+            out["xfused"][fz] = (_digest(lg.float().cpu().numpy()),
+                                 [_digest(lc.ssm_state.cpu().numpy()) for lc in cache.layers])
+        os.environ.pop("MTP_XPROJ_FUSED")
+        get_comm(None, rank, ws, cfg.dt_rank + 2 * cfg.d_state, cfg.d_model).check()
+        del m
         # ---- out_proj epilogue through one-shot, two-shot and a capped grid
         rows, d = 3000, 1024
         comm = get_comm(None, rank, ws, 48, d)
@@ -306,6 +322,20 @@ def test_vocab_parallel_lm_head_equals_replicated(ws):
             got, ref = res[r]["vocab"][(dtype, "256")], res[r]["vocab"][(dtype, "0")]
             assert got[:3] == ref[:3] == rep[:3], (dtype, r)
             assert np.array_equal(got[3], ref[3]) and np.array_equal(got[3], rep[3]), (dtype, r)
+
+
+# ------------------------------------------------------------------ x_proj reduction in the GEMM epilogue
+@pytest.mark.parametrize("ws", WS_LIST)
+def test_xproj_epilogue_reduction_equals_kernel_pair(ws):
+    """The x_proj GEMM that writes AllReduce #1's wire rows (int8 / fp32 / fp16 sites)
+    into every rank's slots plus the finishing reduction give the bits of the GEMM into
+    an fp32 partial followed by the reduction kernel, on every rank."""
+    if _ngpu() < ws:
+        pytest.skip(f"needs {ws} GPUs")
+    res = suite(ws)
+    ref = res[0]["xfused"]["0"]
+    for r in range(ws):
+        assert res[r]["xfused"]["1"] == res[r]["xfused"]["0"] == ref, r
 
 
 # ------------------------------------------------------------------ protocols agree (out_proj epilogue, bf16 gather)
