@@ -247,8 +247,9 @@ int mtp_reduce_outproj(mtp_comm *c, int mode, const float *partial, int rows, in
  * over the ranks in rank order and splits it.  xc and w are ab_dtype (the fused form
  * needs MTP_BF16).  Bit-identical to mtp_gemm into `partial`
  * followed by mtp_reduce_xproj, which is what runs when the shape does not fit the fused
- * form (N % 16, N <= 192, R % 16, 16-byte aligned operands and outputs, rows within the
- * context's slots, no grid cap; MTP_XPROJ_FUSED=0 forces it): `partial` [rows, N] fp32 is
+ * form (N % 16, N <= 192, R % 16, 16-byte aligned operands and outputs; at world size > 1
+ * the int8 wire only, rows within the context's slots, no grid cap; MTP_XPROJ_FUSED=0
+ * forces it): `partial` [rows, N] fp32 is
  * only used then and may be NULL for shapes that fit. */
 int mtp_xproj_fused(mtp_comm *c, int mode, const void *xc, int ld_xc, const void *w, int ld_w, int ab_dtype, int rows,
                     int N, int K, int R, float *partial, void *dt_low, int dt_dtype, float *bc, void *stream);

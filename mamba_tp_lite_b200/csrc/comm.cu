@@ -1860,7 +1860,8 @@ int mtp_xproj_fused(mtp_comm *c, int mode, const void *xc, int ld_xc, const void
   MTP_REQUIRE(ab_dtype == MTP_F32 || ab_dtype == MTP_BF16, "xc / w must be F32 or BF16");
   const bool fused = fused_on && ab_dtype == MTP_BF16 && gemm_tc_eligible(xc, w, rows, N, K, ld_xc, ld_w) && N % 16 == 0 && N <= 192 &&
                      R % 16 == 0 && aligned16(dt_low) && aligned16(bc) &&
-                     (!has_comm || (c->opened && N <= c->cols[0] && rows <= c->max_rows && c->max_ctas == 0));
+                     (!has_comm || (mode == MTP_RED_INT8TOK && c->opened && N <= c->cols[0] && rows <= c->max_rows &&
+                                    c->max_ctas == 0));
   if (!fused) {  // the GEMM into the fp32 partial, then the reduction kernel
     MTP_REQUIRE(partial, "this x_proj shape needs the fp32 partial buffer");
     int rc = mtp_gemm(xc, w, partial, rows, N, K, ld_xc, ld_w, N, ab_dtype, MTP_F32, MTP_EPI_STORE, nullptr, 0, stream);

@@ -173,76 +173,36 @@ __device__ __forceinline__ void tma_store_chunk(const CUtensorMap *tm, uint32_t 
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
 
-// x_proj reduction epilogue for 16 accumulator columns [n0, n0+16) of row `row`.  World
-// size 1: the wire format's round trip (as the reduction kernels' world-size-1 path),
+// x_proj reduction epilogue at world size 1 for 16 accumulator columns [n0, n0+16) of row
+// `row`: the wire format's round trip (as the reduction kernels' world-size-1 path),
 // rounded to the reduction's return dtype, split into dt_low (columns < R) and B|C.
-// World size > 1: the wire row is written into every rank's receive slot (int8: per-row
-// scale s, written by the chunk-0 thread, and the int8 bytes; fp16 / fp32 values), in the
-// layout the reduction kernels read (tp_utils.py:113).
-__device__ __forceinline__ void wire_chunk(const Params &p, int row, int n0, const float (&v)[16], float s,
-                                           unsigned long long half) {
-  if (p.x.ws <= 1) {
-    float o[16];
+__device__ __forceinline__ void wire_chunk_local(const Params &p, int row, int n0, const float (&v)[16], float s) {
+  float o[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float x = p.x.wmode == MTP_RED_INT8TOK ? dq1(v[i], s) : p.x.wmode == MTP_RED_FP16 ? h1(v[i]) : v[i];
-      o[i] = rnd_rdt(x, p.x.rdt);
-    }
-    if (n0 < p.x.R) {
-      if (p.x.dt_dtype == MTP_F32) {
-        float4 *d = reinterpret_cast<float4 *>((float *)p.x.dt_low + (size_t)row * p.x.R + n0);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) d[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-      } else {
-        uint32_t w[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          __nv_bfloat162 h2 = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
-          w[i] = *reinterpret_cast<uint32_t *>(&h2);
-        }
-        uint4 *d = reinterpret_cast<uint4 *>((__nv_bfloat16 *)p.x.dt_low + (size_t)row * p.x.R + n0);
-        d[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        d[1] = make_uint4(w[4], w[5], w[6], w[7]);
-      }
-    } else {
-      float4 *d = reinterpret_cast<float4 *>(p.x.bc + (size_t)row * (p.N - p.x.R) + (n0 - p.x.R));
+  for (int i = 0; i < 16; ++i) {
+    const float x = p.x.wmode == MTP_RED_INT8TOK ? dq1(v[i], s) : p.x.wmode == MTP_RED_FP16 ? h1(v[i]) : v[i];
+    o[i] = rnd_rdt(x, p.x.rdt);
+  }
+  if (n0 < p.x.R) {
+    if (p.x.dt_dtype == MTP_F32) {
+      float4 *d = reinterpret_cast<float4 *>((float *)p.x.dt_low + (size_t)row * p.x.R + n0);
 #pragma unroll
       for (int i = 0; i < 4; ++i) d[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-    }
-    return;
-  }
-  uint32_t q[4];
-  uint4 hv[2];
-  if (p.x.wmode == MTP_RED_INT8TOK) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      q[i] = pack4(quant1(v[4 * i], s), quant1(v[4 * i + 1], s), quant1(v[4 * i + 2], s), quant1(v[4 * i + 3], s));
-  } else if (p.x.wmode == MTP_RED_FP16) {
-    uint32_t w[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      __half2 h2 = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-      w[i] = *reinterpret_cast<uint32_t *>(&h2);
-    }
-    hv[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    hv[1] = make_uint4(w[4], w[5], w[6], w[7]);
-  }
-  for (int k = 0; k < p.x.ws; ++k) {
-    char *dst = p.x.wslot[(p.x.rank + k) % p.x.ws] + half;  // stagger destinations across ranks
-    if (p.x.wmode == MTP_RED_INT8TOK) {
-      if (n0 == 0) reinterpret_cast<float *>(dst)[row] = s;
-      uint32_t *d = reinterpret_cast<uint32_t *>(dst + (size_t)4 * p.M + (size_t)row * p.N + n0);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) d[i] = q[i];
-    } else if (p.x.wmode == MTP_RED_FP16) {
-      uint4 *d = reinterpret_cast<uint4 *>(dst + 2 * ((size_t)row * p.N + n0));
-      d[0] = hv[0];
-      d[1] = hv[1];
     } else {
-      float4 *d = reinterpret_cast<float4 *>(dst + 4 * ((size_t)row * p.N + n0));
+      uint32_t w[8];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) d[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      for (int i = 0; i < 8; ++i) {
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
+        w[i] = *reinterpret_cast<uint32_t *>(&h2);
+      }
+      uint4 *d = reinterpret_cast<uint4 *>((__nv_bfloat16 *)p.x.dt_low + (size_t)row * p.x.R + n0);
+      d[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      d[1] = make_uint4(w[4], w[5], w[6], w[7]);
     }
+  } else {
+    float4 *d = reinterpret_cast<float4 *>(p.x.bc + (size_t)row * (p.N - p.x.R) + (n0 - p.x.R));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
   }
 }
 
@@ -399,6 +359,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // row absmax (TMEM reads are cheap; no cross-warp exchange), then writes its own chunks
       const int nch = p.N / 16;
       const unsigned long long half = (wire_epoch & 1u) ? p.x.whalf : 0ull;
+      // int8 row block of this lane quarter (32 rows x N <= 192 bytes) in the TMA-store staging area
+      unsigned char *wstage = gbase + STAGES * STAGE_BYTES + 256 + (size_t)q * 6144;
       for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
         const int a = local & 1;
         const uint32_t use = (uint32_t)(local >> 1);
@@ -407,7 +369,59 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         int mt, nt;
         tile_coords(p, t, mt, nt);
         const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN_MAX);
-        const int row = mt * BM + q * 32 + lane;
+        const int row0 = mt * BM + q * 32, row = row0 + lane;
+        if (p.x.ws > 1) {
+          // int8 wire to the peers: the part-0 warp of the lane quarter quantises all of its 32
+          // rows into shared memory, releases the accumulator, then writes the rows' bytes as one
+          // contiguous block per rank (512 bytes per store instruction); the scales of the 32
+          // rows are 32 consecutive floats
+          if (part == 0) {
+            float m = 0.f;
+            for (int jc = 0; jc < nch; ++jc) {
+              float v[16];
+              tmem_ld16(tbase + (uint32_t)(16 * jc), v);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v[i]));
+            }
+            const float s = row_scale(m);
+            for (int jc = 0; jc < nch; ++jc) {
+              float v[16];
+              tmem_ld16(tbase + (uint32_t)(16 * jc), v);
+              uint4 w4;
+              w4.x = pack4(quant1(v[0], s), quant1(v[1], s), quant1(v[2], s), quant1(v[3], s));
+              w4.y = pack4(quant1(v[4], s), quant1(v[5], s), quant1(v[6], s), quant1(v[7], s));
+              w4.z = pack4(quant1(v[8], s), quant1(v[9], s), quant1(v[10], s), quant1(v[11], s));
+              w4.w = pack4(quant1(v[12], s), quant1(v[13], s), quant1(v[14], s), quant1(v[15], s));
+              *reinterpret_cast<uint4 *>(wstage + (size_t)lane * p.N + 16 * jc) = w4;
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty_bar(a));
+            const int nrows = p.M - row0 < 32 ? p.M - row0 : 32;
+            if (nrows > 0) {
+              const size_t bytes = (size_t)nrows * p.N;
+              for (int k = 0; k < p.x.ws; ++k) {
+                char *dst = p.x.wslot[(p.x.rank + k) % p.x.ws] + half;  // stagger destinations across ranks
+                if (lane < nrows) reinterpret_cast<float *>(dst)[row] = s;
+                char *blk = dst + (size_t)4 * p.M + (size_t)row0 * p.N;
+                if ((p.M & 3) == 0) {  // 16-byte aligned block
+                  for (size_t i = (size_t)lane * 16; i < bytes; i += 512)
+                    *reinterpret_cast<uint4 *>(blk + i) = *reinterpret_cast<const uint4 *>(wstage + i);
+                } else {
+                  for (size_t i = (size_t)lane * 4; i < bytes; i += 128)
+                    *reinterpret_cast<uint32_t *>(blk + i) = *reinterpret_cast<const uint32_t *>(wstage + i);
+                }
+              }
+            }
+            __syncwarp();  // the staging block is rewritten by the next tile
+          } else {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty_bar(a));
+          }
+          continue;
+        }
+        // world size 1: the three warps of the lane quarter split the 16-column chunks
         float s = 0.f;
         if (p.x.wmode == MTP_RED_INT8TOK) {
           float m = 0.f;
@@ -422,7 +436,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int jc = part; jc < nch; jc += EPI_PARTS) {
           float v[16];
           tmem_ld16(tbase + (uint32_t)(16 * jc), v);
-          if (row < p.M) wire_chunk(p, row, 16 * jc, v, s, half);
+          if (row < p.M) wire_chunk_local(p, row, 16 * jc, v, s);
         }
         tc_fence_before();
         __syncwarp();
@@ -553,7 +567,7 @@ int gemm_tc(const void *A, const void *B, void *C, int M, int N, int K, int lda,
   return check_launch("gemm_tc");
 }
 
-// The x_proj GEMM with the reduction epilogue (see wire_chunk): C is not written.  Returns
+// The x_proj GEMM with the reduction epilogue (wire_chunk_local, the int8 row blocks): C is not written.  Returns
 // the grid size through *grid_out (the finishing kernel waits for that many CTAs per rank).
 int gemm_tc_xproj_wire(const void *A, const void *B, int M, int N, int K, int lda, int ldb, const XprojWire &w,
                        int *grid_out, cudaStream_t stream) {
@@ -561,6 +575,8 @@ int gemm_tc_xproj_wire(const void *A, const void *B, int M, int N, int K, int ld
   MTP_REQUIRE(gemm_tc_eligible(A, B, M, N, K, lda, ldb),
               "tcgen05 GEMM needs 16-byte aligned A/B, K >= 8 and lda, ldb multiples of 8");
   MTP_REQUIRE(N % 16 == 0 && N <= 192 && w.R % 16 == 0 && w.R > 0 && w.R < N, "x_proj epilogue: bad widths");
+  MTP_REQUIRE(w.ws <= 1 || w.wmode == MTP_RED_INT8TOK, "x_proj epilogue over peer memory: int8 wire only");
+  static_assert(NUM_EPI_WARPS * STAGE_C_BYTES >= 4 * 6144, "staging area holds four 32 x 192-byte row blocks");
   Params p{};
   p.x = w;
   p.wire = 1;
@@ -596,7 +612,9 @@ int gemm_tc_xproj_wire(const void *A, const void *B, int M, int N, int K, int ld
   }
   const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
   *grid_out = grid;
-  launch_pdl(gemm_tc_kernel, dim3(grid), dim3(NUM_THREADS), SMEM_BYTES, stream, ta, tb, tcm, p);
+  // the peer path stages int8 row blocks in the TMA-store staging area (4 x 6 KB)
+  launch_pdl(gemm_tc_kernel, dim3(grid), dim3(NUM_THREADS), w.ws > 1 ? SMEM_BYTES_TMA_STORE : SMEM_BYTES, stream, ta,
+             tb, tcm, p);
   return check_launch("gemm_tc_xproj");
 }
 

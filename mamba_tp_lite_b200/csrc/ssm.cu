@@ -7,6 +7,7 @@
 // restating mamba_lite/tp_model.py:93-129 (prefill) and :145-173 (step).
 #include <cstdlib>
 #include <type_traits>
+#include <cstring>
 #include "common.cuh"
 #include "tc_common.cuh"
 
@@ -174,6 +175,89 @@ __global__ void conv1d_silu_vec_kernel(const T *__restrict__ xz, int ld_xz, cons
       o[u] = silu_fast(acc);  // as the scan's conv phase
     }
     Pack16<T>::store(xc + (size_t)(b * (size_t)L + t) * ld_xc + c, o);
+  }
+}
+
+// The vectorised conv with every input load of a thread issued before any arithmetic:
+// a thread owns V channels (one 16-byte word per position) of P consecutive positions and
+// first loads the P + K - 1 words it needs (the K - 1 halo re-read from L2 by the
+// neighbouring position block) into registers, so each thread has P + K - 1 independent
+// loads in flight instead of one per iteration -- the direct kernel above is bound by
+// load latency, not bandwidth.  Same arithmetic, in the same order, as conv1d_silu_vec_kernel.
+template <typename T, int K, int P>
+__global__ void __launch_bounds__(128) conv1d_silu_batch_kernel(const T *__restrict__ xz, int ld_xz,
+                                                                const T *__restrict__ w, const T *__restrict__ bias,
+                                                                const T *__restrict__ hist, T *__restrict__ xc,
+                                                                int ld_xc, int L, int Es, bool wvec) {
+  MTP_PDL_WAIT();
+  MTP_PDL_TRIGGER();
+  constexpr int V = Pack16<T>::V;
+  constexpr int W = P + K - 1;  // input words per thread
+  static_assert(V * K * sizeof(T) == 64, "a group's taps are four 16-byte words");
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * V;
+  const int t0 = blockIdx.y * P;
+  const int b = blockIdx.z;
+  if (c >= Es) return;
+  // every input word first (positions t0 - K + 1 .. t0 + P - 1); out of range: zero, and
+  // positions before the sequence start come from the history below
+  uint4 raw[W];
+  const T *xb = xz + (size_t)b * L * ld_xz + c;
+#pragma unroll
+  for (int i = 0; i < W; ++i) {
+    const int t = t0 - (K - 1) + i;
+    raw[i] = (t >= 0 && t < L) ? __ldg(reinterpret_cast<const uint4 *>(xb + (size_t)t * ld_xz)) : make_uint4(0, 0, 0, 0);
+  }
+  float wk[V][K], bc[V];
+  if (wvec) {
+    T tw[V * K], tb[V];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) reinterpret_cast<uint4 *>(tw)[q] = __ldg(reinterpret_cast<const uint4 *>(w + (size_t)c * K) + q);
+    if (bias) *reinterpret_cast<uint4 *>(tb) = __ldg(reinterpret_cast<const uint4 *>(bias + c));
+#pragma unroll
+    for (int u = 0; u < V; ++u) {
+#pragma unroll
+      for (int j = 0; j < K; ++j) wk[u][j] = ldf(&tw[u * K + j]);
+      bc[u] = bias ? ldf(&tb[u]) : 0.f;
+    }
+  } else {
+#pragma unroll
+    for (int u = 0; u < V; ++u) {
+#pragma unroll
+      for (int j = 0; j < K; ++j) wk[u][j] = ldf(w + (size_t)(c + u) * K + j);
+      bc[u] = bias ? ldf(bias + c + u) : 0.f;
+    }
+  }
+  float win[V][K - 1];
+#pragma unroll
+  for (int j = 0; j < K - 1; ++j) {
+    const int t = t0 - (K - 1) + j;
+    if (t >= 0) {
+      float v[V];
+      Pack16<T>::load(reinterpret_cast<const T *>(&raw[j]), v);
+#pragma unroll
+      for (int u = 0; u < V; ++u) win[u][j] = v[u];
+    } else {
+#pragma unroll
+      for (int u = 0; u < V; ++u) win[u][j] = hist ? ldf(hist + ((size_t)b * Es + c + u) * (K - 1) + (K - 1 + t)) : 0.f;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < P; ++i) {
+    const int t = t0 + i;
+    float xv[V], o[V];
+    Pack16<T>::load(reinterpret_cast<const T *>(&raw[K - 1 + i]), xv);
+#pragma unroll
+    for (int u = 0; u < V; ++u) {
+      float acc = bc[u];
+#pragma unroll
+      for (int j = 0; j < K - 1; ++j) acc = fmaf(wk[u][j], win[u][j], acc);
+      acc = fmaf(wk[u][K - 1], xv[u], acc);
+#pragma unroll
+      for (int j = 0; j < K - 2; ++j) win[u][j] = win[u][j + 1];
+      win[u][K - 2] = xv[u];
+      o[u] = silu_fast(acc);
+    }
+    if (t < L) Pack16<T>::store(xc + ((size_t)b * L + t) * ld_xc + c, o);
   }
 }
 
@@ -1139,6 +1223,25 @@ int mtp_conv1d_silu(const void *xz, int ld_xz, const void *conv_w, const void *c
       const char *e = getenv("MTP_CONV_STAGED");
       return e && e[0] == '1';
     }();
+    // default: all of a thread's loads issued first (MTP_CONV_KERNEL=direct: the
+    // 64-position loop above)
+    const char *ek = getenv("MTP_CONV_KERNEL");  // read per call: tests switch it
+    const bool direct = ek && !strcmp(ek, "direct");
+    const char *ep = getenv("MTP_CONV_P");  // positions per thread: 8 (128 registers, 4 CTAs per SM) or 16
+    const int pos = ep && atoi(ep) == 16 ? 16 : 8;
+    if (!staged && !direct) {
+      constexpr int NB = 128;
+      dim3 g2((groups + NB - 1) / NB, (L + pos - 1) / pos, B);
+      if (pos == 16)
+        MTP_DISPATCH_FB(dtype, T,
+            launch_pdl(conv1d_silu_batch_kernel<T, 4, 16>, dim3(g2), dim3(NB), 0, s, (const T *)xz, ld_xz,
+                       (const T *)conv_w, (const T *)conv_b, (const T *)hist, (T *)xc, ld_xc, L, Es, wvec));
+      else
+        MTP_DISPATCH_FB(dtype, T,
+            launch_pdl(conv1d_silu_batch_kernel<T, 4, 8>, dim3(g2), dim3(NB), 0, s, (const T *)xz, ld_xz,
+                       (const T *)conv_w, (const T *)conv_b, (const T *)hist, (T *)xc, ld_xc, L, Es, wvec));
+      return check_launch("conv1d_silu");
+    }
     dim3 grid((groups + (staged ? NTH : 64) - 1) / (staged ? NTH : 64), (L + TT - 1) / TT, B);
     if (staged) {
       const size_t smem = (size_t)(TT + 3) * NTH * 16;

@@ -267,6 +267,33 @@ def test_conv1d_silu_matches_oracle(dtype, es):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, BF])
+@pytest.mark.parametrize("b,l,es", [(3, 19, 256), (2, 301, 1024), (4, 64, 4096)])
+def test_conv1d_silu_variants_bit_identical(dtype, b, l, es, monkeypatch):
+    """The vectorised conv variants (loads issued first with 8 or 16 positions per
+    thread, the 64-position direct loop, the shared-memory tile) compute the same
+    arithmetic in the same order: identical bits, with a prior history, ragged blocks."""
+    x, z, *_, cw, cb, ci, _ = _ssm_inputs(b, l, es, 16, 21, dtype)
+    xc_ref, _ = O.conv_silu_ref(x, cw, cb, ci)
+    T = b * l
+    xz = t(np.concatenate([x, z], -1).reshape(T, 2 * es), dtype)
+    args = [t(cw, dtype), t(cb, dtype), t(ci, dtype)]
+    outs = []
+    for env in ({}, {"MTP_CONV_P": "16"}, {"MTP_CONV_KERNEL": "direct"}):
+        for k in ("MTP_CONV_P", "MTP_CONV_KERNEL"):
+            monkeypatch.delenv(k, raising=False)
+        for k, v in env.items():
+            monkeypatch.setenv(k, v)
+        xc = torch.full((T, es), float("nan"), device=dev(), dtype=dtype)
+        L.call("mtp_conv1d_silu", L.ptr(xz), 2 * es, *[L.ptr(a) for a in args], L.ptr(xc), es, b, l, es, 4,
+               L.dtype_code(dtype), L.stream_ptr())
+        torch.cuda.synchronize()
+        outs.append(xc)
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    np.testing.assert_allclose(n(outs[0]).reshape(b, l, es), xc_ref, atol=tol, rtol=tol)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, BF])
 @pytest.mark.parametrize("b,es,nst,R", [(1, 512, 16, 128), (32, 256, 16, 64), (5, 96, 8, 2), (64, 64, 16, 160)])
 def test_step_matches_oracle(dtype, b, es, nst, R):
     x, z, _, Bm, Cm, A_log, Dp, cw, cb, ci, si = _ssm_inputs(b, 1, es, nst, 13, dtype)
