@@ -5,6 +5,7 @@ for ncu captures of one kernel on a bounded case.
     python -m mamba_tp_lite_b200.microbench scan --batch 32 --seqlen 1024 --channels 4096
     python -m mamba_tp_lite_b200.microbench step --batch 32 --channels 4096 --rank 128
     torchrun --nproc-per-node N -m mamba_tp_lite_b200.microbench allreduce --rows 32768 --cols 2048 --mode int8
+    torchrun --nproc-per-node N -m mamba_tp_lite_b200.microbench allreduce-ref   # reference, gloo, host CPU
 
 Each prints one JSON line: average kernel time from CUDA events over --iters
 launches after --warmup launches, and the achieved rate against the measured
@@ -17,6 +18,7 @@ import argparse
 import datetime
 import json
 import os
+import sys
 
 import torch
 
@@ -168,6 +170,61 @@ def bench_step(a):
     gbs = nbytes / (ms / 1e3) / 1e9
     return {"kernel": "step", "B": B, "Es": es, "R": R, "avg_ms": ms, "GBps": gbs,
             "frac_of_hbm": gbs / peaks()["hbm_gbs"], "algorithmic_bytes": nbytes}
+
+
+def bench_allreduce_ref(a):
+    """The CPU baseline of BASELINE configuration 2: the unmodified reference's
+    ALLREDUCE_FNS (installed into baseline/_ref) over a gloo process group of host
+    processes (run under torchrun without GPUs), on the same activations as
+    ``allreduce`` (N(0, 1), a seeded 1% of the columns x20).  Times each call with
+    perf_counter between barriers, max over ranks; bus bytes as the NCCL convention,
+    2 (ws-1)/ws x payload for the all-reduces and (ws-1) x payload received for the int8
+    all-gather (tp_utils.py:23-42, :103-131)."""
+    import time
+
+    import torch.distributed as dist
+
+    ref = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "mamba_lite")):
+        raise SystemExit("the reference is not installed in baseline/_ref")
+    sys.path.insert(0, ref)
+    from mamba_lite.tp_utils import ALLREDUCE_FNS
+
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+    torch.set_num_threads(max(1, (os.cpu_count() or 1) // ws))
+    rows_list = [int(r) for r in a.rows_list.split(",")]
+    cols_list = [int(c) for c in a.cols_list.split(",")]
+    for cols in cols_list:
+        for rows in rows_list:
+            g = torch.Generator().manual_seed(rank * 1000 + rows)
+            x = torch.randn(rows, cols, generator=g)
+            x[:, torch.randperm(cols, generator=g)[: max(1, cols // 100)]] *= 20
+            for mname in ("fp32", "fp16", "int8"):
+                fn = ALLREDUCE_FNS[mname]
+                xs = [x.clone() for _ in range(a.warmup + a.iters)]  # fp32 reduces in place
+                for i in range(a.warmup):
+                    fn(xs[i])
+                dist.barrier()
+                t0 = time.perf_counter()
+                for i in range(a.iters):
+                    fn(xs[a.warmup + i])
+                dt = (time.perf_counter() - t0) / a.iters
+                t = torch.tensor([dt], dtype=torch.float64)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                dt = t.item()
+                payload = rows * cols * (4 if mname == "fp32" else 2) if mname != "int8" else rows * (4 + cols)
+                bus = 2 * (ws - 1) / ws * payload if mname != "int8" else (ws - 1) * payload
+                if rank == 0:
+                    print(json.dumps({"kernel": f"reference_{mname}_gloo_cpu", "ws": ws, "rows": rows, "cols": cols,
+                                      "avg_us": dt * 1e6, "bus_GBps": bus / dt / 1e9,
+                                      "threads_per_rank": torch.get_num_threads(), "host_cores": os.cpu_count()}),
+                          flush=True)
+                del xs
+    dist.barrier()
+    dist.destroy_process_group()
+    return None
 
 
 def bench_allreduce(a):
@@ -346,18 +403,22 @@ def main():
     r.add_argument("--epi", choices=["plain", "outproj"], default="plain",
                    help="plain: fp32 out; outproj: bf16 result + residual + next RMSNorm (the model's site)")
     r.add_argument("--sweep", action="store_true", help="every size and mode of the configuration, one line each")
+    rr = sub.add_parser("allreduce-ref", help="the reference's ALLREDUCE_FNS on gloo CPU processes")
+    rr.add_argument("--rows-list", default="1,32,1024")
+    rr.add_argument("--cols-list", default="768,2048,2560")
     dcd = sub.add_parser("decode")
     dcd.add_argument("--shape", default="1.4b")
     dcd.add_argument("--layers", type=int, default=0, help="override n_layer (0: the shape's)")
     dcd.add_argument("--batch", type=int, default=1)
     dcd.add_argument("--spec", default="mixed")
-    for p in (g, s, cv, st, r, dcd):
+    for p in (g, s, cv, st, r, rr, dcd):
         p.add_argument("--warmup", type=int, default=3)
         p.add_argument("--iters", type=int, default=10)
     a = ap.parse_args()
-    L.load()
+    if a.what != "allreduce-ref":  # the CPU baseline runs without the library
+        L.load()
     res = {"gemm": bench_gemm, "scan": bench_scan, "conv": bench_conv, "step": bench_step, "allreduce": bench_allreduce,
-           "decode": bench_decode}[a.what](a)
+           "allreduce-ref": bench_allreduce_ref, "decode": bench_decode}[a.what](a)
     if res is not None:
         print(json.dumps(res), flush=True)
 
