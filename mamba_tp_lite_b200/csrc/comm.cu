@@ -1855,8 +1855,12 @@ int mtp_xproj_fused(mtp_comm *c, int mode, const void *xc, int ld_xc, const void
   if (rows == 0) return MTP_OK;
   cudaStream_t s = (cudaStream_t)stream;
   const bool has_comm = c && c->d.ws > 1;
+  // default: the fused form at world sizes 1 and 2 (B200, 1.4b 32 x 1024: 79 vs 105 us per
+  // layer at 1 rank, 110 vs ~100 at 2); from 3 ranks on, its one-shot push sends every row to
+  // every rank, more than the reduction kernel's two-shot protocol moves, so the kernel pair
+  // stays the default there.  MTP_XPROJ_FUSED=1 forces it at any world size, 0 turns it off.
   const char *fenv = getenv("MTP_XPROJ_FUSED");
-  const bool fused_on = !(fenv && fenv[0] == '0');
+  const bool fused_on = fenv ? fenv[0] == '1' : (!has_comm || c->d.ws <= 2);
   MTP_REQUIRE(ab_dtype == MTP_F32 || ab_dtype == MTP_BF16, "xc / w must be F32 or BF16");
   const bool fused = fused_on && ab_dtype == MTP_BF16 && gemm_tc_eligible(xc, w, rows, N, K, ld_xc, ld_w) && N % 16 == 0 && N <= 192 &&
                      R % 16 == 0 && aligned16(dt_low) && aligned16(bc) &&

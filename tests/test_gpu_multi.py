@@ -180,7 +180,7 @@ def _suite(rank, init_file, q, ws):
         m = TPMambaLM.from_state_dict_shard(cfg, sd, rank, ws, dtype=torch.bfloat16, allreduce_dtype=spec,
                                             device="cuda")
         ids3 = torch.randint(0, cfg.vocab_size, (4, 520), generator=torch.Generator().manual_seed(11)).cuda()
-        for fz in ("0", "1"):
+        for fz in ("0", "1"):  # "1" forces the epilogue form at every world size
             os.environ["MTP_XPROJ_FUSED"] = fz
             lg, cache = m.prefill(ids3)
             out["xfused"][fz] = (_digest(lg.float().cpu().numpy()),
