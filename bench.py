@@ -43,6 +43,9 @@ CLOCK_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.a
                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
 
+NVLINK_GBS = 770.0  # peer copy per direction measured on this pool's B200s (NVLink 5: 900 nominal)
+
+
 def mixed_spec(n_layer: int):
     over = {f"{i}:out_proj": "fp16" for i in (0, n_layer - 4, n_layer - 3, n_layer - 2, n_layer - 1)}
     return {"default": "int8", "overrides": over}
@@ -486,6 +489,13 @@ def run_ours(a):
         ach = k["work"] / (k["avg_ms"] / 1000.0) / 1e12
         roofline = {"kernel": f"gemm_tc ({top})", "bound": "tensor", "achieved": ach, "peak": pk, "unit": "TFLOP/s",
                     "frac": ach / pk, "peak_source": f"{peak_src} sustained bf16"}
+    elif top in ("reduce_x", "reduce_out") and ws > 1:
+        # a peer-memory reduction: bytes this rank sends over NVLink per launch against the
+        # pool's measured peer-copy rate per direction (MEASURED_PEAKS.json has no NVLink figure)
+        ach = k["work"] / (k["avg_ms"] / 1000.0) / 1e9
+        roofline = {"kernel": f"reduce_pipe_kernel ({top})", "bound": "nvlink", "achieved": ach, "peak": NVLINK_GBS,
+                    "unit": "GB/s", "frac": ach / NVLINK_GBS,
+                    "peak_source": "measured peer copy per direction on this pool (900 GB/s nominal)"}
     else:
         ach = k["work"] / (k["avg_ms"] / 1000.0) / 1e9
         roofline = {"kernel": top, "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
@@ -511,6 +521,7 @@ def run_ours(a):
             # work = bytes this rank sends to its peers (0 at TP=1: the wire format's round trip only)
             gbs = v["work"] / (v["avg_ms"] / 1000.0) / 1e9
             row.update({"bound": "nvlink" if ws > 1 else "hbm", "sent_GBps": gbs,
+                        "frac_of_nvlink_770_measured": gbs / NVLINK_GBS if ws > 1 else None,
                         "frac_of_nvlink_900": gbs / 900.0 if ws > 1 else None})
         else:
             gbs = v["work"] / (v["avg_ms"] / 1000.0) / 1e9

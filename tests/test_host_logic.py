@@ -60,6 +60,25 @@ def test_vocab_shard_rejects_too_few_columns():
     assert L.load().mtp_vocab_shard(20, 8, 0, L.C.byref(c0), L.C.byref(n)) == L.MTP_ERR_ARG
 
 
+def test_reduction_trace_parser():
+    """The phase-trace parser follows the reduction kernel's stamp order: one-shot per round
+    push, wait, reduce, signal; two-shot push, push wait, owner reduce, gather wait, copy-out,
+    signal.  The wait time is the sum of the flag waits."""
+    from mamba_tp_lite_b200.tp_utils import _trace_waits
+
+    us = 1000
+    two = [0, 10, 12, 14, 20, 30, 32, 34, 40, 50, 52]  # K = 1: rounds 0, 1, 2
+    r = _trace_waits([v * us for v in two], True, 1)
+    assert r == {"kernel_us": 52.0, "wait_us": (20 - 14) + (40 - 34)}
+    one = [0, 10, 12, 14, 20, 30, 32]
+    r = _trace_waits([v * us for v in one], False, 1)
+    assert r == {"kernel_us": 32.0, "wait_us": 20 - 14}
+    # two rounds, two-shot: k = 0..3
+    st = [0, 5, 6, 7, 9, 12, 13, 14, 15, 18, 19, 20, 21, 22, 24, 27, 28]
+    r = _trace_waits([v * us for v in st], True, 2)
+    assert r["kernel_us"] == 28.0 and r["wait_us"] == (9 - 7) + (15 - 14) + (19 - 18) + (24 - 22)
+
+
 def test_product_has_no_cpu_fallback():
     cfg = MambaConfig(d_model=32, n_layer=1, vocab_size=64, d_state=8)
     m = MambaMixer(cfg, 0)
