@@ -47,8 +47,17 @@ enum {
 enum { MTP_F32 = 0, MTP_BF16 = 1, MTP_F16 = 2 };
 
 /* Reduction (collective) wire modes: the reference's ALLREDUCE_FNS names
- * "fp32", "fp16" and "int8" (== "int8_gather_tok"), mamba_lite/tp_utils.py:152-160. */
-enum { MTP_RED_FP32 = 0, MTP_RED_FP16 = 1, MTP_RED_INT8TOK = 2 };
+ * (mamba_lite/tp_utils.py:152-160): "fp32", "fp16", "int8" (== "int8_gather_tok"), and
+ * the per-tensor-scale variants "int8_gather" (:134-142), "int8_sum" (:78-100) and
+ * "int8_legacy" (:45-75). */
+enum {
+  MTP_RED_FP32 = 0,
+  MTP_RED_FP16 = 1,
+  MTP_RED_INT8TOK = 2,
+  MTP_RED_INT8TENSOR = 3, /* one scale per rank's tensor, int8 gathered, rank-ordered dequant-sum */
+  MTP_RED_INT8SUM = 4,    /* scale shared by all ranks (MAX), values in +-(127 / ws), integer sum */
+  MTP_RED_INT8LEGACY = 5  /* scale shared by all ranks (MAX), values in +-127, integer sum */
+};
 
 /* GEMM epilogues. */
 enum {
@@ -207,6 +216,13 @@ int mtp_comm_reset_state(mtp_comm *c);
  * across micro-batches); 0 restores the default (one CTA per SM, register rows).
  * Results are bit-identical either way. */
 int mtp_comm_set_max_ctas(mtp_comm *c, int max_ctas);
+
+/* Sequence-parallel out_proj epilogue on this context (default on): at world size > 1 each
+ * row's owner rank (row % ws) applies the bias, residual and next RMSNorm and the normed rows
+ * are gathered, so a rank's residual stays current only on its own rows.  A model whose
+ * out_proj sites mix modes with and without that form (the per-tensor-scale modes have no
+ * such form) turns it off for its forward passes, so every reduction updates every row. */
+int mtp_comm_set_sequence_parallel(mtp_comm *c, int on);
 
 /* Bytes this rank sends to its peers over NVLink for one reduction of [rows, cols] in
  * `mode` whose results are rounded to rdt (MTP_F32 / MTP_BF16), with the protocol the

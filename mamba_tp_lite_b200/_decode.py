@@ -15,7 +15,7 @@ import os
 import torch
 
 from . import _lib as L
-from .tp_utils import KERNEL_MODES, comm_for
+from .tp_utils import KERNEL_MODES, ROW_MODES, comm_for
 
 MAX_BATCH = 32        # what a plan is built for (the kernel's limit)
 FUSED_MAX_BATCH = 8   # step() uses the kernel up to this batch; above it the per-layer chain is
@@ -29,7 +29,8 @@ def fused_max_batch() -> int:
 def _site_mode(mixer, site: str):
     if mixer._site_modes is None:
         return L.RED_FP32
-    return KERNEL_MODES.get(mixer._site_modes[site])
+    name = mixer._site_modes[site]
+    return KERNEL_MODES[name] if name in ROW_MODES else None
 
 
 def supported(lm) -> str | None:
@@ -47,7 +48,7 @@ def supported(lm) -> str | None:
     for blk in lm.layers:
         m = blk.mixer
         if _site_mode(m, "x_proj") is None or _site_mode(m, "out_proj") is None:
-            return "a site uses a reduction variant without a kernel mode"
+            return "a site uses a per-tensor-scale reduction variant (no per-row form in the decode kernel)"
     return None
 
 

@@ -15,7 +15,7 @@ LIB_PATH = os.path.join(PKG, "libmtp.so")
 
 MTP_OK, MTP_ERR_ARG, MTP_ERR_CUDA, MTP_ERR_TIMEOUT, MTP_ERR_UNSUPPORTED = 0, 1, 2, 3, 4
 F32, BF16, F16 = 0, 1, 2
-RED_FP32, RED_FP16, RED_INT8TOK = 0, 1, 2
+RED_FP32, RED_FP16, RED_INT8TOK, RED_INT8TENSOR, RED_INT8SUM, RED_INT8LEGACY = 0, 1, 2, 3, 4, 5
 EPI_STORE, EPI_BIAS_SOFTPLUS, EPI_BIAS = 0, 1, 2
 GEMM_AUTO, GEMM_TCGEN05, GEMM_SIMT, GEMM_GEMV = 0, 1, 2, 3
 
@@ -52,6 +52,7 @@ _SIGS = {
     "mtp_comm_reset_status": [_vp],
     "mtp_comm_reset_state": [_vp],
     "mtp_comm_set_max_ctas": [_vp, _i],
+    "mtp_comm_set_sequence_parallel": [_vp, _i],
     "mtp_comm_set_trace": [_vp, _i],
     "mtp_comm_read_trace": [_vp, C.POINTER(_u64), _i, C.POINTER(_i)],
     "mtp_comm_sent_bytes": [_vp, _i, _i, _i, _i, C.POINTER(_d)],

@@ -26,7 +26,7 @@ import os
 import torch
 
 from . import _lib as L
-from .tp_utils import KERNEL_MODES, comm_for, count_collective, torch_allreduce
+from .tp_utils import KERNEL_MODES, ROW_MODES, comm_for, count_collective
 
 # Optional launch timing for benchmarks: when set to a dict, CUDA events are
 # recorded around the named kernel launches into PROFILE[name] as
@@ -105,11 +105,8 @@ class MixerKernels:
         if name is not None:
             if OVERLAP_STREAM is None:
                 count_collective(self.comm, name, partial.shape, self._dt())
-            if name in KERNEL_MODES:
-                mode = KERNEL_MODES[name]
-                ctx = comm_for(self)
-            else:  # out-of-scope variants keep the reference's torch.distributed algorithm
-                partial = torch_allreduce(name, partial.to(self._dt()), self.group).float().contiguous()
+            mode = KERNEL_MODES[name]
+            ctx = comm_for(self)
 
         def launch():
             L.call("mtp_reduce_xproj", ctx, mode, L.ptr(partial), rows, cfg.dt_rank, 2 * cfg.d_state, L.ptr(dt_low),
@@ -129,10 +126,10 @@ class MixerKernels:
         writes the wire rows (or, at world size 1, dt_low | B|C after the wire round trip),
         so the fp32 partial is not written; ``partial`` is only the fallback buffer of the
         library for shapes the fused form does not take.  False (nothing launched) for the
-        torch.distributed variants and while micro-batches overlap."""
+        per-tensor-scale variants and while micro-batches overlap."""
         cfg = self.cfg
         name = None if self._site_modes is None else self._site_modes["x_proj"]
-        if OVERLAP_STREAM is not None or (name is not None and name not in KERNEL_MODES):
+        if OVERLAP_STREAM is not None or (name is not None and name not in ROW_MODES):
             return False
         ctx, mode = None, L.RED_FP32
         if name is not None:
@@ -158,11 +155,8 @@ class MixerKernels:
         if name is not None:
             if OVERLAP_STREAM is None:
                 count_collective(self.comm, name, partial.shape, self._dt())
-            if name in KERNEL_MODES:
-                mode = KERNEL_MODES[name]
-                ctx = comm_for(self)
-            else:
-                partial = torch_allreduce(name, partial.to(self._dt()), self.group).float().contiguous()
+            mode = KERNEL_MODES[name]
+            ctx = comm_for(self)
         bias = self._out_bias()
         odt = normed.dtype if normed is not None else self._dt()
 

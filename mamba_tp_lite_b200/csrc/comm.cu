@@ -1358,17 +1358,255 @@ static double sent_bytes(int ws, int max_rows, int mode, int rows, int cols, int
   for (int r0 = 0; r0 < rows; r0 += max_rows) {
     const int nr = rows - r0 < max_rows ? rows - r0 : max_rows;
     const double w = (double)nr * wire_row_bytes(mode, cols);
+    if (mode >= MTP_RED_INT8TENSOR) {  // one-shot int8 rows (+ the 4-byte maximum of the shared-scale modes)
+      total += (double)(ws - 1) * (w + (mode == MTP_RED_INT8TENSOR ? 0.0 : 4.0));
+      continue;
+    }
     total += use_two_shot(ws, mode, nr, cols, rdt) ? (double)(ws - 1) / ws * (w + (double)nr * rdt_row_bytes(rdt, cols))
                                                    : (double)(ws - 1) * w;
   }
   return total;
 }
 
+
+// ----------------------------------------------------------------- per-tensor-scale int8 reductions
+// int8_gather (tp_utils.py:134-142): each rank quantises its whole tensor with one scale
+//   max(|x|, 1e-8) / 127, the int8 values are gathered and every rank sums
+//   float(q_r) * s_r from zeros in rank order (the per-token arithmetic with one scale per rank);
+// int8_sum (:78-100): the scale is shared, max over ranks of max(|x|, 1e-8), / (127 / ws) (integer
+//   division), values clamped to +-(127 / ws), summed as integers (exactly, so in any order), times
+//   the scale;
+// int8_legacy (:45-75): as int8_sum with +-127 (the reference carries int32 on the wire; the sum
+//   of int8 values is the same integer).
+// tensor_amax_kernel writes per-CTA maxima of |partial|; reduce_scaled_kernel takes their max, and
+// for the shared-scale modes CTA 0 pushes it to every rank's slot tail (phase-1 flag of CTA 0) and
+// every CTA waits for all ranks' maxima; then one warp per row quantises, pushes the row's int8
+// bytes to every rank (one-shot), flags, waits for CTA j of every rank, reduces, rounds and runs the
+// site's epilogue.  Receive layout per source rank: [rows x 4 scale bytes | rows x cols int8 | ...
+// | max at the slot's last 16 bytes].
+__global__ void __launch_bounds__(256) tensor_amax_kernel(const float *__restrict__ x, long n, float *partials) {
+  MTP_PDL_WAIT();
+  MTP_PDL_TRIGGER();
+  __shared__ float wm[8];
+  float m = 0.f;
+  const long stride = (long)gridDim.x * blockDim.x;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    const long n4 = n / 4;
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+      const float4 v = reinterpret_cast<const float4 *>(x)[i];
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+    for (long i = 4 * n4 + (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) m = fmaxf(m, fabsf(x[i]));
+  } else {
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) m = fmaxf(m, fabsf(x[i]));
+  }
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, wm[w]);
+    partials[blockIdx.x] = m;
+  }
+}
+
+__device__ __forceinline__ int quant_q(float x, float s, float qmax) {
+  float r = rintf(__fdiv_rn(x, s));
+  r = fminf(fmaxf(r, -qmax), qmax);
+  return (int)r;
+}
+
+template <int MODE, int EPI>
+__global__ void __launch_bounds__(WPB * 32) reduce_scaled_kernel(CommDev d, bool has_comm, int site,
+                                                                 const float *__restrict__ partial, int rows, int cols,
+                                                                 const float *partials, int G1, float *scratch,
+                                                                 EpiOut e) {
+  MTP_PDL_WAIT();
+  MTP_PDL_TRIGGER();
+  __shared__ int abort_sm;
+  __shared__ uint32_t epoch_sm;
+  __shared__ float amax_sm;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int j = blockIdx.x, G = gridDim.x;
+  if (warp == 0) {
+    float m = 0.f;
+    for (int i = lane; i < G1; i += 32) m = fmaxf(m, partials[i]);
+    m = warp_max(m);
+    if (lane == 0) amax_sm = m;
+  }
+  __syncthreads();
+  const float amax = amax_sm;
+  const int ws = has_comm ? d.ws : 1;
+  const float qmax = MODE == MTP_RED_INT8SUM ? (float)(127 / ws) : 127.0f;
+  float *wrow = scratch + (size_t)(j * WPB + warp) * cols;
+  if (!has_comm) {
+    const float s = MODE == MTP_RED_INT8TENSOR ? row_scale(amax) : __fdiv_rn(fmaxf(amax, 1e-8f), qmax);
+    for (int r = j * WPB + warp; r < rows; r += G * WPB) {
+      const float *row = partial + (size_t)r * cols;
+      for (int c = lane; c < cols; c += 32) {
+        const float q = (float)quant_q(row[c], s, qmax);
+        wrow[c] = rnd_rdt(MODE == MTP_RED_INT8TENSOR ? __fadd_rn(0.f, __fmul_rn(q, s)) : __fmul_rn(q, s), e.rdt);
+      }
+      __syncwarp();
+      epilogue_row<EPI>(e, wrow, r, cols, lane);
+      __syncwarp();
+    }
+    return;
+  }
+  uint32_t *ep = reinterpret_cast<uint32_t *>(d.peer[d.rank] + d.off_epoch) + site;
+  if (threadIdx.x == 0) {
+    abort_sm = 0;
+    epoch_sm = *reinterpret_cast<volatile uint32_t *>(ep) + 1u;
+  }
+  __syncthreads();
+  const uint32_t epoch = epoch_sm;
+  auto finish = [&]() {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      unsigned int *done = reinterpret_cast<unsigned int *>(d.peer[d.rank] + d.off_done) + site;
+      if (atomicAdd(done, 1u) == (unsigned)G - 1u) {
+        *done = 0u;
+        *reinterpret_cast<volatile uint32_t *>(ep) = epoch;
+        __threadfence();
+      }
+    }
+  };
+  const size_t half = (size_t)(epoch & 1u) * d.ws * d.slot_bytes[site];
+  const uint32_t all = (1u << d.ws) - 1u;
+  const size_t tail = d.slot_bytes[site] - 16;
+  float s;
+  if (MODE == MTP_RED_INT8TENSOR) {
+    s = row_scale(amax);
+  } else {
+    // the shared scale: every rank's maximum
+    if (j == 0 && threadIdx.x < (unsigned)d.ws) {
+      *reinterpret_cast<float *>(d.peer[threadIdx.x] + d.off_recv[site] + half + (size_t)d.rank * d.slot_bytes[site] +
+                                 tail) = amax;
+      __threadfence_system();
+      st_release_sys(flag_ptr(d.peer[threadIdx.x], d, site, 1, d.rank, 0), epoch);
+    }
+    if (threadIdx.x < (unsigned)d.ws) {
+      const uint32_t *f = flag_ptr(d.peer[d.rank], d, site, 1, threadIdx.x, 0);
+      const unsigned long long t0 = globaltimer_ns();
+      uint32_t it = 0;
+      while ((int)(ld_acquire_sys(f) - epoch) < 0) {
+        if ((++it & 63u) == 0 && globaltimer_ns() - t0 > d.timeout_ns) {
+          atomicExch(reinterpret_cast<int *>(d.peer[d.rank] + d.off_status), MTP_ERR_TIMEOUT);
+          abort_sm = 1;
+          break;
+        }
+      }
+      __threadfence();
+    }
+    __syncthreads();
+    if (abort_sm) { finish(); return; }
+    float m = 0.f;
+    for (int k = 0; k < d.ws; ++k)
+      m = fmaxf(m, __ldcg(reinterpret_cast<const float *>(d.peer[d.rank] + d.off_recv[site] + half +
+                                                          (size_t)k * d.slot_bytes[site] + tail)));
+    s = __fdiv_rn(fmaxf(m, 1e-8f), qmax);
+  }
+  // push: every row's int8 values (and, per-tensor, this rank's scale) to every rank
+  const size_t my_slot = d.off_recv[site] + half + (size_t)d.rank * d.slot_bytes[site];
+  for (int r = j * WPB + warp; r < rows; r += G * WPB) {
+    const float *row = partial + (size_t)r * cols;
+    for (int q = 0; q < d.ws; ++q) {
+      char *dst = d.peer[(d.rank + q) % d.ws] + my_slot;  // stagger destinations across ranks
+      if (lane == 0) reinterpret_cast<float *>(dst)[r] = s;
+      int8_t *qd = reinterpret_cast<int8_t *>(dst + (size_t)4 * rows + (size_t)r * cols);
+      if ((cols & 3) == 0 && (rows & 3) == 0) {
+        for (int c = 4 * lane; c < cols; c += 128)
+          *reinterpret_cast<uint32_t *>(qd + c) = pack4(quant_q(row[c], s, qmax), quant_q(row[c + 1], s, qmax),
+                                                        quant_q(row[c + 2], s, qmax), quant_q(row[c + 3], s, qmax));
+      } else {
+        for (int c = lane; c < cols; c += 32) qd[c] = (int8_t)quant_q(row[c], s, qmax);
+      }
+    }
+  }
+  signal(d, site, 0, epoch, all);
+  if (!wait_all(d, site, 0, epoch, all, &abort_sm)) { finish(); return; }
+  const char *slots[MAX_WS];
+  for (int k = 0; k < d.ws; ++k) slots[k] = d.peer[d.rank] + d.off_recv[site] + half + (size_t)k * d.slot_bytes[site];
+  for (int r = j * WPB + warp; r < rows; r += G * WPB) {
+    float sk[MAX_WS];
+    if (MODE == MTP_RED_INT8TENSOR)
+      for (int k = 0; k < d.ws; ++k) sk[k] = __ldcg(reinterpret_cast<const float *>(slots[k]) + r);
+    for (int c = lane; c < cols; c += 32) {
+      float acc = 0.f;
+      if (MODE == MTP_RED_INT8TENSOR) {
+        for (int k = 0; k < d.ws; ++k) {
+          const float q = (float)__ldcg(reinterpret_cast<const signed char *>(slots[k] + (size_t)4 * rows + (size_t)r * cols + c));
+          acc = __fadd_rn(acc, __fmul_rn(q, sk[k]));
+        }
+      } else {
+        int isum = 0;
+        for (int k = 0; k < d.ws; ++k)
+          isum += (int)__ldcg(reinterpret_cast<const signed char *>(slots[k] + (size_t)4 * rows + (size_t)r * cols + c));
+        acc = __fmul_rn((float)isum, s);
+      }
+      wrow[c] = rnd_rdt(acc, e.rdt);
+    }
+    __syncwarp();
+    epilogue_row<EPI>(e, wrow, r, cols, lane);
+    __syncwarp();
+  }
+  finish();
+}
+
+template <int EPI>
+static int run_reduce_scaled(mtp_comm *c, int site, int mode, const float *partial, int rows, int cols, EpiOut e,
+                             cudaStream_t s) {
+  const bool has_comm = c && c->d.ws > 1;
+  const int sms = num_sms();
+  const int step = has_comm ? c->max_rows : rows;
+  for (int r0 = 0; r0 < rows; r0 += step) {
+    const int nr = rows - r0 < step ? rows - r0 : step;
+    if (has_comm)
+      MTP_REQUIRE((size_t)4 * nr + (size_t)nr * cols + 16 <= c->d.slot_bytes[site], "rows exceed the receive slot");
+    int G = ceil_div(nr, WPB);
+    if (G > sms) G = sms;
+    if (G > G_MAX) G = G_MAX;
+    const long n = (long)nr * cols;
+    int G1 = (int)((n + 4095) / 4096);
+    if (G1 > 2 * sms) G1 = 2 * sms;
+    if (G1 < 1) G1 = 1;
+    float *scr = row_scratch(((size_t)G * WPB * cols + 512) * sizeof(float));
+    if (!scr) return fail(MTP_ERR_CUDA, "could not allocate reduction scratch");
+    float *partials = scr + (size_t)G * WPB * cols;
+    EpiOut ee = e;
+    ee.wide = 0;
+    if (EPI == EPI_PLAIN) ee.out = e.out + (size_t)r0 * cols;
+    if (EPI == EPI_XPROJ) {
+      ee.dt_low = (char *)e.dt_low + (size_t)r0 * e.R * (e.dt_dtype == MTP_F32 ? 4 : 2);
+      ee.bc = e.bc + (size_t)r0 * (cols - e.R);
+    }
+    if (EPI == EPI_OUTPROJ) {
+      ee.resid = e.resid + (size_t)r0 * cols;
+      if (e.normed) ee.normed = (char *)e.normed + (size_t)r0 * cols * (e.out_dtype == MTP_F32 ? 4 : 2);
+    }
+    const float *pp = partial + (size_t)r0 * cols;
+    launch_pdl(tensor_amax_kernel, dim3(G1), dim3(256), 0, s, pp, n, partials);
+    int rc = check_launch("tensor_amax");
+    if (rc) return rc;
+    CommDev d{};
+    if (has_comm) d = c->d;
+#define MTP_RS(M) launch_pdl(reduce_scaled_kernel<M, EPI>, dim3(G), dim3(WPB * 32), 0, s, d, has_comm, site, pp, nr, cols, \
+                             (const float *)partials, G1, scr, ee)
+    if (mode == MTP_RED_INT8TENSOR) MTP_RS(MTP_RED_INT8TENSOR);
+    else if (mode == MTP_RED_INT8SUM) MTP_RS(MTP_RED_INT8SUM);
+    else MTP_RS(MTP_RED_INT8LEGACY);
+#undef MTP_RS
+    rc = check_launch("reduce_scaled");
+    if (rc) return rc;
+  }
+  return MTP_OK;
+}
+
 template <int EPI>
 static int run_reduce(mtp_comm *c, int site, int mode, const float *partial, int rows, int cols, EpiOut e,
                       cudaStream_t s) {
   MTP_REQUIRE(partial && rows >= 0 && cols > 0, "bad arguments");
-  MTP_REQUIRE(mode == MTP_RED_FP32 || mode == MTP_RED_FP16 || mode == MTP_RED_INT8TOK, "unknown reduction mode");
+  MTP_REQUIRE(mode >= MTP_RED_FP32 && mode <= MTP_RED_INT8LEGACY, "unknown reduction mode");
   MTP_REQUIRE(aligned16(partial), "partial must be 16-byte aligned");
   if (rows == 0) return MTP_OK;
   const bool has_comm = c && c->d.ws > 1;
@@ -1376,6 +1614,7 @@ static int run_reduce(mtp_comm *c, int site, int mode, const float *partial, int
     MTP_REQUIRE(c->opened, "comm context peers not opened");
     MTP_REQUIRE(cols <= c->cols[site], "row width exceeds the context's site width");
   }
+  if (mode >= MTP_RED_INT8TENSOR) return run_reduce_scaled<EPI>(c, site, mode, partial, rows, cols, e, s);
   const int sms = num_sms();
   // rows per launch: bounded by the context's slots; each launch is a complete reduction
   const int step = has_comm ? c->max_rows : rows;
@@ -1410,7 +1649,7 @@ static int run_reduce(mtp_comm *c, int site, int mode, const float *partial, int
     // protocol, which it implies.  B200, [32768, 2048] int8 / fp16: 338 / 472 us at 2 ranks
     // (one-shot 366 / 634), 409 / 641 us at 4 (two-shot without it 453 / 684).
     // MTP_COMM_SP=0 turns it off.
-    bool sp = EPI == EPI_OUTPROJ && has_comm && ee.normed != nullptr && !capped;
+    bool sp = EPI == EPI_OUTPROJ && has_comm && ee.normed != nullptr && !capped && c->sp_allowed;
     if (sp) {
       const char *env = getenv("MTP_COMM_SP");
       if (env && !strcmp(env, "0")) sp = false;
@@ -1746,6 +1985,12 @@ int mtp_comm_read_trace(mtp_comm *c, uint64_t *out, int capacity, int *n_records
 int mtp_comm_set_max_ctas(mtp_comm *c, int max_ctas) {
   MTP_REQUIRE(c && max_ctas >= 0, "bad arguments");
   c->max_ctas = max_ctas;
+  return MTP_OK;
+}
+
+int mtp_comm_set_sequence_parallel(mtp_comm *c, int on) {
+  MTP_REQUIRE(c, "null argument");
+  c->sp_allowed = on != 0;
   return MTP_OK;
 }
 

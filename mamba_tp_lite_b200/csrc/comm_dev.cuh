@@ -45,6 +45,7 @@ struct mtp_comm {
   size_t total = 0;
   int max_rows = 0, cols[2] = {0, 0};
   int max_ctas = 0;  // > 0: cap on a reduction's grid, low-register kernel (runs beside compute kernels)
+  bool sp_allowed = true;  // sequence-parallel out_proj epilogue (mtp_comm_set_sequence_parallel)
   bool opened = false;
   cudaIpcMemHandle_t handle;
 };

@@ -209,11 +209,11 @@ class _LMKernels:
     def _overlap_split(self, b: int, l: int):
         """Micro-batch split of a prefill for compute/communication overlap, or None.
         Opt-in (MTP_PREFILL_OVERLAP=1): for models that run collectives over a comm
-        context (world size > 1, every site in a kernel wire format) and batches of
+        context (world size > 1, every site in a per-row wire format) and batches of
         at least 2 sequences.  Off by default: the reduction kernel needs most SMs to
         reach its bandwidth (1.4b TP=2 on B200: 160 ms per prefill step overlapped
         vs 139 ms serial), so the overlap does not pay yet; results are bit-identical."""
-        from .tp_utils import KERNEL_MODES
+        from .tp_utils import ROW_MODES
 
         if os.environ.get("MTP_PREFILL_OVERLAP", "0") != "1" or b < 2 or b * l < 2048:
             return None
@@ -221,7 +221,7 @@ class _LMKernels:
             m = blk.mixer
             if m._site_modes is None or m.world_size < 2:
                 return None
-            if any(m._site_modes[s] not in KERNEL_MODES for s in ("x_proj", "out_proj")):
+            if any(m._site_modes[s] not in ROW_MODES for s in ("x_proj", "out_proj")):
                 return None
         return [(0, b // 2), (b // 2, b)]
 
@@ -289,7 +289,23 @@ class _LMKernels:
             cur.wait_stream(st)
         return [LayerCache(conv_state=c, ssm_state=sm) for c, sm in zip(conv_all, ssm_all)]
 
+    def _sync_sequence_parallel(self) -> None:
+        """Tensor-parallel models: the sequence-parallel out_proj epilogue (each row's
+        residual kept by its owner rank) only when every out_proj site has a per-row wire
+        format; a per-tensor-scale site updates every row's residual, so mixing the two
+        would read stale rows.  Set before every forward pass (the context is shared)."""
+        if getattr(self, "world_size", 1) < 2:
+            return
+        from .tp_utils import ROW_MODES, get_comm
+
+        cfg = self.cfg
+        c = get_comm(self.group, self.rank, self.world_size, cfg.dt_rank + 2 * cfg.d_state, cfg.d_model)
+        ok = all(blk.mixer._site_modes is None or blk.mixer._site_modes["out_proj"] in ROW_MODES
+                 for blk in self.layers)
+        c.set_sequence_parallel(ok)
+
     def _forward_prefill(self, input_ids: torch.Tensor, cache=None):
+        self._sync_sequence_parallel()
         b, l = input_ids.shape
         resid = self._embed(input_ids)
         normed = torch.empty(resid.shape, device=resid.device, dtype=self._param_dtype())
@@ -345,6 +361,7 @@ class _LMKernels:
                 count_collective(m.comm, m._site_modes["out_proj"], (b, self.cfg.d_model), m._dt())
 
     def _forward_step(self, input_ids: torch.Tensor, cache):
+        self._sync_sequence_parallel()
         b = input_ids.shape[0]
         fused = self._decode_plan(b, cache)
         if fused is not None:

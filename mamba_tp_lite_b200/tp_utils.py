@@ -2,12 +2,12 @@
 (``mamba_lite/tp_utils.py``): ``CommCounter``, ``ALLREDUCE_FNS``,
 ``channel_slice``, ``SITES``, ``site_dtype``.
 
-The "fp32", "fp16" and "int8" (= "int8_gather_tok") reductions run in
-libmtp's peer-memory kernels over NVLink (one allocation per rank mapped by
-its peers through CUDA IPC; see ``comm_for``).  The remaining variants of the
-reference ("int8_gather" per-tensor, "int8_sum", "int8_legacy") keep the
-reference's torch.distributed algorithm on CUDA tensors.  Nothing here runs on
-the CPU.
+Every reduction of the reference runs in libmtp's peer-memory kernels over NVLink
+(one allocation per rank mapped by its peers through CUDA IPC; see ``comm_for``):
+"fp32", "fp16" and "int8" (= "int8_gather_tok") with per-row wire formats, and the
+per-tensor-scale variants "int8_gather", "int8_sum" and "int8_legacy" (a max-|x|
+kernel, for the shared scale an exchange of the ranks' maxima, then the quantise /
+push / sum kernel).  Nothing here runs on the CPU.
 """
 from __future__ import annotations
 
@@ -33,8 +33,12 @@ class CommCounter:
         self.bytes = 0
 
 
-# names served by the fused kernels -> libmtp wire mode
-KERNEL_MODES = {"fp32": L.RED_FP32, "fp16": L.RED_FP16, "int8": L.RED_INT8TOK, "int8_gather_tok": L.RED_INT8TOK}
+# reduction names -> libmtp wire mode
+KERNEL_MODES = {"fp32": L.RED_FP32, "fp16": L.RED_FP16, "int8": L.RED_INT8TOK, "int8_gather_tok": L.RED_INT8TOK,
+                "int8_gather": L.RED_INT8TENSOR, "int8_sum": L.RED_INT8SUM, "int8_legacy": L.RED_INT8LEGACY}
+# names with a per-row wire format: the ones the x_proj GEMM epilogue, the persistent decode
+# kernel and the sequence-parallel out_proj epilogue take
+ROW_MODES = frozenset({"fp32", "fp16", "int8", "int8_gather_tok"})
 ALL_NAMES = ("fp32", "fp16", "int8", "int8_legacy", "int8_sum", "int8_gather", "int8_gather_tok")
 SITES = ("x_proj", "out_proj")
 
@@ -151,6 +155,12 @@ class Comm:
     def set_max_ctas(self, max_ctas: int) -> None:
         """Caps the grid of this context's reductions (0: default); see mtp_comm_set_max_ctas."""
         L.call("mtp_comm_set_max_ctas", self.handle, int(max_ctas))
+
+    def set_sequence_parallel(self, on: bool) -> None:
+        """Sequence-parallel out_proj epilogue on / off (mtp_comm_set_sequence_parallel)."""
+        if getattr(self, "_sp", True) != bool(on):
+            L.call("mtp_comm_set_sequence_parallel", self.handle, int(bool(on)))
+            self._sp = bool(on)
 
     def set_trace(self, records: int) -> None:
         """Ring of ``records`` phase-trace records of this context's reductions (0 frees
@@ -306,66 +316,22 @@ def all_reduce_sum_int8_gather_tok(tensor, group=None, counter=None):
     return _kernel_allreduce("int8", tensor, group, counter)
 
 
-def _payload_gather_dequant(tensor: torch.Tensor, group, rows: int, cols: int) -> torch.Tensor:
-    """Quantise [rows, cols] with libmtp, all-gather the packed payloads with
-    torch.distributed, dequant-sum in rank order with libmtp."""
-    _, ws = _world(group)
-    t = tensor.reshape(rows, cols).float().contiguous()
-    payload = torch.empty(rows * (4 + cols), dtype=torch.uint8, device=t.device)
-    scales = payload[: 4 * rows].view(torch.float32)
-    q = payload[4 * rows:].view(torch.int8)
-    L.call("mtp_quantize_rows_int8", L.ptr(t), rows, cols, cols, L.ptr(scales), L.ptr(q), L.stream_ptr())
-    gathered = torch.empty(ws * payload.numel(), dtype=torch.uint8, device=t.device)
-    if ws > 1:
-        dist.all_gather_into_tensor(gathered, payload, group=group)
-    else:
-        gathered.copy_(payload)
-    out = torch.empty(rows, cols, dtype=torch.float32, device=t.device)
-    L.call("mtp_dequant_sum", L.ptr(gathered), ws, rows, cols, L.ptr(out), L.stream_ptr())
-    return out
-
-
 def all_reduce_sum_int8_gather(tensor, group=None, counter=None):
-    """One int8 scale for the whole tensor (tp_utils.py:134-142)."""
-    L.require_cuda(tensor, "int8_gather")
-    count_collective(counter, "int8_gather", tensor.shape, tensor.dtype)
-    out = _payload_gather_dequant(tensor, group, 1, tensor.numel())
-    return out.view(tensor.shape).to(tensor.dtype)
+    """One int8 scale per rank's tensor, int8 gathered, rank-ordered dequant-sum
+    (tp_utils.py:134-142)."""
+    return _kernel_allreduce("int8_gather", tensor, group, counter)
 
 
 def all_reduce_sum_int8_sum(tensor, group=None, counter=None):
-    """Shared scale from a MAX reduction, +-(127 // world_size) int8 values
-    summed in int8 (tp_utils.py:78-100)."""
-    L.require_cuda(tensor, "int8_sum")
-    count_collective(counter, "int8_sum", tensor.shape, tensor.dtype)
-    _, ws = _world(group)
-    qmax = 127 // ws
-    t = tensor.contiguous().float()
-    amax = t.abs().max().clamp(min=1e-8).reshape(1)
-    if ws > 1:
-        dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=group)
-    scale = amax / qmax
-    q = torch.clamp(torch.round(t / scale), -qmax, qmax).to(torch.int8)
-    if ws > 1:
-        dist.all_reduce(q, op=dist.ReduceOp.SUM, group=group)
-    return (q.float() * scale).to(tensor.dtype)
+    """Shared scale from the ranks' maxima, +-(127 // world_size) int8 values summed
+    (tp_utils.py:78-100)."""
+    return _kernel_allreduce("int8_sum", tensor, group, counter)
 
 
 def all_reduce_sum_int8_legacy(tensor, group=None, counter=None):
-    """Per-tensor scale agreed through a MAX reduction read back to the host,
-    then an int32 SUM (tp_utils.py:45-75); not graph-capturable."""
-    L.require_cuda(tensor, "int8_legacy")
-    count_collective(counter, "int8_legacy", tensor.shape, tensor.dtype)
-    _, ws = _world(group)
-    t = tensor.contiguous()
-    m = t.abs().max().clamp(min=1e-8).reshape(1)
-    if ws > 1:
-        dist.all_reduce(m, op=dist.ReduceOp.MAX, group=group)
-    scale = m.item() / 127.0
-    q32 = torch.clamp(torch.round(t / scale), -127, 127).to(torch.int8).to(torch.int32)
-    if ws > 1:
-        dist.all_reduce(q32, op=dist.ReduceOp.SUM, group=group)
-    return (q32.float() * scale).to(tensor.dtype)
+    """Shared scale from the ranks' maxima, +-127 values, integer sum (tp_utils.py:45-75);
+    the scale stays on the device (the reference reads it back to the host)."""
+    return _kernel_allreduce("int8_legacy", tensor, group, counter)
 
 
 ALLREDUCE_FNS = {
@@ -378,8 +344,3 @@ ALLREDUCE_FNS = {
     "int8_gather_tok": all_reduce_sum_int8_gather_tok,
 }
 
-
-def torch_allreduce(name: str, tensor: torch.Tensor, group) -> torch.Tensor:
-    """The reference algorithm of an out-of-kernel variant, without counting
-    (the mixer counts)."""
-    return ALLREDUCE_FNS[name](tensor, group, None)

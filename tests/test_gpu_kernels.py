@@ -462,6 +462,33 @@ def test_xproj_fused_falls_back_for_other_shapes():
                L.ptr(dl), L.BF16, L.ptr(bc), L.stream_ptr())
 
 
+@pytest.mark.parametrize("name", ["int8_gather", "int8_sum", "int8_legacy"])
+@pytest.mark.parametrize("rows,cols", [(1, 160), (37, 18), (1000, 2048), (300, 2050)])
+def test_per_tensor_scale_reductions_world_size_one(name, rows, cols):
+    """The per-tensor-scale variants at world size 1 (tp_utils.py:45-100, :134-142): the
+    whole tensor's max |x| (a grid reduction), the round trip through int8 with that scale,
+    bit-exact against the oracle; through the x_proj and out_proj epilogues too."""
+    from mamba_tp_lite_b200.tp_utils import KERNEL_MODES
+
+    mode = KERNEL_MODES[name]
+    x = _rand((rows, cols), rows + cols, 3.0)
+    x[:, :: max(1, cols // 7)] *= 20
+    xt = t(x)
+    out = torch.empty_like(xt)
+    L.call("mtp_allreduce", None, 1, mode, L.ptr(xt), L.ptr(out), rows, cols, L.stream_ptr())
+    torch.cuda.synchronize()
+    want = O.REDUCE_FNS[name]([x])
+    np.testing.assert_array_equal(n(out), want)
+    if cols > 32:  # x_proj site: rounded to bf16, split
+        R = cols - 32
+        dl = torch.empty(rows, R, device=dev(), dtype=BF)
+        bc = torch.empty(rows, 32, device=dev())
+        L.call("mtp_reduce_xproj", None, mode, L.ptr(xt), rows, R, 32, L.ptr(dl), L.BF16, L.ptr(bc), L.stream_ptr())
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(n(dl), O.bf16_round(want[:, :R]))
+        np.testing.assert_array_equal(n(bc), O.bf16_round(want[:, R:]))
+
+
 def test_embedding_rmsnorm_argmax():
     V, D = 1000, 256
     table = torch.randn(V, D, device=dev(), dtype=BF)

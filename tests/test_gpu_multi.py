@@ -121,7 +121,8 @@ def _suite(rank, init_file, q, ws):
                 big = len(case) == 3
                 comm = get_comm(None, rank, ws, cols, cols)
                 x = _partial(rank, rows, cols, outliers=big).cuda()
-                for mode in ((L.RED_INT8TOK,) if big else (L.RED_FP32, L.RED_FP16, L.RED_INT8TOK)):
+                for mode in ((L.RED_INT8TOK,) if big else (L.RED_FP32, L.RED_FP16, L.RED_INT8TOK, L.RED_INT8TENSOR,
+                                                             L.RED_INT8SUM, L.RED_INT8LEGACY)):
                     y = torch.empty_like(x)
                     for _ in range(2):  # back-to-back calls on one site
                         L.call("mtp_allreduce", comm.ptr, 1, mode, L.ptr(x), L.ptr(y), rows, cols, L.stream_ptr())
@@ -157,6 +158,17 @@ def _suite(rank, init_file, q, ws):
                     all(torch.equal(a, b) for a, b in zip(eager, graphed)), count, chain,
                     getattr(m, "_mtp_decode", None) is not None)
                 del m
+        # ---- per-tensor-scale variants mixed with per-row sites (sequence-parallel epilogue off)
+        sd = random_init_state_dict(cfg, seed=12, dtype=torch.float32)
+        vspec = build_spec({"default": "int8", "overrides": {"0:out_proj": "int8_sum", "1:x_proj": "int8_gather",
+                                                             "2:out_proj": "int8_legacy", "2:x_proj": "int8_sum",
+                                                             "1:out_proj": "fp16"}}, cfg.n_layer)
+        m = TPMambaLM.from_state_dict_shard(cfg, sd, rank, ws, dtype=torch.float32, allreduce_dtype=vspec,
+                                            device="cuda")
+        lg, cache = m.prefill(ids.cuda())
+        st = m.step(torch.full((2, 1), 5, dtype=torch.long, device="cuda"), cache)
+        out["variants"] = (lg.float().cpu().numpy(), st.float().cpu().numpy(), m.layers[0].mixer.comm.count)
+        del m
         # ---- vocabulary-parallel lm_head (default up to 256 rows) == replicated lm_head, bitwise
         out["vocab"] = {}
         for dtype in (torch.float32, torch.bfloat16):
@@ -252,7 +264,8 @@ def test_peer_reductions_bit_exact_vs_oracle(ws):
     from oracle import mamba_oracle as O
 
     res = suite(ws)
-    names = {L.RED_FP32: "fp32", L.RED_FP16: "fp16", L.RED_INT8TOK: "int8"}
+    names = {L.RED_FP32: "fp32", L.RED_FP16: "fp16", L.RED_INT8TOK: "int8", L.RED_INT8TENSOR: "int8_gather",
+             L.RED_INT8SUM: "int8_sum", L.RED_INT8LEGACY: "int8_legacy"}
     want_cache = {}
     for (protocol, rows, cols, mode), got in res[0]["reduce"].items():
         key = (rows, cols, mode)
@@ -305,6 +318,38 @@ def test_tp_model_matches_oracle_and_ranks_agree(ws, dtype_name):
         else:
             met = O.quant_metrics(ref, lg0)
             assert met["kl"].mean() <= 2e-3 and met["top1"].mean() >= 0.95, (spec, met)
+
+
+# ------------------------------------------------------------------ per-tensor-scale variants in the model
+@pytest.mark.parametrize("ws", WS_LIST)
+def test_tp_model_with_per_tensor_scale_variants(ws):
+    """int8_gather / int8_sum / int8_legacy sites (kernels over peer memory) mixed with
+    per-row sites: the same logits on every rank, close to the oracle's TP emulation with
+    the same map (prefill and one cached step), and the reference's accounting (int8_sum
+    and int8_legacy count two collectives per call)."""
+    if _ngpu() < ws:
+        pytest.skip(f"needs {ws} GPUs")
+    from mamba_tp_lite_b200.checkpoint import random_init_state_dict
+    from mamba_tp_lite_b200.config import MambaConfig
+    from mamba_tp_lite_b200.tp_utils import build_spec
+    from oracle import mamba_oracle as O
+
+    res = suite(ws)
+    lg0, st0, count = res[0]["variants"]
+    for r in range(1, ws):
+        assert np.array_equal(res[r]["variants"][0], lg0) and np.array_equal(res[r]["variants"][1], st0), r
+    assert count == 2 * (1 + 2)  # layer 0 per call (prefill, step): x_proj int8 1, out_proj int8_sum 2
+    cfg = MambaConfig(d_model=256, n_layer=3, vocab_size=1000, dt_rank=16)
+    sd = random_init_state_dict(cfg, seed=12, dtype=torch.float32)
+    vspec = build_spec({"default": "int8", "overrides": {"0:out_proj": "int8_sum", "1:x_proj": "int8_gather",
+                                                         "2:out_proj": "int8_legacy", "2:x_proj": "int8_sum",
+                                                         "1:out_proj": "fp16"}}, cfg.n_layer)
+    ids = torch.randint(0, cfg.vocab_size, (2, 72), generator=torch.Generator().manual_seed(4)).numpy()
+    lm = O.OracleLM(O.Cfg(cfg.d_model, cfg.n_layer, cfg.vocab_size, dt_rank=cfg.dt_rank), O.state_dict_numpy(sd),
+                    world_size=ws, spec=vspec)
+    ref, _ = lm.prefill(ids)
+    met = O.quant_metrics(ref, lg0)
+    assert met["kl"].mean() <= 2e-3 and met["top1"].mean() >= 0.95, met
 
 
 # ------------------------------------------------------------------ vocabulary-parallel lm_head

@@ -79,6 +79,17 @@ def test_reduction_trace_parser():
     assert r["kernel_us"] == 28.0 and r["wait_us"] == (9 - 7) + (15 - 14) + (19 - 18) + (24 - 22)
 
 
+def test_every_reduction_name_has_a_kernel_mode():
+    """All seven ALLREDUCE_FNS names of the reference run in libmtp kernels; the per-row
+    wire formats are the ones the fused epilogues and the decode kernel take."""
+    from mamba_tp_lite_b200.tp_utils import KERNEL_MODES, ROW_MODES
+
+    assert set(KERNEL_MODES) == set(ALLREDUCE_FNS) == {"fp32", "fp16", "int8", "int8_legacy", "int8_sum",
+                                                       "int8_gather", "int8_gather_tok"}
+    assert ROW_MODES == {"fp32", "fp16", "int8", "int8_gather_tok"}
+    assert len({KERNEL_MODES[k] for k in KERNEL_MODES}) == 6  # int8 == int8_gather_tok
+
+
 def test_product_has_no_cpu_fallback():
     cfg = MambaConfig(d_model=32, n_layer=1, vocab_size=64, d_state=8)
     m = MambaMixer(cfg, 0)
