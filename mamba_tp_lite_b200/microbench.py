@@ -4,6 +4,7 @@ for ncu captures of one kernel on a bounded case.
     python -m mamba_tp_lite_b200.microbench gemm --m 32768 --n 8192 --k 2048
     python -m mamba_tp_lite_b200.microbench scan --batch 32 --seqlen 1024 --channels 4096
     python -m mamba_tp_lite_b200.microbench step --batch 32 --channels 4096 --rank 128
+    python -m mamba_tp_lite_b200.microbench xproj --fused 1   # x_proj with AllReduce #1 in its epilogue
     torchrun --nproc-per-node N -m mamba_tp_lite_b200.microbench allreduce --rows 32768 --cols 2048 --mode int8
     torchrun --nproc-per-node N -m mamba_tp_lite_b200.microbench allreduce-ref   # reference, gloo, host CPU
 
@@ -70,6 +71,30 @@ def bench_gemm(a):
         ref = A.float() @ W.float().T
         out["max_rel_err"] = ((C.float() - ref).abs().max() / ref.abs().max()).item()
     return out
+
+
+def bench_xproj(a):
+    """x_proj with AllReduce #1 at world size 1 (1.4b TP=1 site: [32768, 4096] x [160, 4096]),
+    int8 map: the GEMM whose epilogue applies the wire round trip and writes dt_low | B|C
+    (--fused 1), or the GEMM into an fp32 partial followed by the reduction kernel (0)."""
+    M, K, R, N2 = a.m, a.k, a.rank, 32
+    N = R + N2
+    xc = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    part = torch.empty(M, N, device="cuda")
+    dl = torch.empty(M, R, device="cuda", dtype=torch.bfloat16)
+    bc = torch.empty(M, N2, device="cuda")
+    os.environ["MTP_XPROJ_FUSED"] = "1" if a.fused else "0"
+
+    def run():
+        L.call("mtp_xproj_fused", None, L.RED_INT8TOK, L.ptr(xc), K, L.ptr(w), K, L.BF16, M, N, K, R, L.ptr(part),
+               L.ptr(dl), L.BF16, L.ptr(bc), L.stream_ptr())
+
+    ms = _time(run, a.warmup, a.iters)
+    tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
+    nbytes = M * K * 2 + N * K * 2 + M * (R * 2 + N2 * 4)  # xc and w read, dt_low and B|C written
+    return {"kernel": "xproj_fused" if a.fused else "xproj_gemm_then_reduce", "M": M, "N": N, "K": K, "avg_ms": ms,
+            "TFLOPs": tf, "GBps": nbytes / (ms / 1e3) / 1e9, "frac_of_hbm": nbytes / (ms / 1e3) / 1e9 / peaks()["hbm_gbs"]}
 
 
 def bench_scan(a):
@@ -386,6 +411,11 @@ def main():
     s.add_argument("--variant", choices=["xc", "raw"], default="xc",
                    help="xc: the scan over the conv output (prefill path); raw: conv inside the scan")
     s.add_argument("--dt", choices=["bf16", "f32"], default="bf16", help="dt element type (unfused scan)")
+    xp = sub.add_parser("xproj")
+    xp.add_argument("--m", type=int, default=32768)
+    xp.add_argument("--k", type=int, default=4096)
+    xp.add_argument("--rank", type=int, default=128)
+    xp.add_argument("--fused", type=int, default=1)
     cv = sub.add_parser("conv")
     cv.add_argument("--batch", type=int, default=32)
     cv.add_argument("--seqlen", type=int, default=1024)
@@ -411,13 +441,13 @@ def main():
     dcd.add_argument("--layers", type=int, default=0, help="override n_layer (0: the shape's)")
     dcd.add_argument("--batch", type=int, default=1)
     dcd.add_argument("--spec", default="mixed")
-    for p in (g, s, cv, st, r, rr, dcd):
+    for p in (g, s, xp, cv, st, r, rr, dcd):
         p.add_argument("--warmup", type=int, default=3)
         p.add_argument("--iters", type=int, default=10)
     a = ap.parse_args()
     if a.what != "allreduce-ref":  # the CPU baseline runs without the library
         L.load()
-    res = {"gemm": bench_gemm, "scan": bench_scan, "conv": bench_conv, "step": bench_step, "allreduce": bench_allreduce,
+    res = {"gemm": bench_gemm, "scan": bench_scan, "xproj": bench_xproj, "conv": bench_conv, "step": bench_step, "allreduce": bench_allreduce,
            "allreduce-ref": bench_allreduce_ref, "decode": bench_decode}[a.what](a)
     if res is not None:
         print(json.dumps(res), flush=True)
