@@ -265,7 +265,8 @@ int mtp_reduce_outproj(mtp_comm *c, int mode, const float *partial, int rows, in
  * followed by mtp_reduce_xproj, which is what runs when the shape does not fit the fused
  * form (N % 16, N <= 192, R % 16, 16-byte aligned operands and outputs; at world size > 1
  * the int8 wire only, rows within the context's slots, no grid cap; by default only at world
- * sizes 1 and 2, whose one-shot push is not larger than the two-shot protocol's traffic;
+ * sizes 1 and 2, whose one-shot push is not larger than the two-shot protocol's traffic, and
+ * with at least 64 x (SM count) rows;
  * MTP_XPROJ_FUSED=1 / 0 forces the fused form / the kernel pair): `partial` [rows, N] fp32 is
  * only used then and may be NULL for shapes that fit. */
 int mtp_xproj_fused(mtp_comm *c, int mode, const void *xc, int ld_xc, const void *w, int ld_w, int ab_dtype, int rows,

@@ -2104,8 +2104,12 @@ int mtp_xproj_fused(mtp_comm *c, int mode, const void *xc, int ld_xc, const void
   // layer at 1 rank, 110 vs ~100 at 2); from 3 ranks on, its one-shot push sends every row to
   // every rank, more than the reduction kernel's two-shot protocol moves, so the kernel pair
   // stays the default there.  MTP_XPROJ_FUSED=1 forces it at any world size, 0 turns it off.
+  // Also only with at least half an SM-wave of 128-row tiles: the epilogue form keeps whole
+  // rows in one N tile, so short inputs would run on a few CTAs where the kernel pair's GEMM
+  // narrows its N tile to fill the SMs.
   const char *fenv = getenv("MTP_XPROJ_FUSED");
-  const bool fused_on = fenv ? fenv[0] == '1' : (!has_comm || c->d.ws <= 2);
+  const bool fused_on = fenv ? fenv[0] == '1'
+                             : ((!has_comm || c->d.ws <= 2) && (long)ceil_div(rows, 128) * 2 >= num_sms());
   MTP_REQUIRE(ab_dtype == MTP_F32 || ab_dtype == MTP_BF16, "xc / w must be F32 or BF16");
   const bool fused = fused_on && ab_dtype == MTP_BF16 && gemm_tc_eligible(xc, w, rows, N, K, ld_xc, ld_w) && N % 16 == 0 && N <= 192 &&
                      R % 16 == 0 && aligned16(dt_low) && aligned16(bc) &&

@@ -186,7 +186,13 @@ class _LMKernels:
         from .tp_utils import get_comm
 
         cfg = self.cfg
-        return get_comm(self.group, self.rank, ws, cfg.dt_rank + 2 * cfg.d_state, cfg.d_model)
+        c = get_comm(self.group, self.rank, ws, cfg.dt_rank + 2 * cfg.d_state, cfg.d_model)
+        # the exchange goes through one receive slot of the out_proj site
+        _, shard = L.vocab_shard(cfg.vocab_size, ws, 0)
+        es = self.embedding.weight.element_size()
+        if rows * shard * es > c.max_rows * (4 * cfg.d_model + 16):
+            return None
+        return c
 
     def _lm_head(self, normed: torch.Tensor) -> torch.Tensor:
         w = self.embedding.weight

@@ -410,10 +410,12 @@ XPROJ_CASES = [  # (rows, R, 2N, K): the 1.4b / 2.8b / 370m / 130m x_proj sites,
 @pytest.mark.parametrize("rows,R,N2,K", XPROJ_CASES)
 @pytest.mark.parametrize("mode", [L.RED_FP32, L.RED_FP16, L.RED_INT8TOK])
 @pytest.mark.parametrize("dt_dtype", [L.BF16, L.F32])
-def test_xproj_gemm_epilogue_equals_gemm_then_reduce(rows, R, N2, K, mode, dt_dtype):
+def test_xproj_gemm_epilogue_equals_gemm_then_reduce(rows, R, N2, K, mode, dt_dtype, monkeypatch):
     """World size 1: the x_proj GEMM whose epilogue applies AllReduce #1's wire round
     trip and the dt | B|C split gives the bits of the GEMM into an fp32 partial followed
-    by the reduction kernel (tp_model.py:106-108), with 1% outlier columns."""
+    by the reduction kernel (tp_model.py:106-108), with 1% outlier columns.  The epilogue
+    form is forced (by default short inputs take the kernel pair)."""
+    monkeypatch.setenv("MTP_XPROJ_FUSED", "1")
     N = R + N2
     g = torch.Generator(device="cpu").manual_seed(rows + R + mode)
     xc = torch.randn(rows, K, generator=g).to(dev(), BF)
