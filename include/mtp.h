@@ -6,18 +6,19 @@
  * (passed as void*), returns an int status (0 = ok, see MTP_ERR_*) and launches
  * only on the given stream.  Device memory is allocated by the create / bind
  * calls (mtp_comm_create, mtp_decode_plan_create, mtp_decode_bind_cache) and,
- * on first use, for three internal buffers kept until exit: a status word of
- * the tensor-core GEMM, one of the fused dt_proj scan, and the row scratch of
+ * on first use, for four internal buffers kept until exit: a status word of
+ * the tensor-core GEMM, one of the fused dt_proj scan, the row scratch of
  * the reductions that do not hold a row in registers (rows wider than 3072
- * values or not a multiple of 4, or a grid capped by mtp_comm_set_max_ctas),
- * which grows to the largest size used.  A call that is to be recorded in a
+ * values or not a multiple of 4, a grid capped by mtp_comm_set_max_ctas, or a
+ * per-tensor-scale mode), and the state scratch of the sequence-chunked scan;
+ * the last two grow to the largest size used.  A call that is to be recorded in a
  * CUDA graph therefore needs one call of the same kind before the capture (the
  * package's GraphedStepper runs warm-up steps first).  No torch types appear
  * here; the Python package binds this header with ctypes.
  *
  * Devices: the library serves one device per process (one rank per process), except
- * the allocation-free reduction scratch and the reductions' row scratch, which are kept
- * per device; the status words of the GEMM and of the fused scan are per process.
+ * the allocation-free reduction scratch, the reductions' row scratch and the chunked
+ * scan's state scratch, which are kept per device; the status words of the GEMM and of the fused scan are per process.
  *
  * Layout conventions: matrices are row-major; a "token row" is one position
  * of one sequence, tokens ordered (batch, position).  Element type codes are
@@ -122,7 +123,11 @@ int mtp_scan_prefill(const void *xz, int ld_xz, const void *dt, int ld_dt, int d
  * xc [B*L, ld_xc] = SiLU(conv1d(x)) as written by mtp_conv1d_silu (the x_proj input,
  * computed once per layer); z is read from columns [Es, 2Es) of xz and the raw x
  * columns [0, Es) of xz only for the final conv history.  Other arguments as
- * mtp_scan_prefill (conv weights are not needed).  State pairs are updated with
+ * mtp_scan_prefill (conv weights are not needed).  With few recurrences (B x Es <= 8192)
+ * over long sequences (L >= 2048) the sequence is cut into up to 16 chunks: a state pass
+ * gives each chunk's end state from zero and its sum of dt, and each chunk's output pass
+ * starts from the state carried through the earlier chunks (MTP_SCAN_CHUNKS=n forces n
+ * chunks; the results agree with the unchunked scan to rounding).  State pairs are updated with
  * packed fp32 arithmetic; optionally (MTP_SCAN_POLY pairs per thread, 0 by default) part
  * of the state exponentials is evaluated on the FP32 pipe (the polynomial of mtp_exp2_fma).  Replaces tp_model.py:101-103 and :113-129
  * (model.py:210-241), the Python loop over t at tp_model.py:124-126. */

@@ -590,12 +590,22 @@ struct ScanXcSmem {
   float bc[2][TL][2 * N];
 };
 
-template <typename T, typename TD, int N, int TPC, int TL, int K, int NPP, int MINB>
+// Sequence chunks (few independent recurrences per SM, e.g. 640 channels x 8 sequences):
+// blockIdx.z = chunk k covers positions [k Lc, min(L, (k+1) Lc)) of every sequence.  ST = true
+// is the state pass: the chunk's end state from a zero state, E_k, and its sum of dt, S_k,
+// into slot k of chunk_io [B][NC][Es][N + 1] (no outputs); its chunk-0 CTAs also copy the
+// initial state into slot NC - 1 (the last chunk needs no end state), because the output
+// pass may overwrite ssm_init in place (ssm_final aliasing it) while other chunks still need
+// it.  ST = false starts chunk k from h = exp2(A2 S_{k-1}) (... (exp2(A2 S_0) h_init + E_0) ...)
+// + E_{k-1} and writes y for the chunk, the last chunk also the final state and conv history.
+// (exp2(A2 S) is the product of the chunk's per-position decays up to rounding.)  Unchunked:
+// NC = 1, Lc = L, h_init read from ssm_init.
+template <typename T, typename TD, int N, int TPC, int TL, int K, int NPP, int MINB, bool ST>
 __global__ void __launch_bounds__(128, MINB) scan_xc_kernel(
     const T *__restrict__ xc, int ld_xc, const T *__restrict__ xz, int ld_xz, const TD *__restrict__ dtp, int ld_dt,
     const float *__restrict__ bcp, int ld_bc, const T *__restrict__ A_log, const T *__restrict__ Dp,
-    const T *conv_init, const float *ssm_init, T *__restrict__ y, int ld_y, T *conv_final, float *ssm_final, int L,
-    int Es, bool vec16) {
+    const T *conv_init, const float *ssm_init, T *__restrict__ y, int ld_y, T *conv_final, float *ssm_final,
+    int Lseq, int Es, bool vec16, int Lc, int NC, float *chunk_io) {
   MTP_PDL_WAIT();
   MTP_PDL_TRIGGER();
   using S = ScanXcSmem<T, TD, N, TPC, TL>;
@@ -608,13 +618,16 @@ __global__ void __launch_bounds__(128, MINB) scan_xc_kernel(
   S &sm = *reinterpret_cast<S *>(smem_raw);
 
   const int b = blockIdx.y;
+  const int kz = blockIdx.z;
   const int c0 = blockIdx.x * CB;
   const int cl = threadIdx.x / TPC;
   const int sub = threadIdx.x % TPC;
   const int c = c0 + cl;
   const bool live = c < Es;
   const int ncb = min(CB, Es - c0);
-  const size_t row0 = (size_t)b * L;
+  const int tb = kz * Lc;
+  const int L = min(Lc, Lseq - tb);  // positions of this chunk
+  const size_t row0 = (size_t)b * Lseq + tb;
 
   float2 A2[NP], h[NP];
 #pragma unroll
@@ -622,9 +635,38 @@ __global__ void __launch_bounds__(128, MINB) scan_xc_kernel(
     const int n = sub * NS + 2 * i;
     A2[i].x = live ? -expf(ldf(A_log + (size_t)c * N + n)) * kLog2e : 0.f;
     A2[i].y = live ? -expf(ldf(A_log + (size_t)c * N + n + 1)) * kLog2e : 0.f;
-    h[i].x = (live && ssm_init) ? ssm_init[((size_t)b * Es + c) * N + n] : 0.f;
-    h[i].y = (live && ssm_init) ? ssm_init[((size_t)b * Es + c) * N + n + 1] : 0.f;
+    h[i] = make_float2(0.f, 0.f);
+    if (live && ssm_init && (ST ? kz == 0 : NC == 1)) {  // the state pass copies it (below)
+      h[i].x = ssm_init[((size_t)b * Es + c) * N + n];
+      h[i].y = ssm_init[((size_t)b * Es + c) * N + n + 1];
+    }
+    if (!ST && NC > 1 && live && ssm_init) {  // the copy taken by the state pass
+      const float *ini = chunk_io + (((size_t)b * NC + NC - 1) * Es + c) * (N + 1);
+      h[i] = make_float2(ini[n], ini[n + 1]);
+    }
   }
+  if (ST && kz == 0 && live && ssm_init) {
+    float *ini = chunk_io + (((size_t)b * NC + NC - 1) * Es + c) * (N + 1);
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+      ini[sub * NS + 2 * i] = h[i].x;
+      ini[sub * NS + 2 * i + 1] = h[i].y;
+      h[i] = make_float2(0.f, 0.f);  // the end state of chunk 0 is taken from zero too
+    }
+  }
+  if (!ST && live) {  // carry the state through the earlier chunks
+    for (int jz = 0; jz < kz; ++jz) {
+      const float *io = chunk_io + (((size_t)b * NC + jz) * Es + c) * (N + 1);
+      const float sdt = io[N];
+#pragma unroll
+      for (int i = 0; i < NP; ++i) {
+        const int n = sub * NS + 2 * i;
+        const float2 dec = make_float2(ex2_hw(A2[i].x * sdt), ex2_hw(A2[i].y * sdt));
+        h[i] = __ffma2_rn(dec, h[i], make_float2(io[n], io[n + 1]));
+      }
+    }
+  }
+  float ssum = 0.f;  // state pass: sum of dt over the chunk
   const float Dv = live ? ldf(Dp + c) : 0.f;
 
   auto load_chunk = [&](int k, int buf) {
@@ -687,7 +729,7 @@ __global__ void __launch_bounds__(128, MINB) scan_xc_kernel(
     // front (one lane per position); TPC == 1 gates each position where it is stored
     constexpr int NG = TPC == 1 ? 1 : TL / TPC;
     float gt[NG];
-    if constexpr (TPC > 1) {
+    if constexpr (TPC > 1 && !ST) {
 #pragma unroll
       for (int i = 0; i < NG; ++i) {
         const int tt = sub + TPC * i;
@@ -698,6 +740,25 @@ __global__ void __launch_bounds__(128, MINB) scan_xc_kernel(
     auto token = [&](const int tt) {
       const float xv = ldf(&sm.xc[buf][tt][cl]);
       const float dt = ldf(&sm.dt[buf][tt][cl]);
+      if constexpr (ST) {  // state pass: the recurrence and the sum of dt only
+        const float2 dt2 = make_float2(dt, dt);
+        const float2 dtx2 = make_float2(dt * xv, dt * xv);
+        const float4 *bv = reinterpret_cast<const float4 *>(&sm.bc[buf][tt][sub * NS]);
+        ssum += dt;
+#pragma unroll
+        for (int q = 0; q < NS / 4; ++q) {
+          const float4 B4 = bv[q];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int i = 2 * q + u;
+            const float2 Bp = u ? make_float2(B4.z, B4.w) : make_float2(B4.x, B4.y);
+            const float2 arg = __fmul2_rn(dt2, A2[i]);
+            const float2 dA = make_float2(ex2_hw(arg.x), ex2_hw(arg.y));
+            h[i] = __ffma2_rn(dA, h[i], __fmul2_rn(Bp, dtx2));
+          }
+        }
+        return;
+      }
       const float2 dt2 = make_float2(dt, dt);
       const float dtx = dt * xv;
       const float2 dtx2 = make_float2(dtx, dtx);
@@ -743,20 +804,32 @@ __global__ void __launch_bounds__(128, MINB) scan_xc_kernel(
     // buffer `buf` is refilled by the next iteration's prefetch only after this barrier
     __syncthreads();
   }
-  if (live) {
+  if (ST) {  // chunk end state from zero and its sum of dt
+    if (live) {
+      float *io = chunk_io + (((size_t)b * NC + kz) * Es + c) * (N + 1);
+#pragma unroll
+      for (int i = 0; i < NP; ++i) {
+        io[sub * NS + 2 * i] = h[i].x;
+        io[sub * NS + 2 * i + 1] = h[i].y;
+      }
+      if (sub == 0) io[N] = ssum;
+    }
+    return;
+  }
+  if (live && kz == NC - 1) {
 #pragma unroll
     for (int i = 0; i < NP; ++i) {
       ssm_final[((size_t)b * Es + c) * N + sub * NS + 2 * i] = h[i].x;
       ssm_final[((size_t)b * Es + c) * N + sub * NS + 2 * i + 1] = h[i].y;
     }
     if (sub == 0) {
-      // conv history for the next chunk: the last K-1 inputs of [conv_init | x]
-      // (all read before any write: conv_final may alias conv_init)
+      // conv history for the next prefill: the last K-1 inputs of [conv_init | x] of the
+      // whole sequence (all read before any write: conv_final may alias conv_init)
       float hv[K - 1];
 #pragma unroll
       for (int j = 0; j < K - 1; ++j) {
-        const int t = L - (K - 1) + j;
-        hv[j] = t >= 0 ? ldf(xz + (row0 + t) * ld_xz + c)
+        const int t = Lseq - (K - 1) + j;
+        hv[j] = t >= 0 ? ldf(xz + ((size_t)b * Lseq + t) * ld_xz + c)
                        : (conv_init ? ldf(conv_init + ((size_t)b * Es + c) * (K - 1) + (K - 1 + t)) : 0.f);
       }
 #pragma unroll
@@ -1140,29 +1213,70 @@ static int launch_scan(const void *xz, int ld_xz, const void *dt_v, int ld_dt, c
 // (exp2_poly2), by threads per channel; MTP_SCAN_POLY overrides it (0 .. N / (2 TPC)).
 constexpr int kPolyPairsTpc1 = 0, kPolyPairsTpc2 = 0, kPolyPairsTpc4 = 0;
 
+// Scratch of the chunked scan's state pass ([B][NC][Es][N+1] fp32), per device, grown on
+// demand (outside stream capture: the prefill is not captured).
+static float *scan_chunk_scratch(size_t bytes) {
+  constexpr int MAXD = 64;
+  static float *ptr[MAXD] = {};
+  static size_t cap[MAXD] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAXD) return nullptr;
+  if (cap[dev] < bytes) {
+    if (ptr[dev]) {
+      cudaDeviceSynchronize();
+      cudaFree(ptr[dev]);
+    }
+    ptr[dev] = nullptr;
+    cap[dev] = 0;
+    if (cudaMalloc(&ptr[dev], bytes) != cudaSuccess) return nullptr;
+    cap[dev] = bytes;
+  }
+  return ptr[dev];
+}
+
 template <typename T, typename TD, int N, int TPC, int NPP, int MINB>
 static int launch_scan_xc(const void *xc, int ld_xc, const void *xz, int ld_xz, const void *dt_v, int ld_dt,
                           const float *bc, int ld_bc, const void *A_log, const void *Dp, const void *conv_init,
                           const float *ssm_init, void *y, int ld_y, void *conv_final, float *ssm_final, int B, int L,
-                          int Es, cudaStream_t s) {
+                          int Es, int nc, cudaStream_t s) {
   constexpr int TL = 16, K = 4;
   using S = ScanXcSmem<T, TD, N, TPC, TL>;
   constexpr int CB = S::CB;
-  auto kern = scan_xc_kernel<T, TD, N, TPC, TL, K, NPP, MINB>;
+  auto kern = scan_xc_kernel<T, TD, N, TPC, TL, K, NPP, MINB, false>;
+  auto kern_st = scan_xc_kernel<T, TD, N, TPC, TL, K, NPP, MINB, true>;
   const TD *dt = (const TD *)dt_v;
   static bool attr_set = false;  // per template instance
   if (!attr_set) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(S)) != cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(S)) != cudaSuccess ||
+        cudaFuncSetAttribute(kern_st, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(S)) != cudaSuccess)
       return check_launch("scan_prefill_xc attr");
     attr_set = true;
   }
   const bool vec16 = Es % CB == 0 && aligned16(xc) && aligned16(xz) && aligned16(dt) && aligned16(bc) &&
                      ((size_t)ld_xc * sizeof(T)) % 16 == 0 && ((size_t)ld_xz * sizeof(T)) % 16 == 0 &&
                      ((size_t)Es * sizeof(T)) % 16 == 0 && ((size_t)ld_dt * sizeof(TD)) % 16 == 0 && ld_bc % 4 == 0;
-  dim3 grid((Es + CB - 1) / CB, B);
+  // sequence chunks of Lc positions (a multiple of the token tile)
+  int Lc = L, NC = 1;
+  if (nc > 1) {
+    Lc = (L + nc - 1) / nc;
+    Lc = (Lc + TL - 1) / TL * TL;
+    NC = (L + Lc - 1) / Lc;
+  }
+  float *io = nullptr;
+  if (NC > 1) {
+    io = scan_chunk_scratch((size_t)B * NC * Es * (N + 1) * sizeof(float));
+    if (!io) return fail(MTP_ERR_CUDA, "could not allocate the chunked scan's state scratch");
+    dim3 g1((Es + CB - 1) / CB, B, NC - 1);  // the last chunk's end state is not needed
+    launch_pdl(kern_st, dim3(g1), dim3(128), sizeof(S), s, (const T *)xc, ld_xc, (const T *)xz, ld_xz, dt, ld_dt, bc,
+               ld_bc, (const T *)A_log, (const T *)Dp, (const T *)conv_init, ssm_init, (T *)y, ld_y, (T *)conv_final,
+               ssm_final, L, Es, vec16, Lc, NC, io);
+    int rc = check_launch("scan_prefill_xc states");
+    if (rc) return rc;
+  }
+  dim3 grid((Es + CB - 1) / CB, B, NC);
   launch_pdl(kern, dim3(grid), dim3(128), sizeof(S), s, (const T *)xc, ld_xc, (const T *)xz, ld_xz, dt, ld_dt, bc,
              ld_bc, (const T *)A_log, (const T *)Dp, (const T *)conv_init, ssm_init, (T *)y, ld_y, (T *)conv_final,
-             ssm_final, L, Es, vec16);
+             ssm_final, L, Es, vec16, Lc, NC, io);
   return check_launch("scan_prefill_xc");
 }
 
@@ -1176,10 +1290,10 @@ template <typename T, typename TD, int N, int TPC>
 static int scan_xc_npp(int npp, int occ, const void *xc, int ld_xc, const void *xz, int ld_xz, const void *dt,
                        int ld_dt, const float *bc, int ld_bc, const void *A_log, const void *Dp, const void *conv_init,
                        const float *ssm_init, void *y, int ld_y, void *conv_final, float *ssm_final, int B, int L,
-                       int Es, cudaStream_t s) {
+                       int Es, int nc, cudaStream_t s) {
 #define MTP_SXC(P, OCC)                                                                                          \
   return launch_scan_xc<T, TD, N, TPC, P, OCC>(xc, ld_xc, xz, ld_xz, dt, ld_dt, bc, ld_bc, A_log, Dp, conv_init, \
-                                               ssm_init, y, ld_y, conv_final, ssm_final, B, L, Es, s)
+                                               ssm_init, y, ld_y, conv_final, ssm_final, B, L, Es, nc, s)
   constexpr int NP = N / TPC / 2;
   constexpr int DEF = TPC == 1 ? kPolyPairsTpc1 : TPC == 2 ? kPolyPairsTpc2 : kPolyPairsTpc4;
   constexpr int D0 = DEF < NP ? DEF : NP;
@@ -1213,9 +1327,9 @@ int mtp_conv1d_silu(const void *xz, int ld_xz, const void *conv_w, const void *c
   const int V = (int)(16 / es_b);
   const bool vec = Es % V == 0 && aligned16(xz) && aligned16(xc) && (ld_xz * es_b) % 16 == 0 && (ld_xc * es_b) % 16 == 0;
   if (vec) {
-    // 64 positions per thread (the 3-position halo is re-read once per 64), register-direct
-    // loads; MTP_CONV_STAGED=1 stages the input tile in shared memory instead (B200, 1.4b
-    // TP=1 shard: 0.23 ms staged vs 0.20 ms direct)
+    // B200, 1.4b TP=1 shard: all of a thread's loads issued first, 8 positions per thread
+    // (0.121 ms, the default); the 64-position direct loop (MTP_CONV_KERNEL=direct, 0.170 ms);
+    // the input tile staged in shared memory (MTP_CONV_STAGED=1, 0.234 ms)
     constexpr int TT = 64, NTH = 32;
     const int groups = Es / V;
     const bool wvec = aligned16(conv_w) && (conv_b == nullptr || aligned16(conv_b));
@@ -1349,9 +1463,18 @@ int mtp_scan_prefill_xc(const void *xc, int ld_xc, const void *xz, int ld_xz, co
   if (npp < 0) npp = 0;
   int occ = 0;
   if (const char *env = getenv("MTP_SCAN_OCC")) occ = atoi(env);
+  // sequence chunks when few recurrences run per SM (B x Es up to 8192, e.g. 8 sequences x
+  // 640 channels) and the sequences are long: the state pass doubles the SFU work of all but
+  // the last chunk but multiplies the parallelism.  B200, 8 x 8192 x 640 (2.8b TP=8 shard):
+  // 1.275 ms unchunked, 0.620 / 0.625 / 0.450 ms with 4 / 8 / 16 chunks; 32 x 1024 x 512 (1.4b
+  // TP=8): 0.187 / 0.184 / 0.193 ms with 1 / 2 / 4, so no chunks there.  MTP_SCAN_CHUNKS=n forces n.
+  int nc = 1;
+  if (pairs <= 8192 && L >= 2048) nc = L / 512 < 16 ? L / 512 : 16;
+  if (const char *env = getenv("MTP_SCAN_CHUNKS")) nc = atoi(env);
+  if (nc < 1) nc = 1;
 #define MTP_SXC_CASE(TT, TDD, NN, TP)                                                                          \
   return scan_xc_npp<TT, TDD, NN, TP>(npp, occ, xc, ld_xc, xz, ld_xz, dt, ld_dt, bc, ld_bc, A_log, Dp, conv_init, \
-                                      ssm_init, y, ld_y, conv_final, ssm_final, B, L, Es, s)
+                                      ssm_init, y, ld_y, conv_final, ssm_final, B, L, Es, nc, s)
   using bf16 = __nv_bfloat16;
   if (dtype == MTP_F32) {
     if (N == 16) { if (tpc == 1) MTP_SXC_CASE(float, float, 16, 1); if (tpc == 2) MTP_SXC_CASE(float, float, 16, 2); MTP_SXC_CASE(float, float, 16, 4); }

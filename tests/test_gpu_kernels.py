@@ -168,6 +168,70 @@ def test_scan_prefill_xc_matches_oracle(monkeypatch, dtype, b, l, es, nst, init,
     np.testing.assert_allclose(n(sf), sf_ref, atol=tol, rtol=tol)
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, BF])
+@pytest.mark.parametrize("b,l,es,init", [(2, 600, 256, True), (3, 1000, 130, False), (1, 2048, 64, True)])
+@pytest.mark.parametrize("chunks,tpc", [("3", None), ("7", "2"), ("16", "4"), ("5", "1")])
+def test_scan_prefill_xc_sequence_chunks_match_oracle(monkeypatch, dtype, b, l, es, init, chunks, tpc):
+    """The sequence-chunked scan (a state pass per chunk, then each chunk's output pass from
+    the carried state): the oracle recurrence over the whole sequence, with and without an
+    initial state, ragged last chunks, every threads-per-channel width."""
+    monkeypatch.setenv("MTP_SCAN_CHUNKS", chunks)
+    if tpc is not None:
+        monkeypatch.setenv("MTP_SCAN_TPC", tpc)
+    x, z, dt, Bm, Cm, A_log, Dp, cw, cb, ci, si = _ssm_inputs(b, l, es, 16, 15, dtype)
+    if not init:
+        ci = si = None
+    rnd = O.bf16_round if dtype == BF else (lambda v: v)
+    xc_in = rnd(O.conv_silu_ref(x, cw, cb, ci)[0])
+    dt = rnd(dt)
+    cf_ref = O.final_conv_history(x, ci)
+    y_ref, _, sf_ref = O.scan_xc_ref(xc_in, cf_ref, z, dt, Bm, Cm, A_log, Dp, si)
+    T = b * l
+    xz = t(np.concatenate([x, z], -1).reshape(T, 2 * es), dtype)
+    xct, dtt = t(xc_in.reshape(T, es), dtype), t(dt.reshape(T, es), dtype)
+    bc = t(np.concatenate([Bm, Cm], -1).reshape(T, 32))
+    y = torch.empty(T, es, device=dev(), dtype=dtype)
+    cf = torch.empty(b, es, 3, device=dev(), dtype=dtype)
+    sf = torch.empty(b, es, 16, device=dev(), dtype=torch.float32)
+    args = [t(A_log, dtype), t(Dp, dtype), None if ci is None else t(ci, dtype), None if si is None else t(si)]
+    L.call("mtp_scan_prefill_xc", L.ptr(xct), es, L.ptr(xz), 2 * es, L.ptr(dtt), es, L.dtype_code(dtype), L.ptr(bc),
+           32, *[L.ptr(a) for a in args], L.ptr(y), es, L.ptr(cf), L.ptr(sf), b, l, es, 16, 4, L.dtype_code(dtype),
+           L.stream_ptr())
+    torch.cuda.synchronize()
+    tol = 2e-4 if dtype == torch.float32 else 2e-2
+    np.testing.assert_allclose(n(y).reshape(b, l, es), y_ref, atol=tol, rtol=tol)
+    np.testing.assert_allclose(n(cf), rnd(cf_ref), atol=0, rtol=0)
+    np.testing.assert_allclose(n(sf), sf_ref, atol=tol, rtol=tol)
+
+
+def test_scan_prefill_xc_sequence_chunks_in_place(monkeypatch):
+    """Chunked scan with the cache's state passed as both ssm_init and ssm_final (chunked
+    prefill from a cache): the same results as separate buffers -- the initial state is
+    copied by the state pass before the last chunk overwrites it."""
+    monkeypatch.setenv("MTP_SCAN_CHUNKS", "6")
+    b, l, es, nst = 2, 777, 128, 16
+    x, z, dt, Bm, Cm, A_log, Dp, cw, cb, ci, si = _ssm_inputs(b, l, es, nst, 18, BF)
+    xc_in = O.bf16_round(O.conv_silu_ref(x, cw, cb, ci)[0])
+    T = b * l
+    xz = t(np.concatenate([x, z], -1).reshape(T, 2 * es), BF)
+    xct, dtt = t(xc_in.reshape(T, es), BF), t(O.bf16_round(dt).reshape(T, es), BF)
+    bc = t(np.concatenate([Bm, Cm], -1).reshape(T, 2 * nst))
+    A_t, D_t = t(A_log, BF), t(Dp, BF)
+    outs = []
+    for in_place in (False, True):
+        ci_t, si_t = t(ci, BF), t(si)
+        cf = ci_t if in_place else torch.empty_like(ci_t)
+        sf = si_t if in_place else torch.empty_like(si_t)
+        y = torch.empty(T, es, device=dev(), dtype=BF)
+        L.call("mtp_scan_prefill_xc", L.ptr(xct), es, L.ptr(xz), 2 * es, L.ptr(dtt), es, L.BF16, L.ptr(bc), 2 * nst,
+               L.ptr(A_t), L.ptr(D_t), L.ptr(ci_t), L.ptr(si_t), L.ptr(y), es, L.ptr(cf), L.ptr(sf), b, l, es, nst, 4,
+               L.BF16, L.stream_ptr())
+        torch.cuda.synchronize()
+        outs.append((n(y), n(cf), n(sf)))
+    for a, c in zip(*outs):
+        np.testing.assert_array_equal(a, c)
+
+
 def test_scan_prefill_xc_in_place_history():
     """Chunked prefill passes the cache's conv history as both conv_init and
     conv_final (and the ssm state likewise): results equal the out-of-place call."""
